@@ -1,0 +1,366 @@
+"""Benchmark: Chronos-2-base encoder forward (bf16, fp32 accumulate) on B200.
+
+Workload: per GPU 256 independent univariate
+series, context 2048 (128 patches), prediction_length 64 (4 future patches),
+synthetic seeded data (random walk + daily/weekly sinusoids + noise, 2% NaN),
+random-init weights (seed 0, N(0, 0.02), RMS weights 1).  One step = one
+forward over the batch -> (256, 21, 64) quantile forecasts.  Under torchrun
+each rank runs its own 256 series (weak scaling) and the quantile outputs are
+gathered to every rank with NCCL all_gather inside the step.
+
+Metric: forecasts/s (whole job).  Timing: CUDA events on the launching stream
+per step; L2 is flushed (256 MB write) before every timed step, outside the
+event pair; barrier + synchronize around the timed loop; max over ranks.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+--impl reference times the reference algorithm's CPU path (the CPU oracle
+restatement of cutechronos CuteChronos2Model.forward, fp32 torch on all host
+cores) on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+METRIC = "forecasts/sec/GPU, Chronos-2-base shape ctx2048 bf16; p50 batch-1 latency"
+UNIT = "forecasts/s"
+GFLOP_PER_FORECAST = None  # filled from the oracle's FLOP formula
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms in a thread."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.rows = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=2)
+            except Exception:
+                self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=2)
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in self.rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in self.rows if num(r[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in self.rows for n, v in zip(names, r[5:9]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows),
+                "power_w_max": max((num(r[3]) or 0.0) for r in self.rows)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d["hbm_gbs"], d["bf16_tflops"], d.get("bf16_tflops_sustained", d["bf16_tflops"]), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class CpuReference:
+    """The reference algorithm on the host cores: the CPU oracle restatement of
+    CuteChronos2Model.forward in fp32 torch, all host threads."""
+
+    def __init__(self):
+        from cutechronos_b200.model import CuteChronos2Config, CuteChronos2Model
+        from cutechronos_b200.workloads import seeded_state_dict
+        from oracle import chronos2_oracle as orc
+
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        m = CuteChronos2Model(CuteChronos2Config())
+        self.W = seeded_state_dict([(n, tuple(p.shape)) for n, p in m.named_parameters()], seed=0)
+        self.orc = orc
+
+    def forecasts_per_s(self, n_series: int, L: int = 2048, N: int = 4, seed: int = 1) -> float:
+        from cutechronos_b200.workloads import series_cfg1
+
+        ctx = series_cfg1(n_series, L, seed)
+        t0 = time.perf_counter()
+        self.orc.forward(self.orc.OracleConfig(), self.W, ctx, None, N)
+        return n_series / (time.perf_counter() - t0)
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    n = 16
+    ref = CpuReference()
+    for _ in range(args.warmup):
+        ref.forecasts_per_s(2)
+    vals = [ref.forecasts_per_s(n) for _ in range(args.steps)]
+    threads = ref.threads
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * n / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (configs[1] generator, seed 1)",
+        "config": {"workload": "configs[1]: B=256 univariate, ctx 2048, pred 64 (4 patches), Chronos-2-base",
+                   "sample": f"{n} series per step", "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{n} series of configs[1] per step, fp32 CPU oracle restatement of "
+                                   "CuteChronos2Model.forward"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_b200(args):
+    import torch.distributed as dist
+
+    from cutechronos_b200 import _native as nat
+    from cutechronos_b200.model import CuteChronos2Config, CuteChronos2Model
+    from cutechronos_b200.workloads import seeded_init_, series_cfg1
+    from oracle.chronos2_oracle import forecast_flops
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev)
+    B, L, N = args.batch, 2048, 4
+    P = L // 16
+    S = P + 1 + N
+    gflop = forecast_flops(S, P, N) / 1e9
+
+    model = seeded_init_(CuteChronos2Model(CuteChronos2Config()), seed=0).to(dev, torch.bfloat16).eval()
+    ctx_host = series_cfg1(B, L, 1 + rank).pin_memory()
+    ctx = ctx_host.to(dev)
+    out_host = torch.empty(B, 21, N * 16, dtype=torch.bfloat16).pin_memory()
+    gathered = torch.empty(world * B, 21, N * 16, dtype=torch.bfloat16, device=dev) if world > 1 else None
+    flush = torch.empty(256 * 2**20, dtype=torch.uint8, device=dev)
+    lib = nat.load()
+
+    def step(x):
+        y = model(x, num_output_patches=N)
+        if world > 1:
+            dist.all_gather_into_tensor(gathered, y)
+        return y
+
+    with torch.inference_mode():
+        for _ in range(args.warmup):
+            step(ctx)
+        torch.cuda.synchronize()
+        # ---- device-timed region: inputs resident in HBM --------------------
+        cap = 256 * args.steps
+        clocks = ClockSampler(local)
+        clocks.start()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        nat.check(lib.cc2_profile_begin(cap), "cc2_profile_begin")
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            evs[i][0].record()
+            step(ctx)
+            evs[i][1].record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        clocks.stop()
+        step_ms = [a.elapsed_time(b) for a, b in evs]
+        kinds = (C.c_int * cap)()
+        ms = (C.c_float * cap)()
+        fl = (C.c_double * cap)()
+        by = (C.c_double * cap)()
+        cnt = C.c_int()
+        nat.check(lib.cc2_profile_read(kinds, ms, fl, by, cap, C.byref(cnt)), "cc2_profile_read")
+        total_ms = sum(step_ms)
+        t = torch.tensor([total_ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        value = world * B * args.steps / (total_ms / 1e3)
+
+        # ---- end to end through the public API with host buffers --------------
+        if world > 1:
+            dist.barrier()
+        e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            e2e_ev[i][0].record()
+            x = ctx_host.to(dev, non_blocking=True)
+            y = step(x)
+            out_host.copy_(y, non_blocking=True)
+            e2e_ev[i][1].record()
+        torch.cuda.synchronize()
+        e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev)
+        t = torch.tensor([e2e_ms], device=dev)
+        if world > 1:
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_value = world * B * args.steps / (float(t.item()) / 1e3)
+
+        # ---- p50 batch-1 latency (CUDA graph of one B=1 forward) ---------------
+        lat_p50 = None
+        if rank == 0 and not args.no_latency:
+            x1 = ctx[:1].clone()
+            model(x1, num_output_patches=N)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                model(x1, num_output_patches=N)
+                with torch.cuda.graph(g, stream=s):
+                    model(x1, num_output_patches=N)
+            torch.cuda.synchronize()
+            lats = []
+            for _ in range(50):
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                g.replay()
+                b.record()
+                b.synchronize()
+                lats.append(a.elapsed_time(b))
+            lat_p50 = statistics.median(lats)
+
+    # ---- roofline of the dominant kernel (tcgen05 GEMM), live from the timed region
+    n = cnt.value
+    agg = {}
+    for i in range(min(n, cap)):
+        k = nat.KIND_NAMES.get(kinds[i], str(kinds[i]))
+        a = agg.setdefault(k, {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
+        a["launches"] += 1
+        a["ms"] += ms[i]
+        a["flops"] += fl[i]
+        a["bytes"] += by[i]
+    hbm, tf_burst, tf_sus, peak_src = measured_peaks()
+    gemm = agg.get("gemm_tc", {"launches": 0, "ms": 1.0, "flops": 0.0})
+    achieved_tf = gemm["flops"] / (gemm["ms"] / 1e3) / 1e12
+    pre = agg.get("preprocess")
+    result = None
+    if rank == 0:
+        cpu_v, cpu_threads = None, 0
+        if not args.no_cpu:
+            ref = CpuReference()
+            ref.forecasts_per_s(1, L, N)
+            cpu_v, cpu_threads = ref.forecasts_per_s(8, L, N), ref.threads
+        clk = clocks.summary()
+        roofline = {
+            "bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05, all GEMM launches of the step)",
+            "achieved": achieved_tf, "peak": tf_sus, "unit": "TFLOP/s", "frac": achieved_tf / tf_sus,
+            "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long step)",
+            "traffic": None,
+            "launches_per_step": gemm["launches"] / args.steps,
+            "avg_launch_us": 1e3 * gemm["ms"] / max(1, gemm["launches"]),
+        }
+        kernels = {k: {"launches": v["launches"], "ms_total": round(v["ms"], 4),
+                       "share": round(v["ms"] / sum(x["ms"] for x in agg.values()), 4)} for k, v in agg.items()}
+        if pre:
+            kernels["preprocess"]["hbm_gbs"] = pre["bytes"] / (pre["ms"] / 1e3) / 1e9
+        result = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (configs[1] generator; random-init weights seed 0)",
+            "config": {"workload": "configs[1]: Chronos-2-base encoder forward, B=256 univariate series per GPU, "
+                                   "ctx 2048 (128 patches), pred 64 (4 patches), S=133 tokens",
+                       "global_batch": world * B, "seq_len": S, "parallelism": f"series sharding x{world}",
+                       "l2": "flushed (256 MB write) before every timed step"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": B * L * 4,
+                    "d2h_bytes_per_step": B * 21 * N * 16 * 2,
+                    "path": "CuteChronos2Model.forward on pinned host input, D2H of the (B,21,64) bf16 forecasts"},
+            "gpu_launches": n,
+            "roofline": roofline,
+            "model_flops_frac": value / world * gflop * 1e9 / (tf_sus * 1e12),
+            "gflop_per_forecast": gflop,
+            "latency_b1_p50_ms": lat_p50,
+            "kernels": kernels,
+            "clocks": clk,
+            "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads, "kind": "port",
+                             "sample": "8 series of configs[1] (ctx 2048, N=4), fp32 CPU oracle restatement "
+                                       "of CuteChronos2Model.forward, one forward"},
+        }
+        print(json.dumps(result), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return result
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--batch", type=int, default=256)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-latency", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,407 @@
+// Unscaled self-attention over "sets" of token rows (no 1/sqrt(d) factor).
+//
+//   time attention  (mode 0): set b = the S tokens of series b; RoPE (when a
+//     cos/sin table is given) is applied to Q and K in the prologue at
+//     positions 0..S-1; keys with token_mask 0
+//     are masked.  Reference: TimeSelfAttentionFallback.forward
+//     (cutechronos/model.py:209-275), RoPE model.py:94-128 / rope.py:126-180,
+//     unscaled_attention kernel_backends.py:113-153 (SDPA with scale=1.0).
+//   group attention (mode 1): set (t, g) = token t of every series in group g;
+//     no RoPE; key (b, t) is masked when token_mask[b, t] is 0.  Reference:
+//     GroupSelfAttentionFallback.forward (model.py:295-312) with the group-time
+//     mask of model.py:561-569 - the reference materialises all B x B scores per
+//     time step and masks the other groups; here only the group is visited.
+//
+// Masking: a masked key scores -1e30 (finite, like the reference's additive
+// finfo.min), a key past the end of the set scores -inf.  A query whose keys
+// are all masked therefore averages its set's values with equal weights
+// (finite output); such queries are padding tokens whose state never reaches
+// a forecast.
+//
+// Kernels:
+//   attn_mma_kernel   bf16, flash-style: 64 queries per CTA (16 per warp),
+//                     64-key blocks, mma.sync m16n8k16 with fp32 accumulation,
+//                     online softmax in fp32 (exp2 domain), P re-used from
+//                     registers as the A operand of P.V.  S x S never leaves
+//                     registers.
+//   attn_simt_kernel  float or bf16 storage, fp32 math on CUDA cores: used for
+//                     the fp32 model mode and for small groups (<= 32 members),
+//                     where a 64-row MMA tile would be mostly empty.
+#include "common.cuh"
+
+namespace cc2 {
+namespace {
+
+typedef __nv_bfloat16 bf16;
+
+struct SetInfo {
+  int mode;  // 0 time, 1 group
+  int S;     // tokens per series
+  const int32_t* members;
+  const int32_t* offsets;
+  int num_groups;
+};
+
+struct SetGeom {
+  int n;
+  int base;               // time: first row
+  int t;                  // group: time index
+  const int32_t* mem;     // group: member list
+  __device__ __forceinline__ int row(int i, int S) const { return mem ? mem[i] * S + t : base + i; }
+};
+
+__device__ __forceinline__ SetGeom set_geom(const SetInfo& si, int set) {
+  SetGeom g;
+  if (si.mode == 0) {
+    g.n = si.S; g.base = set * si.S; g.t = 0; g.mem = nullptr;
+  } else {
+    const int t = set / si.num_groups, grp = set % si.num_groups;
+    const int o0 = si.offsets[grp];
+    g.n = si.offsets[grp + 1] - o0; g.base = 0; g.t = t; g.mem = si.members + o0;
+  }
+  return g;
+}
+
+constexpr float kMaskedScore = -1e30f;
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ---------------------------------------------------------------------------
+// tensor-core flash kernel (bf16)
+// ---------------------------------------------------------------------------
+constexpr int QT = 64, KT = 64, DH = 64, LDS = DH + 8;  // padded smem rows (144 B)
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// Rotate-half RoPE on a [rows][LDS] bf16 tile in shared memory (fp32 math,
+// one rounding), positions pos0 + r for rows r < valid.
+__device__ __forceinline__ void rope_tile(bf16 (*T)[LDS], int valid, int pos0, const float2* __restrict__ cs) {
+  for (int idx = threadIdx.x; idx < valid * (DH / 2); idx += blockDim.x) {
+    const int r = idx / (DH / 2), i = idx % (DH / 2);
+    const float2 c = cs[(size_t)(pos0 + r) * (DH / 2) + i];
+    const float x1 = __bfloat162float(T[r][i]), x2 = __bfloat162float(T[r][i + DH / 2]);
+    T[r][i] = __float2bfloat16_rn(x1 * c.x - x2 * c.y);
+    T[r][i + DH / 2] = __float2bfloat16_rn(x2 * c.x + x1 * c.y);
+  }
+}
+
+template <bool ROPE>
+__global__ void __launch_bounds__(128)
+attn_mma_kernel(const bf16* __restrict__ qkv, int ld, int qcol, int kcol, int vcol, bf16* __restrict__ out,
+                int ldo, const uint8_t* __restrict__ tok, const float2* __restrict__ rope, SetInfo si) {
+  __shared__ __align__(16) bf16 Qs[QT][LDS];
+  __shared__ __align__(16) bf16 Ks[KT][LDS];
+  __shared__ __align__(16) bf16 Vs[KT][LDS];
+  __shared__ float kbias[KT];
+
+  const SetGeom g = set_geom(si, blockIdx.z);
+  const int h = blockIdx.y;
+  const int q0 = blockIdx.x * QT;
+  if (q0 >= g.n) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hq = qcol + h * DH, hk = kcol + h * DH, hv = vcol + h * DH;
+
+  // ---- Q tile (+RoPE) -> registers ----
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = (tid >> 3) + 16 * i, c = (tid & 7) * 8;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (q0 + r < g.n) v = *reinterpret_cast<const uint4*>(qkv + (size_t)g.row(q0 + r, si.S) * ld + hq + c);
+    *reinterpret_cast<uint4*>(&Qs[r][c]) = v;
+  }
+  __syncthreads();
+  if (ROPE) {
+    rope_tile(Qs, min(QT, g.n - q0), q0, rope);
+    __syncthreads();
+  }
+  uint32_t qf[4][4];
+  {
+    const uint32_t base = (uint32_t)__cvta_generic_to_shared(&Qs[16 * warp + (lane & 15)][(lane >> 4) * 8]);
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) ldsm_x4(base + ks * 32, qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+  }
+
+  float o[8][4];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+
+  for (int k0 = 0; k0 < g.n; k0 += KT) {
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = (tid >> 3) + 16 * i, c = (tid & 7) * 8;
+      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+      if (k0 + r < g.n) {
+        const size_t rb = (size_t)g.row(k0 + r, si.S) * ld;
+        kv = *reinterpret_cast<const uint4*>(qkv + rb + hk + c);
+        vv = *reinterpret_cast<const uint4*>(qkv + rb + hv + c);
+      }
+      *reinterpret_cast<uint4*>(&Ks[r][c]) = kv;
+      *reinterpret_cast<uint4*>(&Vs[r][c]) = vv;
+    }
+    if (tid < KT) {
+      const int kj = k0 + tid;
+      float b = -INFINITY;
+      if (kj < g.n) b = tok[g.row(kj, si.S)] ? 0.0f : kMaskedScore;
+      kbias[tid] = b;
+    }
+    __syncthreads();
+    if (ROPE) {
+      rope_tile(Ks, min(KT, g.n - k0), k0, rope);
+      __syncthreads();
+    }
+    // ---- S = Q K^T (16 x 64 per warp) ----
+    float s[8][4];
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+      const uint32_t kb = (uint32_t)__cvta_generic_to_shared(&Ks[nt * 8 + (lane & 7)][(lane >> 3) * 8]);
+#pragma unroll
+      for (int ks = 0; ks < 4; ks += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kb + ks * 32, b0, b1, b2, b3);
+        mma16816(s[nt], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], b0, b1);
+        mma16816(s[nt], qf[ks + 1][0], qf[ks + 1][1], qf[ks + 1][2], qf[ks + 1][3], b2, b3);
+      }
+    }
+    // ---- mask + online softmax (log2 domain) ----
+    float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const int c = nt * 8 + 2 * (lane & 3);
+      const float b0 = kbias[c], b1 = kbias[c + 1];
+      s[nt][0] = b0 == 0.0f ? s[nt][0] * kLog2e : b0;
+      s[nt][1] = b1 == 0.0f ? s[nt][1] * kLog2e : b1;
+      s[nt][2] = b0 == 0.0f ? s[nt][2] * kLog2e : b0;
+      s[nt][3] = b1 == 0.0f ? s[nt][3] * kLog2e : b1;
+      mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
+      mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
+    }
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+    const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+    const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
+    m0 = mn0; m1 = mn1;
+    l0 *= c0; l1 *= c1;
+#pragma unroll
+    for (int dt = 0; dt < 8; ++dt) { o[dt][0] *= c0; o[dt][1] *= c0; o[dt][2] *= c1; o[dt][3] *= c1; }
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      s[nt][0] = exp2f(s[nt][0] - mn0); s[nt][1] = exp2f(s[nt][1] - mn0);
+      s[nt][2] = exp2f(s[nt][2] - mn1); s[nt][3] = exp2f(s[nt][3] - mn1);
+      l0 += s[nt][0] + s[nt][1];
+      l1 += s[nt][2] + s[nt][3];
+    }
+    // ---- O += P V ----
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t a0 = pack2(s[2 * j][0], s[2 * j][1]);
+      const uint32_t a1 = pack2(s[2 * j][2], s[2 * j][3]);
+      const uint32_t a2 = pack2(s[2 * j + 1][0], s[2 * j + 1][1]);
+      const uint32_t a3 = pack2(s[2 * j + 1][2], s[2 * j + 1][3]);
+      const uint32_t vb = (uint32_t)__cvta_generic_to_shared(&Vs[16 * j + (lane & 15)][(lane >> 4) * 8]);
+#pragma unroll
+      for (int dt = 0; dt < 8; dt += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vb + dt * 16, b0, b1, b2, b3);
+        mma16816(o[dt], a0, a1, a2, a3, b0, b1);
+        mma16816(o[dt + 1], a0, a1, a2, a3, b2, b3);
+      }
+    }
+  }
+  // ---- normalise, stage through smem (own rows of Qs), coalesced store ----
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+  const int r0 = 16 * warp + (lane >> 2);
+#pragma unroll
+  for (int dt = 0; dt < 8; ++dt) {
+    const int c = dt * 8 + 2 * (lane & 3);
+    *reinterpret_cast<uint32_t*>(&Qs[r0][c]) = pack2(o[dt][0] * i0, o[dt][1] * i0);
+    *reinterpret_cast<uint32_t*>(&Qs[r0 + 8][c]) = pack2(o[dt][2] * i1, o[dt][3] * i1);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int rr = 16 * warp + (lane >> 3) + 4 * i, c = (lane & 7) * 8;
+    if (q0 + rr < g.n)
+      *reinterpret_cast<uint4*>(out + (size_t)g.row(q0 + rr, si.S) * ldo + h * DH + c) =
+          *reinterpret_cast<const uint4*>(&Qs[rr][c]);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// SIMT kernel (fp32 mode, small groups)
+// ---------------------------------------------------------------------------
+constexpr int SQ = 16;  // queries per CTA (4 per warp)
+constexpr int SK = 32;  // keys per block (one per lane)
+
+template <typename T, bool ROPE>
+__global__ void __launch_bounds__(128)
+attn_simt_kernel(const T* __restrict__ qkv, int ld, int qcol, int kcol, int vcol, T* __restrict__ out, int ldo,
+                 const uint8_t* __restrict__ tok, const float2* __restrict__ rope, SetInfo si) {
+  __shared__ float Qs[SQ][DH];
+  __shared__ float Ks[SK][DH + 1];
+  __shared__ float Vs[SK][DH];
+  __shared__ float kbias[SK];
+  const SetGeom g = set_geom(si, blockIdx.z);
+  const int h = blockIdx.y;
+  const int q0 = blockIdx.x * SQ;
+  if (q0 >= g.n) return;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int hq = qcol + h * DH, hk = kcol + h * DH, hv = vcol + h * DH;
+
+  for (int idx = tid; idx < SQ * (DH / 2); idx += blockDim.x) {
+    const int r = idx / (DH / 2), i = idx % (DH / 2);
+    float x1 = 0.0f, x2 = 0.0f;
+    if (q0 + r < g.n) {
+      const T* src = qkv + (size_t)g.row(q0 + r, si.S) * ld + hq;
+      x1 = tof<T>(src[i]);
+      x2 = tof<T>(src[i + DH / 2]);
+      if (ROPE) {
+        const float2 c = rope[(size_t)(q0 + r) * (DH / 2) + i];
+        const float y1 = x1 * c.x - x2 * c.y, y2 = x2 * c.x + x1 * c.y;
+        x1 = roundT<T>(y1);
+        x2 = roundT<T>(y2);
+      }
+    }
+    Qs[r][i] = x1;
+    Qs[r][i + DH / 2] = x2;
+  }
+  float m[4], l[4], o0[4], o1[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) { m[r] = -INFINITY; l[r] = 0.0f; o0[r] = 0.0f; o1[r] = 0.0f; }
+
+  for (int k0 = 0; k0 < g.n; k0 += SK) {
+    __syncthreads();
+    for (int idx = tid; idx < SK * (DH / 2); idx += blockDim.x) {
+      const int r = idx / (DH / 2), i = idx % (DH / 2);
+      float k1 = 0.0f, k2 = 0.0f, v1 = 0.0f, v2 = 0.0f;
+      if (k0 + r < g.n) {
+        const size_t rb = (size_t)g.row(k0 + r, si.S) * ld;
+        k1 = tof<T>(qkv[rb + hk + i]);
+        k2 = tof<T>(qkv[rb + hk + i + DH / 2]);
+        v1 = tof<T>(qkv[rb + hv + i]);
+        v2 = tof<T>(qkv[rb + hv + i + DH / 2]);
+        if (ROPE) {
+          const float2 c = rope[(size_t)(k0 + r) * (DH / 2) + i];
+          const float y1 = k1 * c.x - k2 * c.y, y2 = k2 * c.x + k1 * c.y;
+          k1 = roundT<T>(y1);
+          k2 = roundT<T>(y2);
+        }
+      }
+      Ks[r][i] = k1; Ks[r][i + DH / 2] = k2;
+      Vs[r][i] = v1; Vs[r][i + DH / 2] = v2;
+    }
+    if (tid < SK) {
+      const int kj = k0 + tid;
+      kbias[tid] = kj < g.n ? (tok[g.row(kj, si.S)] ? 0.0f : kMaskedScore) : -INFINITY;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int qr = warp * 4 + r;
+      float sc = 0.0f;
+#pragma unroll 16
+      for (int d = 0; d < DH; ++d) sc = fmaf(Qs[qr][d], Ks[lane][d], sc);
+      const float b = kbias[lane];
+      sc = b == 0.0f ? sc : b;
+      float mx = sc;
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float mn = fmaxf(m[r], mx);
+      const float corr = expf(m[r] - mn);
+      const float p = expf(sc - mn);
+      float ps = p;
+      for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+      l[r] = l[r] * corr + ps;
+      float a0 = o0[r] * corr, a1 = o1[r] * corr;
+      for (int j = 0; j < SK; ++j) {
+        const float pj = __shfl_sync(0xffffffffu, p, j);
+        a0 = fmaf(pj, Vs[j][2 * lane], a0);
+        a1 = fmaf(pj, Vs[j][2 * lane + 1], a1);
+      }
+      o0[r] = a0; o1[r] = a1;
+      m[r] = mn;
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int qi = q0 + warp * 4 + r;
+    if (qi < g.n) {
+      T* dst = out + (size_t)g.row(qi, si.S) * ldo + h * DH;
+      const float inv = 1.0f / l[r];
+      dst[2 * lane] = fromf<T>(o0[r] * inv);
+      dst[2 * lane + 1] = fromf<T>(o1[r] * inv);
+    }
+  }
+}
+
+}  // namespace
+
+int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int kcol, int vcol, void* out,
+                     int ldo, const uint8_t* tok, int num_sets, int S, int heads, int dkv,
+                     const int32_t* members, const int32_t* offsets, int num_groups, int max_group,
+                     const float* rope_cs, cudaStream_t st) {
+  CC2_REQUIRE(dkv == DH, "attention: d_kv must be %d (got %d)", DH, dkv);
+  CC2_REQUIRE(mode == 0 || mode == 1, "attention: bad mode");
+  CC2_REQUIRE(qkv && out && tok && num_sets > 0 && S > 0 && heads > 0, "attention: bad args");
+  CC2_REQUIRE(mode == 0 || (members && offsets && num_groups > 0 && max_group > 0),
+              "attention: group mode needs members/offsets");
+  SetInfo si{mode, S, members, offsets, num_groups};
+  const int nmax = mode == 0 ? S : max_group;
+  const float2* cs = (const float2*)rope_cs;
+  if (dtype == CC2_BF16) {
+    CC2_REQUIRE(ld % 8 == 0 && ldo % 8 == 0 && qcol % 8 == 0 && kcol % 8 == 0 && vcol % 8 == 0,
+                "attention(bf16): columns/pitches must be multiples of 8");
+    if (mode == 1 && max_group <= SK) {
+      dim3 grid((nmax + SQ - 1) / SQ, heads, num_sets);
+      attn_simt_kernel<bf16, false><<<grid, 128, 0, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out,
+                                                          ldo, tok, cs, si);
+    } else {
+      dim3 grid((nmax + QT - 1) / QT, heads, num_sets);
+      if (mode == 0 && cs)
+        attn_mma_kernel<true><<<grid, 128, 0, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out, ldo,
+                                                    tok, cs, si);
+      else
+        attn_mma_kernel<false><<<grid, 128, 0, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out, ldo,
+                                                     tok, cs, si);
+    }
+  } else if (dtype == CC2_F32) {
+    dim3 grid((nmax + SQ - 1) / SQ, heads, num_sets);
+    if (mode == 0 && cs)
+      attn_simt_kernel<float, true><<<grid, 128, 0, st>>>((const float*)qkv, ld, qcol, kcol, vcol, (float*)out,
+                                                          ldo, tok, cs, si);
+    else
+      attn_simt_kernel<float, false><<<grid, 128, 0, st>>>((const float*)qkv, ld, qcol, kcol, vcol, (float*)out,
+                                                           ldo, tok, cs, si);
+  } else {
+    CC2_REQUIRE(false, "attention: unsupported dtype %d", dtype);
+  }
+  CC2_CHECK_LAUNCH();
+  return CC2_OK;
+}
+
+}  // namespace cc2

@@ -1,0 +1,92 @@
+// Shared helpers of the cc2 engine: status handling, element conversions,
+// the device-side error word used by bounded waits.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cstdint>
+#include <cstdio>
+#include <string>
+
+#include "../../include/cc2.h"
+
+namespace cc2 {
+
+// ---- host-side status -------------------------------------------------------
+void set_error(const char* fmt, ...);
+void clear_error();
+
+#define CC2_REQUIRE(cond, ...)                 \
+  do {                                         \
+    if (!(cond)) {                             \
+      ::cc2::set_error(__VA_ARGS__);           \
+      return CC2_E_INVALID;                    \
+    }                                          \
+  } while (0)
+
+#define CC2_CUDA(call)                                                        \
+  do {                                                                        \
+    cudaError_t e_ = (call);                                                  \
+    if (e_ != cudaSuccess) {                                                  \
+      ::cc2::set_error("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), \
+                       __FILE__, __LINE__);                                   \
+      return CC2_E_CUDA;                                                      \
+    }                                                                         \
+  } while (0)
+
+#define CC2_CHECK_LAUNCH()                                                     \
+  do {                                                                         \
+    cudaError_t e_ = cudaGetLastError();                                       \
+    if (e_ != cudaSuccess) {                                                   \
+      ::cc2::set_error("kernel launch failed: %s (%s:%d)", cudaGetErrorString(e_), \
+                       __FILE__, __LINE__);                                    \
+      return CC2_E_CUDA;                                                       \
+    }                                                                          \
+  } while (0)
+
+#define CC2_TRY(expr)          \
+  do {                         \
+    int s_ = (expr);           \
+    if (s_ != CC2_OK) return s_; \
+  } while (0)
+
+int num_sms();
+
+// ---- device-side error word -------------------------------------------------
+// Bit flags written by kernels whose bounded waits gave up.
+enum : int {
+  DEV_ERR_GEMM_TIMEOUT = 1,
+};
+// Reads (and optionally clears) the device error word of the current device.
+int read_device_error(int clear, int* value);
+
+// Wall-clock limit for any spin-wait inside a kernel (nanoseconds).
+constexpr unsigned long long kWaitLimitNs = 2000ull * 1000ull * 1000ull;
+
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- element conversions ----------------------------------------------------
+template <typename T> struct Elem;
+template <> struct Elem<float> {
+  static __device__ __forceinline__ float to_f(float x) { return x; }
+  static __device__ __forceinline__ float from_f(float x) { return x; }
+  static constexpr int code = CC2_F32;
+};
+template <> struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ float to_f(__nv_bfloat16 x) { return __bfloat162float(x); }
+  static __device__ __forceinline__ __nv_bfloat16 from_f(float x) { return __float2bfloat16_rn(x); }
+  static constexpr int code = CC2_BF16;
+};
+
+template <typename T> __device__ __forceinline__ float tof(T x) { return Elem<T>::to_f(x); }
+template <typename T> __device__ __forceinline__ T fromf(float x) { return Elem<T>::from_f(x); }
+// Round-trip through T (models the reference's intermediate casts).
+template <typename T> __device__ __forceinline__ float roundT(float x) { return tof<T>(fromf<T>(x)); }
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace cc2

@@ -1,0 +1,636 @@
+// cc2 engine: weight packing, workspace layout, forward orchestration and the
+// C ABI declared in include/cc2.h.
+//
+// Forward (CuteChronos2Model.forward, cutechronos/model.py:738-831) as launched
+// here, for B series of S = P + 1 + N tokens, M = B*S rows, d = d_model:
+//   preprocess           -> E[:, dff:dff+3ps] rows (context/REG/future), token mask, loc, scale
+//   gemm  E[:,dff:] @ W1^T + b1, ReLU               -> E[:, :dff]      (input ResidualBlock hidden)
+//   gemm  E @ [W2|W3]^T + (b2+b3), REG row := shared[1], ssq0 -> X    (hidden + skip in one GEMM)
+//   per layer l:
+//     gemm  X @ Wqkv_t^T * rs(ssq[3l])              -> QKV             (RMSNorm folded)
+//     attention mode 0 (RoPE, key mask)             -> ATT
+//     gemm  ATT @ Wo_t^T + X, ssq[3l+1]             -> X
+//     group size 1: gemm X @ Wv_g^T * rs(ssq[3l+1]) -> ATT             (softmax over one key = V)
+//     else:         gemm X @ Wqkv_g^T * rs -> QKV; attention mode 1 -> ATT
+//     gemm  ATT @ Wo_g^T + X, ssq[3l+2]             -> X
+//     gemm  X @ Wi^T * rs(ssq[3l+2]), ReLU          -> E (as [M, dff])
+//     gemm  E @ Wo^T + X, ssq[3l+3]                 -> X
+//   rmsnorm_rows (final norm of the N future rows)  -> O[:, dff:]
+//   gemm  O[:,dff:] @ W1o^T + b1o, ReLU             -> O[:, :dff]
+//   gemm  O @ [W2o|W3o]^T + (b2o+b3o)               -> PRED [B*N, Q*ps]
+//   output_transform (rearrange, sinh, unscale)     -> out [B, Q, N*ps]
+#include <cmath>
+#include <cstdarg>
+#include <cstring>
+#include <mutex>
+#include <numeric>
+#include <unordered_map>
+#include <vector>
+
+#include "common.cuh"
+
+namespace cc2 {
+
+// ---- status -----------------------------------------------------------------
+static thread_local std::string t_error;
+void set_error(const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_error = buf;
+}
+void clear_error() { t_error.clear(); }
+
+int num_sms() {
+  static int cache[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+// ---- kernels implemented in the other translation units ----------------------
+int launch_preprocess(const float*, const float*, int, int, int, int, float, int, int, int, int, void*, int,
+                      int, uint8_t*, float*, float*, float*, cudaStream_t);
+int launch_output_transform(int, const void*, int, const float*, const float*, void*, int, int, int, int, int,
+                            cudaStream_t);
+int launch_rmsnorm_rows(int, const void*, int, const void*, void*, int, int, int, int, int, int, float,
+                        cudaStream_t);
+int launch_gemm_tc(const void*, int, const void*, int, void*, int, int, int, int, const cc2_epilogue*,
+                   cudaStream_t);
+int launch_gemm_f32(const void*, int, const void*, int, void*, int, int, int, int, const cc2_epilogue*,
+                    cudaStream_t);
+int launch_attention(int, int, const void*, int, int, int, int, void*, int, const uint8_t*, int, int, int, int,
+                     const int32_t*, const int32_t*, int, int, const float*, cudaStream_t);
+
+// ---- packing kernels ------------------------------------------------------------
+template <typename T>
+__global__ void pack_matrix_kernel(T* dst, int ldd, const T* src, int rows, int cols, const T* colscale) {
+  const size_t total = (size_t)rows * cols;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / cols), c = (int)(i % cols);
+    float v = tof<T>(src[i]);
+    if (colscale) v *= tof<T>(colscale[c]);
+    dst[(size_t)r * ldd + c] = fromf<T>(v);
+  }
+}
+template <typename T>
+__global__ void pack_bias_kernel(float* dst, const T* a, const T* b, int n) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
+    dst[i] = tof<T>(a[i]) + (b ? tof<T>(b[i]) : 0.0f);
+}
+
+static int elem_size(int dtype) { return dtype == CC2_BF16 ? 2 : 4; }
+
+template <typename T>
+static int pack_matrix_t(void* dst, int ldd, const void* src, int rows, int cols, const void* colscale,
+                         cudaStream_t st) {
+  CC2_REQUIRE(src != nullptr, "pack: null weight pointer");
+  pack_matrix_kernel<T><<<std::min(4096, (rows * cols + 255) / 256), 256, 0, st>>>(
+      (T*)dst, ldd, (const T*)src, rows, cols, (const T*)colscale);
+  CC2_CHECK_LAUNCH();
+  return CC2_OK;
+}
+static int pack_matrix(int dtype, void* dst, int ldd, const void* src, int rows, int cols, const void* colscale,
+                       cudaStream_t st) {
+  return dtype == CC2_BF16 ? pack_matrix_t<__nv_bfloat16>(dst, ldd, src, rows, cols, colscale, st)
+                           : pack_matrix_t<float>(dst, ldd, src, rows, cols, colscale, st);
+}
+static int pack_bias(int dtype, float* dst, const void* a, const void* b, int n, cudaStream_t st) {
+  CC2_REQUIRE(a != nullptr, "pack: null bias pointer");
+  if (dtype == CC2_BF16)
+    pack_bias_kernel<__nv_bfloat16><<<(n + 255) / 256, 256, 0, st>>>(dst, (const __nv_bfloat16*)a,
+                                                                     (const __nv_bfloat16*)b, n);
+  else
+    pack_bias_kernel<float><<<(n + 255) / 256, 256, 0, st>>>(dst, (const float*)a, (const float*)b, n);
+  CC2_CHECK_LAUNCH();
+  return CC2_OK;
+}
+
+// ---- launch profiling ---------------------------------------------------------------
+struct ProfRecord {
+  int kind;
+  double flops, bytes;
+};
+struct Profiler {
+  bool on = false;
+  int cap = 0;
+  std::vector<cudaEvent_t> ev;
+  std::vector<ProfRecord> rec;
+};
+static thread_local Profiler t_prof;
+
+// Brackets one launch with events when profiling is on.
+struct ProfScope {
+  cudaStream_t st;
+  bool active;
+  ProfScope(int kind, double flops, double bytes, cudaStream_t s) : st(s), active(false) {
+    Profiler& p = t_prof;
+    if (!p.on || (int)p.rec.size() >= p.cap) return;
+    const size_t i = p.rec.size();
+    p.rec.push_back({kind, flops, bytes});
+    cudaEventRecord(p.ev[2 * i], st);
+    active = true;
+  }
+  ~ProfScope() {
+    if (active) cudaEventRecord(t_prof.ev[2 * (t_prof.rec.size() - 1) + 1], st);
+  }
+};
+
+}  // namespace cc2
+
+using namespace cc2;
+
+// ---- model handle ---------------------------------------------------------------
+struct cc2_layer_pack {
+  void* wqkv_t; void* wo_t; void* wqkv_g; void* wo_g; void* wi; void* wo_f;
+};
+
+struct cc2_model {
+  cc2_config cfg;
+  int dtype;
+  int esz;
+  int in_dim;    // 3 * patch
+  int kin;       // dff + in_dim (input ResidualBlock fused K)
+  int kin_pad;   // kin rounded up to 64
+  int kout;      // dff + d (output ResidualBlock fused K)
+  int qps;       // num_quantiles * patch
+  int max_pos;   // RoPE table rows
+  std::vector<cc2_layer_pack> layers;
+  void* w1_in; float* b1_in; void* w23_in; float* b23_in; float* reg;
+  void* final_ln; void* w1_out; float* b1_out; void* w23_out; float* b23_out;
+  float* rope;
+};
+
+namespace {
+
+struct Planner {
+  size_t off = 0;
+  size_t take(size_t bytes) {
+    size_t o = off;
+    off = align_up(off + bytes, 256);
+    return o;
+  }
+};
+
+int validate_cfg(const cc2_config* c) {
+  CC2_REQUIRE(c != nullptr, "config is null");
+  CC2_REQUIRE(c->d_kv == 64, "d_kv must be 64 (got %d)", c->d_kv);
+  CC2_REQUIRE(c->num_heads * c->d_kv == c->d_model, "num_heads * d_kv must equal d_model");
+  CC2_REQUIRE(c->d_model % 64 == 0 && c->d_ff % 64 == 0, "d_model and d_ff must be multiples of 64");
+  CC2_REQUIRE(c->input_patch_size == c->output_patch_size && c->input_patch_size > 0,
+              "input and output patch sizes must match");
+  CC2_REQUIRE(c->num_layers > 0 && c->num_quantiles > 0 && c->context_length > 0, "bad config sizes");
+  CC2_REQUIRE((c->num_quantiles * c->output_patch_size) % 16 == 0,
+              "num_quantiles * output_patch_size must be a multiple of 16");
+  CC2_REQUIRE((3 * c->input_patch_size) % 8 == 0, "3 * patch size must be a multiple of 8");
+  CC2_REQUIRE(c->max_output_patches > 0, "max_output_patches must be positive");
+  CC2_REQUIRE(c->time_encoding_scale != 0.0f, "time_encoding_scale must be non-zero");
+  return CC2_OK;
+}
+
+// Layout of the packed weight buffer (offsets in bytes); fills `m` pointers when base != null.
+size_t plan_pack(const cc2_config& c, int dtype, cc2_model* m, char* base) {
+  const size_t e = elem_size(dtype);
+  const int d = c.d_model, dff = c.d_ff, in = 3 * c.input_patch_size;
+  const int kin_pad = (int)align_up(dff + in, 64);
+  const int qps = c.num_quantiles * c.output_patch_size;
+  const int max_pos = (c.context_length + c.input_patch_size - 1) / c.input_patch_size + 1 + c.max_output_patches;
+  Planner p;
+  std::vector<size_t> lo;
+  for (int l = 0; l < c.num_layers; ++l) {
+    lo.push_back(p.take(e * 3 * d * d));
+    lo.push_back(p.take(e * d * d));
+    lo.push_back(p.take(e * 3 * d * d));
+    lo.push_back(p.take(e * d * d));
+    lo.push_back(p.take(e * (size_t)dff * d));
+    lo.push_back(p.take(e * (size_t)d * dff));
+  }
+  size_t o_w1_in = p.take(e * (size_t)dff * in), o_b1_in = p.take(4 * dff);
+  size_t o_w23_in = p.take(e * (size_t)d * kin_pad), o_b23_in = p.take(4 * d), o_reg = p.take(4 * d);
+  size_t o_fln = p.take(e * d), o_w1_out = p.take(e * (size_t)dff * d), o_b1_out = p.take(4 * dff);
+  size_t o_w23_out = p.take(e * (size_t)qps * (dff + d)), o_b23_out = p.take(4 * qps);
+  size_t o_rope = p.take(sizeof(float) * 2 * (size_t)max_pos * (c.d_kv / 2));
+  if (m && base) {
+    m->layers.resize(c.num_layers);
+    for (int l = 0; l < c.num_layers; ++l) {
+      cc2_layer_pack& L = m->layers[l];
+      L.wqkv_t = base + lo[6 * l + 0]; L.wo_t = base + lo[6 * l + 1];
+      L.wqkv_g = base + lo[6 * l + 2]; L.wo_g = base + lo[6 * l + 3];
+      L.wi = base + lo[6 * l + 4]; L.wo_f = base + lo[6 * l + 5];
+    }
+    m->w1_in = base + o_w1_in; m->b1_in = (float*)(base + o_b1_in);
+    m->w23_in = base + o_w23_in; m->b23_in = (float*)(base + o_b23_in); m->reg = (float*)(base + o_reg);
+    m->final_ln = base + o_fln; m->w1_out = base + o_w1_out; m->b1_out = (float*)(base + o_b1_out);
+    m->w23_out = base + o_w23_out; m->b23_out = (float*)(base + o_b23_out); m->rope = (float*)(base + o_rope);
+    m->in_dim = in; m->kin = dff + in; m->kin_pad = kin_pad; m->kout = dff + d; m->qps = qps; m->max_pos = max_pos;
+  }
+  return p.off;
+}
+
+struct Workspace {
+  char* E; char* X; char* QKV; char* ATT; float* ssq; uint8_t* tok; float* loc; float* scale;
+  int32_t* members; int32_t* offsets; char* O; char* PRED;
+};
+
+size_t plan_ws(const cc2_model& m, int B, int L, int N, Workspace* w, char* base) {
+  const cc2_config& c = m.cfg;
+  const size_t e = m.esz;
+  const int Leff = std::min(L, c.context_length);
+  const int P = (Leff + c.input_patch_size - 1) / c.input_patch_size;
+  const int S = P + (c.use_reg_token ? 1 : 0) + N;
+  const size_t M = (size_t)B * S;
+  const int d = c.d_model, dff = c.d_ff;
+  const int KE = std::max(m.kin_pad, dff);
+  Planner p;
+  size_t oE = p.take(e * M * KE), oX = p.take(e * M * d), oQKV = p.take(e * M * 3 * d), oATT = p.take(e * M * d);
+  const size_t groups = (size_t)(d + 63) / 64;  // 64-column partial sums of squares
+  size_t oSSQ = p.take(4 * M * groups * 2), oTOK = p.take(M);
+  size_t oLOC = p.take(4 * B), oSC = p.take(4 * B), oMEM = p.take(4 * B), oOFF = p.take(4 * (B + 1));
+  size_t oO = p.take(e * (size_t)B * N * m.kout), oPRED = p.take(e * (size_t)B * N * m.qps);
+  if (w && base) {
+    w->E = base + oE; w->X = base + oX; w->QKV = base + oQKV; w->ATT = base + oATT;
+    w->ssq = (float*)(base + oSSQ); w->tok = (uint8_t*)(base + oTOK);
+    w->loc = (float*)(base + oLOC); w->scale = (float*)(base + oSC);
+    w->members = (int32_t*)(base + oMEM); w->offsets = (int32_t*)(base + oOFF);
+    w->O = base + oO; w->PRED = base + oPRED;
+  }
+  return p.off;
+}
+
+int gemm(int dtype, const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,
+         const cc2_epilogue* e, cudaStream_t st) {
+  ProfScope ps_(CC2_K_GEMM, 2.0 * M * N * K, 0.0, st);
+  if (dtype == CC2_BF16) return launch_gemm_tc(A, lda, W, ldw, out, ldo, M, N, K, e, st);
+  return launch_gemm_f32(A, lda, W, ldw, out, ldo, M, N, K, e, st);
+}
+
+cc2_epilogue epi(int flags) {
+  cc2_epilogue e;
+  std::memset(&e, 0, sizeof(e));
+  e.flags = flags;
+  return e;
+}
+
+cc2_epilogue epi_m(int flags, int M) {
+  cc2_epilogue e = epi(flags);
+  e.ssq_ld = M;
+  return e;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* cc2_last_error(void) { return t_error.c_str(); }
+const char* cc2_version(void) { return "cc2-b200 0.1 (sm_100a)"; }
+
+int cc2_device_status(int clear) {
+  clear_error();
+  CC2_CUDA(cudaDeviceSynchronize());
+  int v = 0;
+  CC2_TRY(read_device_error(clear, &v));
+  return v;
+}
+
+int cc2_model_pack_bytes(const cc2_config* cfg, int dtype, size_t* bytes) {
+  clear_error();
+  CC2_TRY(validate_cfg(cfg));
+  CC2_REQUIRE(dtype == CC2_BF16 || dtype == CC2_F32, "unsupported dtype %d", dtype);
+  CC2_REQUIRE(bytes != nullptr, "bytes is null");
+  *bytes = plan_pack(*cfg, dtype, nullptr, nullptr);
+  return CC2_OK;
+}
+
+int cc2_model_create(const cc2_config* cfg, int dtype, const cc2_weights* w, void* pack_buf, size_t pack_bytes,
+                     void* stream, cc2_model** out) {
+  clear_error();
+  CC2_TRY(validate_cfg(cfg));
+  CC2_REQUIRE(dtype == CC2_BF16 || dtype == CC2_F32, "unsupported dtype %d", dtype);
+  CC2_REQUIRE(w && pack_buf && out, "null argument");
+  CC2_REQUIRE(((uintptr_t)pack_buf & 255u) == 0, "pack buffer must be 256-byte aligned");
+  const size_t need = plan_pack(*cfg, dtype, nullptr, nullptr);
+  if (pack_bytes < need) {
+    set_error("pack buffer too small: %zu < %zu", pack_bytes, need);
+    return CC2_E_WORKSPACE;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  cc2_model* m = new cc2_model();
+  m->cfg = *cfg;
+  m->dtype = dtype;
+  m->esz = elem_size(dtype);
+  plan_pack(*cfg, dtype, m, (char*)pack_buf);
+  const cc2_config& c = *cfg;
+  const int d = c.d_model, dff = c.d_ff, in = m->in_dim;
+  const size_t e = m->esz;
+  auto fail = [&](int s) { delete m; return s; };
+  int s = CC2_OK;
+#define PK(expr) do { s = (expr); if (s != CC2_OK) return fail(s); } while (0)
+  for (int l = 0; l < c.num_layers; ++l) {
+    cc2_layer_pack& L = m->layers[l];
+    CC2_REQUIRE(w->time_q && w->time_k && w->time_v && w->time_o && w->time_ln && w->group_q && w->group_k &&
+                    w->group_v && w->group_o && w->group_ln && w->ff_ln && w->ff_wi && w->ff_wo,
+                "per-layer weight arrays must be non-null");
+    PK(pack_matrix(dtype, L.wqkv_t, d, w->time_q[l], d, d, w->time_ln[l], st));
+    PK(pack_matrix(dtype, (char*)L.wqkv_t + e * d * d, d, w->time_k[l], d, d, w->time_ln[l], st));
+    PK(pack_matrix(dtype, (char*)L.wqkv_t + 2 * e * d * d, d, w->time_v[l], d, d, w->time_ln[l], st));
+    PK(pack_matrix(dtype, L.wo_t, d, w->time_o[l], d, d, nullptr, st));
+    PK(pack_matrix(dtype, L.wqkv_g, d, w->group_q[l], d, d, w->group_ln[l], st));
+    PK(pack_matrix(dtype, (char*)L.wqkv_g + e * d * d, d, w->group_k[l], d, d, w->group_ln[l], st));
+    PK(pack_matrix(dtype, (char*)L.wqkv_g + 2 * e * d * d, d, w->group_v[l], d, d, w->group_ln[l], st));
+    PK(pack_matrix(dtype, L.wo_g, d, w->group_o[l], d, d, nullptr, st));
+    PK(pack_matrix(dtype, L.wi, d, w->ff_wi[l], dff, d, w->ff_ln[l], st));
+    PK(pack_matrix(dtype, L.wo_f, dff, w->ff_wo[l], d, dff, nullptr, st));
+  }
+  PK(pack_matrix(dtype, m->w1_in, in, w->in_hidden_w, dff, in, nullptr, st));
+  PK(pack_bias(dtype, m->b1_in, w->in_hidden_b, nullptr, dff, st));
+  if (cudaMemsetAsync(m->w23_in, 0, e * (size_t)d * m->kin_pad, st) != cudaSuccess) {
+    set_error("memset failed");
+    return fail(CC2_E_CUDA);
+  }
+  PK(pack_matrix(dtype, m->w23_in, m->kin_pad, w->in_output_w, d, dff, nullptr, st));
+  PK(pack_matrix(dtype, (char*)m->w23_in + e * dff, m->kin_pad, w->in_residual_w, d, in, nullptr, st));
+  PK(pack_bias(dtype, m->b23_in, w->in_output_b, w->in_residual_b, d, st));
+  CC2_REQUIRE(w->shared != nullptr, "shared embedding is null");
+  PK(pack_bias(dtype, m->reg, (const char*)w->shared + e * (size_t)c.reg_token_id * d, nullptr, d, st));
+  PK(pack_matrix(dtype, m->final_ln, d, w->final_ln, 1, d, nullptr, st));
+  PK(pack_matrix(dtype, m->w1_out, d, w->out_hidden_w, dff, d, nullptr, st));
+  PK(pack_bias(dtype, m->b1_out, w->out_hidden_b, nullptr, dff, st));
+  PK(pack_matrix(dtype, m->w23_out, m->kout, w->out_output_w, m->qps, dff, nullptr, st));
+  PK(pack_matrix(dtype, (char*)m->w23_out + e * dff, m->kout, w->out_residual_w, m->qps, d, nullptr, st));
+  PK(pack_bias(dtype, m->b23_out, w->out_output_b, w->out_residual_b, m->qps, st));
+#undef PK
+  // RoPE table: inv_freq = 1 / theta^(2i/d_kv) and freq = inv_freq * pos in fp32
+  // as in model.py:200-203 / 94-109; cos/sin of the fp32 angle.
+  const int half = c.d_kv / 2;
+  std::vector<float> tab((size_t)m->max_pos * half * 2);
+  for (int i = 0; i < half; ++i) {
+    const float expo = (float)(2 * i) / (float)c.d_kv;
+    const float inv = 1.0f / std::pow(c.rope_theta, expo);
+    for (int pos = 0; pos < m->max_pos; ++pos) {
+      const float f = inv * (float)pos;
+      tab[((size_t)pos * half + i) * 2 + 0] = (float)std::cos((double)f);
+      tab[((size_t)pos * half + i) * 2 + 1] = (float)std::sin((double)f);
+    }
+  }
+  if (cudaMemcpyAsync(m->rope, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess) {
+    set_error("uploading the RoPE table failed");
+    return fail(CC2_E_CUDA);
+  }
+  *out = m;
+  return CC2_OK;
+}
+
+int cc2_model_destroy(cc2_model* m) {
+  delete m;
+  return CC2_OK;
+}
+
+int cc2_group_layout(const int64_t* gid, int B, int32_t* members, int32_t* offsets, int* num_groups,
+                     int* max_group) {
+  clear_error();
+  CC2_REQUIRE(gid && members && offsets && num_groups && max_group && B > 0, "group_layout: bad args");
+  std::unordered_map<int64_t, int> index;
+  std::vector<std::vector<int>> groups;
+  for (int b = 0; b < B; ++b) {
+    auto it = index.find(gid[b]);
+    if (it == index.end()) {
+      index.emplace(gid[b], (int)groups.size());
+      groups.push_back({b});
+    } else {
+      groups[it->second].push_back(b);
+    }
+  }
+  int k = 0, mg = 0;
+  offsets[0] = 0;
+  for (size_t g = 0; g < groups.size(); ++g) {
+    for (int b : groups[g]) members[k++] = b;
+    offsets[g + 1] = k;
+    mg = std::max(mg, (int)groups[g].size());
+  }
+  *num_groups = (int)groups.size();
+  *max_group = mg;
+  return CC2_OK;
+}
+
+int cc2_forward_workspace_bytes(const cc2_model* m, int B, int L, int N, int max_group, size_t* bytes) {
+  clear_error();
+  CC2_REQUIRE(m && bytes && B > 0 && L > 0 && N > 0 && max_group > 0, "workspace_bytes: bad args");
+  *bytes = plan_ws(*m, B, L, N, nullptr, nullptr);
+  return CC2_OK;
+}
+
+int cc2_forward(const cc2_model* m, const float* context, const float* context_mask, int B, int L, int N,
+                const int64_t* group_ids, void* out, float* loc, float* scale, void* workspace, size_t ws_bytes,
+                void* stream) {
+  clear_error();
+  CC2_REQUIRE(m && context && out && workspace, "forward: null argument");
+  CC2_REQUIRE(B > 0 && L > 0, "forward: B and L must be positive");
+  CC2_REQUIRE(N > 0 && N <= m->cfg.max_output_patches, "forward: N must be in [1, %d]", m->cfg.max_output_patches);
+  CC2_REQUIRE(((uintptr_t)workspace & 255u) == 0, "workspace must be 256-byte aligned");
+  const cc2_config& c = m->cfg;
+  cudaStream_t st = (cudaStream_t)stream;
+  const size_t need = plan_ws(*m, B, L, N, nullptr, nullptr);
+  if (ws_bytes < need) {
+    set_error("workspace too small: %zu < %zu", ws_bytes, need);
+    return CC2_E_WORKSPACE;
+  }
+  Workspace w;
+  plan_ws(*m, B, L, N, &w, (char*)workspace);
+  const int dt = m->dtype;
+  const size_t e = m->esz;
+  const int d = c.d_model, dff = c.d_ff, ps = c.input_patch_size;
+  const int Leff = std::min(L, c.context_length);
+  const int P = (Leff + ps - 1) / ps;
+  const int reg = c.use_reg_token ? 1 : 0;
+  const int S = P + reg + N;
+  CC2_REQUIRE(S <= m->max_pos, "forward: sequence of %d tokens exceeds the RoPE table (%d)", S, m->max_pos);
+  const int M = B * S;
+  const int KE = std::max(m->kin_pad, dff);
+  const float eps = c.layer_norm_epsilon;
+
+  // group structure
+  int num_groups = B, max_group = 1;
+  double gsq = (double)B;  // sum over groups of size^2 (attention FLOP count)
+  if (group_ids) {
+    std::vector<int32_t> mem(B), off(B + 1);
+    CC2_TRY(cc2_group_layout(group_ids, B, mem.data(), off.data(), &num_groups, &max_group));
+    gsq = 0.0;
+    for (int g = 0; g < num_groups; ++g) gsq += (double)(off[g + 1] - off[g]) * (off[g + 1] - off[g]);
+    if (max_group > 1) {
+      CC2_CUDA(cudaMemcpyAsync(w.members, mem.data(), sizeof(int32_t) * B, cudaMemcpyHostToDevice, st));
+      CC2_CUDA(cudaMemcpyAsync(w.offsets, off.data(), sizeof(int32_t) * (num_groups + 1), cudaMemcpyHostToDevice, st));
+    }
+  }
+  float* locp = loc ? loc : w.loc;
+  float* scp = scale ? scale : w.scale;
+  // RMS statistics: norm i's partial sums live in buffer i % 2 (its producer
+  // runs after the consumer of norm i-2 in stream order).
+  const size_t groups = (size_t)(d + 63) / 64;
+  auto ssq = [&](int i) { return w.ssq + (size_t)(i & 1) * groups * M; };
+
+  // preprocessing -> E[:, dff : dff + 3ps] (+ zero pad up to kin_pad)
+  {
+  ProfScope ps_(CC2_K_PREPROCESS, 0.0, (double)B * (4.0 * Leff + e * 3 * ps * P + P + 8), st);
+  CC2_TRY(launch_preprocess(context, context_mask, B, L, ps, c.context_length, c.time_encoding_scale,
+                            c.use_arcsinh, reg, N, dt, w.E + e * dff, m->kin_pad, m->kin_pad - dff, w.tok, nullptr,
+                            locp, scp, st));
+  }
+  // input ResidualBlock
+  {
+    cc2_epilogue e1 = epi_m(CC2_EPI_BIAS | CC2_EPI_RELU, M);
+    e1.bias = m->b1_in;
+    CC2_TRY(gemm(dt, w.E + e * dff, m->kin_pad, m->w1_in, m->in_dim, w.E, m->kin_pad, M, dff, m->in_dim, &e1, st));
+    cc2_epilogue e2 = epi_m(CC2_EPI_BIAS | CC2_EPI_SSQ | (reg ? CC2_EPI_SPECIAL : 0), M);
+    e2.bias = m->b23_in;
+    e2.ssq_out = ssq(0);
+    e2.special = m->reg;
+    e2.special_period = S;
+    e2.special_offset = P;
+    CC2_TRY(gemm(dt, w.E, m->kin_pad, m->w23_in, m->kin_pad, w.X, d, M, d, m->kin_pad, &e2, st));
+  }
+  for (int l = 0; l < c.num_layers; ++l) {
+    const cc2_layer_pack& Lw = m->layers[l];
+    // time attention
+    cc2_epilogue a = epi_m(CC2_EPI_ROWSCALE, M);
+    a.ssq_in = ssq(3 * l); a.norm_dim = d; a.eps = eps;
+    CC2_TRY(gemm(dt, w.X, d, Lw.wqkv_t, d, w.QKV, 3 * d, M, 3 * d, d, &a, st));
+    {
+      ProfScope ps_(CC2_K_ATTN_TIME, 4.0 * B * (double)S * S * d, 0.0, st);
+      CC2_TRY(launch_attention(dt, 0, w.QKV, 3 * d, 0, d, 2 * d, w.ATT, d, w.tok, B, S, c.num_heads, c.d_kv,
+                               nullptr, nullptr, 0, 0, m->rope, st));
+    }
+    cc2_epilogue o = epi_m(CC2_EPI_RESID | CC2_EPI_SSQ, M);
+    o.resid = w.X; o.ld_resid = d; o.ssq_out = ssq(3 * l + 1);
+    CC2_TRY(gemm(dt, w.ATT, d, Lw.wo_t, d, w.X, d, M, d, d, &o, st));
+    // group attention
+    cc2_epilogue g = epi_m(CC2_EPI_ROWSCALE, M);
+    g.ssq_in = ssq(3 * l + 1); g.norm_dim = d; g.eps = eps;
+    if (max_group == 1) {
+      // softmax over a single unmasked key is exactly 1: the output is V
+      CC2_TRY(gemm(dt, w.X, d, (const char*)Lw.wqkv_g + e * 2 * d * d, d, w.ATT, d, M, d, d, &g, st));
+    } else {
+      CC2_TRY(gemm(dt, w.X, d, Lw.wqkv_g, d, w.QKV, 3 * d, M, 3 * d, d, &g, st));
+      ProfScope ps_(CC2_K_ATTN_GROUP, 4.0 * (double)S * gsq * d, 0.0, st);
+      CC2_TRY(launch_attention(dt, 1, w.QKV, 3 * d, 0, d, 2 * d, w.ATT, d, w.tok, S * num_groups, S, c.num_heads,
+                               c.d_kv, w.members, w.offsets, num_groups, max_group, nullptr, st));
+    }
+    cc2_epilogue og = epi_m(CC2_EPI_RESID | CC2_EPI_SSQ, M);
+    og.resid = w.X; og.ld_resid = d; og.ssq_out = ssq(3 * l + 2);
+    CC2_TRY(gemm(dt, w.ATT, d, Lw.wo_g, d, w.X, d, M, d, d, &og, st));
+    // feed-forward
+    cc2_epilogue f1 = epi_m(CC2_EPI_ROWSCALE | CC2_EPI_RELU, M);
+    f1.ssq_in = ssq(3 * l + 2); f1.norm_dim = d; f1.eps = eps;
+    CC2_TRY(gemm(dt, w.X, d, Lw.wi, d, w.E, dff, M, dff, d, &f1, st));
+    cc2_epilogue f2 = epi_m(CC2_EPI_RESID | CC2_EPI_SSQ, M);
+    f2.resid = w.X; f2.ld_resid = d; f2.ssq_out = ssq(3 * l + 3);
+    CC2_TRY(gemm(dt, w.E, dff, Lw.wo_f, dff, w.X, d, M, d, dff, &f2, st));
+  }
+  (void)KE;
+  // final RMSNorm of the N future rows -> O[:, dff:]
+  const int BN_rows = B * N;
+  {
+    ProfScope ps_(CC2_K_RMSNORM, 0.0, 2.0 * e * BN_rows * d, st);
+    CC2_TRY(launch_rmsnorm_rows(dt, w.X, d, m->final_ln, w.O + e * dff, m->kout, BN_rows, d, N, S, S - N, eps, st));
+  }
+  // output ResidualBlock
+  {
+    cc2_epilogue e1 = epi_m(CC2_EPI_BIAS | CC2_EPI_RELU, M);
+    e1.bias = m->b1_out;
+    CC2_TRY(gemm(dt, w.O + e * dff, m->kout, m->w1_out, d, w.O, m->kout, BN_rows, dff, d, &e1, st));
+    cc2_epilogue e2 = epi_m(CC2_EPI_BIAS, M);
+    e2.bias = m->b23_out;
+    CC2_TRY(gemm(dt, w.O, m->kout, m->w23_out, m->kout, w.PRED, m->qps, BN_rows, m->qps, m->kout, &e2, st));
+  }
+  {
+    ProfScope ps_(CC2_K_OUTPUT, 0.0, (double)B * (2.0 * e * m->qps * N + 8), st);
+    CC2_TRY(launch_output_transform(dt, w.PRED, m->qps, locp, scp, out, B, N, c.num_quantiles, c.output_patch_size,
+                                    c.use_arcsinh, st));
+  }
+  return CC2_OK;
+}
+
+int cc2_profile_begin(int capacity) {
+  clear_error();
+  CC2_REQUIRE(capacity > 0, "profile capacity must be positive");
+  Profiler& p = t_prof;
+  for (cudaEvent_t e : p.ev) cudaEventDestroy(e);
+  p.ev.assign(2 * (size_t)capacity, nullptr);
+  for (auto& e : p.ev) CC2_CUDA(cudaEventCreate(&e));
+  p.rec.clear();
+  p.rec.reserve(capacity);
+  p.cap = capacity;
+  p.on = true;
+  return CC2_OK;
+}
+
+int cc2_profile_read(int* kinds, float* ms, double* flops, double* bytes, int capacity, int* count) {
+  clear_error();
+  Profiler& p = t_prof;
+  p.on = false;
+  const int n = (int)p.rec.size();
+  if (count) *count = n;
+  for (int i = 0; i < n && i < capacity; ++i) {
+    CC2_CUDA(cudaEventSynchronize(p.ev[2 * i + 1]));
+    float t = 0.0f;
+    CC2_CUDA(cudaEventElapsedTime(&t, p.ev[2 * i], p.ev[2 * i + 1]));
+    if (kinds) kinds[i] = p.rec[i].kind;
+    if (ms) ms[i] = t;
+    if (flops) flops[i] = p.rec[i].flops;
+    if (bytes) bytes[i] = p.rec[i].bytes;
+  }
+  for (cudaEvent_t e : p.ev) cudaEventDestroy(e);
+  p.ev.clear();
+  p.rec.clear();
+  return CC2_OK;
+}
+
+// ---- component entry points ---------------------------------------------------------
+int cc2_preprocess(const float* context, const float* context_mask, int B, int L, int patch_size, int context_length,
+                   float te_scale, int use_arcsinh, int use_reg, int N, int dtype, void* patched, int ld_patched,
+                   int pad_cols, uint8_t* token_mask, float* attn_mask, float* loc, float* scale, void* stream) {
+  clear_error();
+  return launch_preprocess(context, context_mask, B, L, patch_size, context_length, te_scale, use_arcsinh, use_reg,
+                           N, dtype, patched, ld_patched, pad_cols, token_mask, attn_mask, loc, scale,
+                           (cudaStream_t)stream);
+}
+
+int cc2_gemm(int dtype, const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,
+             const cc2_epilogue* epi_, void* stream) {
+  clear_error();
+  CC2_REQUIRE(dtype == CC2_BF16 || dtype == CC2_F32, "gemm: unsupported dtype %d", dtype);
+  CC2_REQUIRE(A && W && out, "gemm: null operand");
+  return gemm(dtype, A, lda, W, ldw, out, ldo, M, N, K, epi_, (cudaStream_t)stream);
+}
+
+int cc2_rmsnorm_rows(int dtype, const void* x, int ld_x, const void* w, void* y, int ld_y, int rows, int dim, int per,
+                     int stride, int offset, float eps, void* stream) {
+  clear_error();
+  return launch_rmsnorm_rows(dtype, x, ld_x, w, y, ld_y, rows, dim, per, stride, offset, eps, (cudaStream_t)stream);
+}
+
+int cc2_attention(int dtype, int mode, const void* qkv, int ld_qkv, int q_col, int k_col, int v_col, void* out,
+                  int ld_out, const uint8_t* token_mask, int num_sets, int S, int num_heads, int d_kv,
+                  const int32_t* members, const int32_t* offsets, int num_groups, int max_group, const float* rope_cs,
+                  void* stream) {
+  clear_error();
+  return launch_attention(dtype, mode, qkv, ld_qkv, q_col, k_col, v_col, out, ld_out, token_mask, num_sets, S,
+                          num_heads, d_kv, members, offsets, num_groups, max_group, rope_cs, (cudaStream_t)stream);
+}
+
+int cc2_output_transform(int dtype, const void* preds, int ld_preds, const float* loc, const float* scale, void* out,
+                         int B, int N, int Q, int ps, int use_arcsinh, void* stream) {
+  clear_error();
+  return launch_output_transform(dtype, preds, ld_preds, loc, scale, out, B, N, Q, ps, use_arcsinh,
+                                 (cudaStream_t)stream);
+}
+
+}  // extern "C"

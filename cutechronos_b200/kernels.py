@@ -1,0 +1,217 @@
+"""Torch-tensor entry points to the component kernels of the C ABI.
+
+Each function mirrors the signature and output layout of the reference op it
+replaces (paths inside lee101/cutedsl) and calls exactly one native kernel
+(``rms_layernorm`` / ``linear`` / ``unscaled_attention`` one each):
+
+  fused_preprocess        cutechronos/kernels.py:106-155 (-> cc2_preprocess)
+  fused_output_transform  cutechronos/triton_kernels/fused_output.py:83-140
+  rms_layernorm           cutechronos/kernel_backends.py:85-110
+  linear                  F.linear call sites with fused epilogues (cc2_gemm)
+  unscaled_attention      cutechronos/kernel_backends.py:113-153 (+ RoPE when
+                          ``rope=True``: triton_kernels/rope.py:126-180)
+  group_attention         cutechronos/model.py:295-312 attention core
+
+All inputs must be CUDA tensors; nothing here runs on the CPU.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+
+import torch
+
+from . import _native as nat
+
+_CODES = {torch.bfloat16: nat.CC2_BF16, torch.float32: nat.CC2_F32}
+
+
+def _code(dt: torch.dtype) -> int:
+    if dt not in _CODES:
+        raise TypeError(f"dtype {dt} not supported (bfloat16 / float32)")
+    return _CODES[dt]
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _cuda(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise RuntimeError("cutechronos_b200 kernels take CUDA tensors only (no CPU path)")
+
+
+def fused_preprocess(context: torch.Tensor, patch_size: int = 16, context_length: int = 512,
+                     use_arcsinh: bool = False, *, context_mask: torch.Tensor | None = None,
+                     time_encoding_scale: float | None = None, dtype: torch.dtype = torch.float32):
+    """-> (patched (B,P,3ps), attention_mask (B,P) f32, loc (B,1), scale (B,1))."""
+    _cuda(context, context_mask)
+    lib = nat.load()
+    ctx = context.float().contiguous()
+    mask = context_mask.float().contiguous() if context_mask is not None else None
+    B, L = ctx.shape
+    Leff = min(L, context_length)
+    P = math.ceil(Leff / patch_size)
+    dev = ctx.device
+    patched = torch.empty(B, P, 3 * patch_size, dtype=dtype, device=dev)
+    tok = torch.empty(B * P, dtype=torch.uint8, device=dev)
+    attn = torch.empty(B, P, dtype=torch.float32, device=dev)
+    loc = torch.empty(B, 1, dtype=torch.float32, device=dev)
+    scale = torch.empty(B, 1, dtype=torch.float32, device=dev)
+    tes = float(time_encoding_scale if time_encoding_scale is not None else context_length)
+    nat.check(lib.cc2_preprocess(ctx.data_ptr(), mask.data_ptr() if mask is not None else None, B, L, patch_size,
+                                 context_length, tes, int(use_arcsinh), 0, 0, _code(dtype), patched.data_ptr(),
+                                 3 * patch_size, 3 * patch_size, tok.data_ptr(), attn.data_ptr(), loc.data_ptr(),
+                                 scale.data_ptr(), _stream(ctx)), "cc2_preprocess")
+    return patched, attn, loc, scale
+
+
+def fused_output_transform(x: torch.Tensor, loc: torch.Tensor, scale: torch.Tensor, num_quantiles: int = 21,
+                           patch_size: int = 16, use_arcsinh: bool = True) -> torch.Tensor:
+    """(B, N, Q*P) -> (B, Q, N*P): rearrange, sinh, * scale + loc (in x's dtype)."""
+    _cuda(x, loc, scale)
+    B, N, QP = x.shape
+    if QP != num_quantiles * patch_size:
+        raise ValueError(f"Last dim of x ({QP}) must equal num_quantiles * patch_size")
+    x = x.contiguous()
+    out = torch.empty(B, num_quantiles, N * patch_size, dtype=x.dtype, device=x.device)
+    lf, sf = loc.reshape(B).float().contiguous(), scale.reshape(B).float().contiguous()
+    nat.check(nat.load().cc2_output_transform(_code(x.dtype), x.data_ptr(), QP, lf.data_ptr(), sf.data_ptr(),
+                                              out.data_ptr(), B, N, num_quantiles, patch_size, int(use_arcsinh),
+                                              _stream(x)), "cc2_output_transform")
+    return out
+
+
+def rms_layernorm(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """T5 RMSNorm over the last dim: weight * cast(x * rsqrt(mean(x^2) + eps))."""
+    _cuda(x, weight)
+    shape = x.shape
+    D = shape[-1]
+    x2 = x.reshape(-1, D).contiguous()
+    w = weight.to(x.dtype).contiguous()
+    y = torch.empty_like(x2)
+    rows = x2.shape[0]
+    nat.check(nat.load().cc2_rmsnorm_rows(_code(x.dtype), x2.data_ptr(), D, w.data_ptr(), y.data_ptr(), D, rows, D,
+                                          rows, 0, 0, float(eps), _stream(x)), "cc2_rmsnorm_rows")
+    return y.reshape(shape)
+
+
+def row_sumsq_parts(x: torch.Tensor) -> torch.Tensor:
+    """(G, M) fp32 partial sums of squares over 64-column groups of x (M, K):
+    the layout the SSQ epilogue writes and the ROWSCALE epilogue reads."""
+    M, Kd = x.shape
+    G = (Kd + 63) // 64
+    xp = torch.nn.functional.pad(x.float(), (0, G * 64 - Kd))
+    return xp.reshape(M, G, 64).pow(2).sum(-1).T.contiguous()
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *, relu: bool = False,
+           residual: torch.Tensor | None = None, row_ssq: torch.Tensor | None = None, norm_dim: int = 0,
+           eps: float = 1e-6, ssq_out: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = epilogue(x @ weight^T): optional row scale
+    rsqrt(row_ssq.sum(0) / norm_dim + eps) with ``row_ssq`` (G, M) partial sums
+    per 64-column group, + bias (fp32), ReLU, + residual, and ``ssq_out``
+    (G', M) <- partial sums of squares of the stored output."""
+    _cuda(x, weight, bias, residual, row_ssq, ssq_out)
+    K = x.shape[-1]
+    x2 = x.reshape(-1, K).contiguous()
+    M, N = x2.shape[0], weight.shape[0]
+    w = weight.contiguous()
+    if out is None:
+        out = torch.empty(M, N, dtype=x.dtype, device=x.device)
+    e = nat.Epilogue()
+    flags = 0
+    keep = []
+    if row_ssq is not None:
+        flags |= nat.EPI_ROWSCALE
+        r = row_ssq.float().contiguous()
+        keep.append(r)
+        e.ssq_in, e.norm_dim, e.eps = r.data_ptr(), norm_dim, eps
+        e.ssq_ld = r.shape[-1]
+    if bias is not None:
+        flags |= nat.EPI_BIAS
+        b = bias.float().contiguous()
+        keep.append(b)
+        e.bias = b.data_ptr()
+    if relu:
+        flags |= nat.EPI_RELU
+    if residual is not None:
+        flags |= nat.EPI_RESID
+        rr = residual.reshape(M, N).contiguous()
+        keep.append(rr)
+        e.resid, e.ld_resid = rr.data_ptr(), N
+    if ssq_out is not None:
+        flags |= nat.EPI_SSQ
+        e.ssq_out = ssq_out.data_ptr()
+        e.ssq_ld = ssq_out.shape[-1]
+    e.flags = flags
+    nat.check(nat.load().cc2_gemm(_code(x.dtype), x2.data_ptr(), K, w.data_ptr(), K, out.data_ptr(), N, M, N, K,
+                                  C.byref(e), _stream(x)), "cc2_gemm")
+    return out.reshape(*x.shape[:-1], N)
+
+
+_ROPE_CACHE: dict = {}
+
+
+def rope_table(S: int, d_kv: int = 64, theta: float = 10000.0, device=None) -> torch.Tensor:
+    """(S, d_kv/2, 2) fp32 (cos, sin) of inv_freq * pos, computed like the
+    engine's table (fp32 angle, accurate cos/sin)."""
+    key = (S, d_kv, theta, str(device))
+    if key not in _ROPE_CACHE:
+        inv = 1.0 / (theta ** (torch.arange(0, d_kv, 2, dtype=torch.int64).float() / d_kv))
+        ang = (torch.arange(S, dtype=torch.float32)[:, None] * inv[None, :]).double()
+        tab = torch.stack([ang.cos(), ang.sin()], dim=-1).float()
+        _ROPE_CACHE[key] = tab.to(device)
+    return _ROPE_CACHE[key]
+
+
+def unscaled_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor | None = None, *,
+                       rope: bool = False, rope_theta: float = 10000.0) -> torch.Tensor:
+    """softmax(q k^T + mask) v with no 1/sqrt(d) factor; q,k,v (B,H,S,64).
+    ``mask``: additive (B,1,1,S) float mask (finfo.min = masked) or (B,S)
+    bool key mask.  ``rope=True`` rotates q and k at positions 0..S-1 first."""
+    _cuda(q, k, v, mask)
+    B, H, S, D = q.shape
+    dev = q.device
+    packed = torch.cat([t.transpose(1, 2).reshape(B, S, H * D) for t in (q, k, v)], dim=-1).reshape(B * S, 3 * H * D)
+    packed = packed.contiguous()
+    if mask is None:
+        tok = torch.ones(B * S, dtype=torch.uint8, device=dev)
+    elif mask.dtype == torch.bool:
+        tok = mask.reshape(B * S).to(torch.uint8).contiguous()
+    else:
+        m = mask.reshape(B, -1)[:, -S:] if mask.numel() == B * S else mask.reshape(B, S)
+        tok = (m > torch.finfo(m.dtype).min / 2).reshape(B * S).to(torch.uint8).contiguous()
+    out = torch.empty(B * S, H * D, dtype=q.dtype, device=dev)
+    cs = rope_table(S, D, rope_theta, dev) if rope else None
+    nat.check(nat.load().cc2_attention(_code(q.dtype), 0, packed.data_ptr(), 3 * H * D, 0, H * D, 2 * H * D,
+                                       out.data_ptr(), H * D, tok.data_ptr(), B, S, H, D, None, None, 0, 0,
+                                       cs.data_ptr() if cs is not None else None, _stream(q)), "cc2_attention")
+    return out.reshape(B, S, H, D).transpose(1, 2)
+
+
+def group_attention(qkv: torch.Tensor, token_mask: torch.Tensor, group_ids: torch.Tensor, num_heads: int,
+                    ) -> torch.Tensor:
+    """Group self-attention core over token rows: qkv (B, S, 3*H*64) packed
+    [Q|K|V], token_mask (B, S) bool, group_ids (B,) -> (B, S, H*64)."""
+    _cuda(qkv, token_mask)
+    B, S, W = qkv.shape
+    HD = W // 3
+    lib = nat.load()
+    g = torch.as_tensor(group_ids).to("cpu", torch.int64).contiguous()
+    mem = (C.c_int32 * B)()
+    off = (C.c_int32 * (B + 1))()
+    ng, mg = C.c_int(), C.c_int()
+    nat.check(lib.cc2_group_layout(g.data_ptr(), B, mem, off, C.byref(ng), C.byref(mg)), "cc2_group_layout")
+    dev = qkv.device
+    mem_t = torch.tensor(list(mem), dtype=torch.int32).to(dev)
+    off_t = torch.tensor(list(off)[: ng.value + 1], dtype=torch.int32).to(dev)
+    x = qkv.reshape(B * S, W).contiguous()
+    tok = token_mask.reshape(B * S).to(torch.uint8).contiguous()
+    out = torch.empty(B * S, HD, dtype=qkv.dtype, device=dev)
+    nat.check(lib.cc2_attention(_code(qkv.dtype), 1, x.data_ptr(), W, 0, HD, 2 * HD, out.data_ptr(), HD,
+                                tok.data_ptr(), S * ng.value, S, num_heads, HD // num_heads, mem_t.data_ptr(),
+                                off_t.data_ptr(), ng.value, mg.value, None, _stream(qkv)), "cc2_attention")
+    return out.reshape(B, S, HD)

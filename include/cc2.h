@@ -1,0 +1,231 @@
+/*
+ * cc2.h -- C ABI of the B200 (sm_100a) CuteChronos2 encoder engine.
+ *
+ * Every entry point takes plain pointers, sizes and a CUDA stream (as void*),
+ * returns 0 on success or a negative CC2_E* code, and never allocates device
+ * memory: the caller owns every buffer (weights pack, workspace, outputs).
+ * On error, cc2_last_error() returns a message for the calling thread.
+ * Device pointers are marked (dev), host pointers (host).
+ *
+ * Element types: CC2_F32 (float) or CC2_BF16 (bfloat16, fp32 accumulate).
+ * "dtype" buffers hold elements of the model dtype.
+ *
+ * Reference interfaces these replace (paths inside lee101/cutedsl):
+ *   cc2_preprocess        <- cutechronos/cpp/preprocessing.cpp:99-120 (pybind
+ *                            fused_preprocess) and model.py:473-549
+ *   cc2_output_transform  <- cutechronos/triton_kernels/fused_output.py:83-140
+ *                            and model.py:816-829
+ *   cc2_gemm              <- F.linear call sites model.py:178-181, 227-229,
+ *                            271, 301-303, 308, 328-329; fused RMSNorm+QKV
+ *                            kernel_backends.py:168-176; fused MLP
+ *                            triton_kernels/fused_mlp.py:254-300
+ *   cc2_rmsnorm_rows      <- kernel_backends.py:85-110 (rms_layernorm)
+ *   cc2_attention         <- kernel_backends.py:113-153 (unscaled_attention)
+ *                            + rope.py:126-180 (apply_rope) for time attention;
+ *                            model.py:131-142 via model.py:305 for group attention
+ *   cc2_model_* /
+ *   cc2_forward           <- CuteChronos2Model.forward, model.py:738-831
+ *                            (weights in the layout of load_chronos2_weights,
+ *                            model.py:833-900)
+ */
+#ifndef CC2_H
+#define CC2_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define CC2_API __attribute__((visibility("default")))
+#else
+#define CC2_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { CC2_F32 = 0, CC2_BF16 = 1 };
+
+enum {
+  CC2_OK = 0,
+  CC2_E_INVALID = -1,     /* bad argument (shape, null pointer, alignment) */
+  CC2_E_CUDA = -2,        /* a CUDA runtime/driver call failed */
+  CC2_E_UNSUPPORTED = -3, /* configuration not supported by this build */
+  CC2_E_WORKSPACE = -4,   /* workspace or pack buffer too small */
+  CC2_E_DEVICE = -5       /* a kernel reported a device-side error (timeout) */
+};
+
+/* Message for the last failing call on this thread (empty if none). */
+CC2_API const char* cc2_last_error(void);
+/* Library version string. */
+CC2_API const char* cc2_version(void);
+/* Device-side error word written by bounded waits inside kernels (0 = none);
+ * synchronises the current device.  clear != 0 resets it. */
+CC2_API int cc2_device_status(int clear);
+
+/* ------------------------------------------------------------------------ */
+/* Model configuration: mirror of CuteChronos2Config (model.py:59-91).       */
+/* ------------------------------------------------------------------------ */
+typedef struct {
+  int d_model, d_kv, d_ff, num_layers, num_heads;
+  float layer_norm_epsilon;
+  float rope_theta;
+  int reg_token_id;
+  int context_length;        /* longer contexts keep their last context_length values */
+  int input_patch_size;      /* must equal output_patch_size and input_patch_stride */
+  int output_patch_size;
+  int num_quantiles;
+  int use_reg_token;
+  int use_arcsinh;
+  float time_encoding_scale;
+  int max_output_patches;    /* largest N a forward may ask for (sizes the RoPE table) */
+} cc2_config;
+
+/* Weights in the reference layout (nn.Linear: out x in, row-major), device
+ * pointers of the model dtype.  Per-layer fields point to HOST arrays of
+ * num_layers device pointers.  Names follow model.py:833-900. */
+typedef struct {
+  const void* shared;                 /* (vocab, d) embedding */
+  const void* in_hidden_w;  const void* in_hidden_b;   /* (d_ff, 3*ps), (d_ff) */
+  const void* in_output_w;  const void* in_output_b;   /* (d, d_ff), (d) */
+  const void* in_residual_w; const void* in_residual_b; /* (d, 3*ps), (d) */
+  const void* const* time_ln;  const void* const* time_q;  const void* const* time_k;
+  const void* const* time_v;   const void* const* time_o;
+  const void* const* group_ln; const void* const* group_q; const void* const* group_k;
+  const void* const* group_v;  const void* const* group_o;
+  const void* const* ff_ln;    const void* const* ff_wi;   const void* const* ff_wo;
+  const void* final_ln;                                 /* (d) */
+  const void* out_hidden_w;  const void* out_hidden_b;  /* (d_ff, d), (d_ff) */
+  const void* out_output_w;  const void* out_output_b;  /* (Q*ps, d_ff), (Q*ps) */
+  const void* out_residual_w; const void* out_residual_b; /* (Q*ps, d), (Q*ps) */
+} cc2_weights;
+
+typedef struct cc2_model cc2_model;
+
+/* Bytes of the device buffer that holds the packed (RMS-folded, fused)
+ * weights of a model. */
+CC2_API int cc2_model_pack_bytes(const cc2_config* cfg, int dtype, size_t* bytes);
+/* Packs `w` into `pack_buf` (dev, >= cc2_model_pack_bytes, 256-byte aligned)
+ * on `stream` and returns a handle that references pack_buf (not `w`).
+ * The caller keeps pack_buf alive until cc2_model_destroy. */
+CC2_API int cc2_model_create(const cc2_config* cfg, int dtype, const cc2_weights* w,
+                     void* pack_buf, size_t pack_bytes, void* stream, cc2_model** out);
+CC2_API int cc2_model_destroy(cc2_model* m);
+
+/* Group layout helper (host): turns per-series group ids into the member
+ * list / offsets cc2_forward uses.  members_out (B) and offsets_out (B+1)
+ * are host arrays; *num_groups and *max_group are written.  Series keep
+ * their order inside a group; groups are ordered by first appearance. */
+CC2_API int cc2_group_layout(const int64_t* group_ids, int B, int32_t* members_out,
+                     int32_t* offsets_out, int* num_groups, int* max_group);
+
+/* Workspace bytes for one forward of B series of length L with N output
+ * patches; max_group is the largest group size (1 = every series alone). */
+CC2_API int cc2_forward_workspace_bytes(const cc2_model* m, int B, int L, int N, int max_group,
+                                size_t* bytes);
+
+/* CuteChronos2Model.forward (model.py:738-831).
+ *   context      (dev) float32 (B, L), NaN = missing
+ *   context_mask (dev) float32 (B, L) or NULL (NULL: mask = !isnan(context))
+ *   group_ids    (host) int64 (B) or NULL (NULL: each series its own group)
+ *   out          (dev) dtype (B, num_quantiles, N*output_patch_size)
+ *   loc, scale   (dev) float32 (B) or NULL: the instance-norm statistics
+ *   workspace    (dev) >= cc2_forward_workspace_bytes, 256-byte aligned
+ * With group_ids == NULL the call issues only asynchronous work on `stream`
+ * and may be captured into a CUDA graph. */
+CC2_API int cc2_forward(const cc2_model* m, const float* context, const float* context_mask,
+                int B, int L, int N, const int64_t* group_ids, void* out, float* loc,
+                float* scale, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Launch profiling.  Between cc2_profile_begin and cc2_profile_read, every
+ * kernel that cc2_forward launches on the calling thread is bracketed by a
+ * pair of CUDA events (at most `capacity` launches are recorded).
+ * cc2_profile_read synchronises those events, writes per launch its kind
+ * (CC2_K_*), device time (ms), algorithmic FLOPs and algorithmic HBM bytes,
+ * stores the number of launches in *count and stops profiling. */
+enum {
+  CC2_K_PREPROCESS = 1, CC2_K_GEMM = 2, CC2_K_ATTN_TIME = 3, CC2_K_ATTN_GROUP = 4,
+  CC2_K_RMSNORM = 5, CC2_K_OUTPUT = 6
+};
+CC2_API int cc2_profile_begin(int capacity);
+CC2_API int cc2_profile_read(int* kinds, float* ms, double* flops, double* bytes, int capacity,
+                             int* count);
+
+/* ------------------------------------------------------------------------ */
+/* Component kernels (each is one stage of cc2_forward).                     */
+/* ------------------------------------------------------------------------ */
+
+/* Fused preprocessing (model.py:473-519 + 521-549): NaN-aware instance norm,
+ * arcsinh, left-pad + 16-wide patching, time encoding.  Writes, for each
+ * series b, S = P + use_reg + N token rows at row b*S of `patched`
+ * (row pitch ld_patched elements, dtype): the first 3*ps columns hold
+ * [time_enc | value | mask] for the P context patches, zeros for the REG
+ * row, and [future time_enc | 0 | 0] for the N future rows; columns
+ * [3*ps, pad_cols) are zeroed.  token_mask (dev, uint8, B*S): 1 = attendable.
+ * attn_mask (dev, float32 (B,P)) may be NULL.  loc/scale (dev, float32 B). */
+CC2_API int cc2_preprocess(const float* context, const float* context_mask, int B, int L,
+                   int patch_size, int context_length, float time_encoding_scale,
+                   int use_arcsinh, int use_reg, int N, int dtype, void* patched,
+                   int ld_patched, int pad_cols, uint8_t* token_mask, float* attn_mask,
+                   float* loc, float* scale, void* stream);
+
+/* Epilogue flags for cc2_gemm. */
+enum {
+  CC2_EPI_ROWSCALE = 1,  /* acc *= rsqrt(sum_g ssq_in[g*ssq_ld + row] / norm_dim + eps),
+                            g < ceil(norm_dim / 64)                           */
+  CC2_EPI_BIAS = 2,      /* acc += bias[col] (float32)                         */
+  CC2_EPI_RELU = 4,      /* acc = max(acc, 0)                                  */
+  CC2_EPI_RESID = 8,     /* out = resid[row, col] + acc (resid may == out)     */
+  CC2_EPI_SSQ = 16,      /* ssq_out[g*ssq_ld + row] = sum over the 64 columns
+                            64g..64g+63 of out[row, col]^2 (partial sums per
+                            64-column group: deterministic, no atomics)        */
+  CC2_EPI_SPECIAL = 32   /* rows with row % period == offset get special[]     */
+};
+
+typedef struct {
+  int flags;
+  const float* ssq_in; int norm_dim; float eps;
+  const float* bias;
+  const void* resid; int ld_resid;
+  float* ssq_out;
+  int ssq_ld;            /* row stride between 64-column groups of ssq_in / ssq_out */
+  const float* special; int special_period; int special_offset;
+} cc2_epilogue;
+
+/* out[M, N] = epilogue(A[M, K] @ W[N, K]^T); A, W, out, resid of `dtype`,
+ * row-major with the given row pitches (elements).  bf16 runs on tcgen05
+ * tensor cores (TMEM accumulators, TMA-fed); f32 runs on CUDA cores. */
+CC2_API int cc2_gemm(int dtype, const void* A, int lda, const void* W, int ldw, void* out, int ldo,
+             int M, int N, int K, const cc2_epilogue* epi, void* stream);
+
+/* y[r] = w * round(x[src_row(r)] * rsqrt(mean(x^2) + eps)) for r < rows, where
+ * src_row(r) = (r / per) * stride + offset + r % per; y row pitch ld_y.
+ * (T5 RMSNorm of the reference, applied to a strided subset of rows.) */
+CC2_API int cc2_rmsnorm_rows(int dtype, const void* x, int ld_x, const void* w, void* y, int ld_y,
+                     int rows, int dim, int per, int stride, int offset, float eps, void* stream);
+
+/* Unscaled attention (no 1/sqrt(d)) over sets of token rows.
+ *   mode 0 (time):  set b = rows b*S .. b*S+S-1, RoPE at positions 0..S-1
+ *                   (rope_cs: float2 (cos, sin) table, [pos][d_kv/2]; NULL
+ *                   = no RoPE).
+ *   mode 1 (group): set (t, g) = rows members[offsets[g]+i]*S + t, no RoPE.
+ * qkv rows hold Q at q_col, K at k_col, V at v_col (head h at +h*d_kv);
+ * keys whose token_mask is 0 are masked; out gets head h at h*d_kv. */
+CC2_API int cc2_attention(int dtype, int mode, const void* qkv, int ld_qkv, int q_col, int k_col,
+                  int v_col, void* out, int ld_out, const uint8_t* token_mask, int num_sets,
+                  int S, int num_heads, int d_kv, const int32_t* members,
+                  const int32_t* offsets, int num_groups, int max_group,
+                  const float* rope_cs, void* stream);
+
+/* Rearrange b n (q p) -> b q (n p), sinh (if use_arcsinh), * scale + loc
+ * (model.py:816-829).  preds (B*N, Q*ps) dtype with row pitch ld_preds;
+ * out (B, Q, N*ps) dtype. */
+CC2_API int cc2_output_transform(int dtype, const void* preds, int ld_preds, const float* loc,
+                         const float* scale, void* out, int B, int N, int Q, int ps,
+                         int use_arcsinh, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CC2_H */

@@ -1,0 +1,238 @@
+"""Component kernels on the GPU (through the C ABI) against the CPU oracle /
+fp32 torch references.  Mirrors the reference's kernel tests
+(cutechronos/tests/test_preprocessing.py, test_output.py,
+test_rms_layernorm.py, test_fused_mlp.py, test_attention.py,
+test_group_attention.py)."""
+
+import math
+
+import pytest
+import torch
+
+from conftest import case_inputs, oracle_config
+from oracle import chronos2_oracle as orc
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def K():
+    from cutechronos_b200 import kernels
+    return kernels
+
+
+def _ctx(B, L, nan_frac, seed, scale=1.0, offset=0.0):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.cumsum(torch.randn(B, L, generator=g), -1) * scale + offset
+    x[torch.rand(B, L, generator=g) < nan_frac] = float("nan")
+    return x
+
+
+# ---------------------------------------------------------------------------
+# preprocessing (instance norm + arcsinh + patching + time encoding)
+# ---------------------------------------------------------------------------
+PRE_CASES = [
+    ("basic", _ctx(4, 512, 0.1, 1), 512),
+    ("pad_500", _ctx(3, 500, 0.05, 2), 512),          # L not a multiple of 16
+    ("truncate", _ctx(2, 1024, 0.0, 3), 512),          # L > context_length
+    ("scale_1e6", _ctx(2, 256, 0.1, 4, 1e3, 1e6), 512),
+    ("nan_90", _ctx(3, 128, 0.9, 5), 512),
+    ("long_8192", _ctx(2, 8192, 0.02, 6), 8192),
+]
+
+
+def _edge_ctx():
+    x = _ctx(5, 64, 0.0, 7)
+    x[0] = float("nan")      # all-NaN -> loc 0, scale 1
+    x[1] = 2.5               # constant -> scale 1e-5
+    x[2, :40] = float("nan")  # left-padded
+    x[3, 17] = float("nan")
+    return x
+
+
+@pytest.mark.parametrize("name,ctx,cl", PRE_CASES + [("edge", _edge_ctx(), 512)])
+@pytest.mark.parametrize("arcsinh", [True, False])
+def test_preprocess_f32(name, ctx, cl, arcsinh):
+    cfg = orc.OracleConfig(context_length=cl, use_arcsinh=arcsinh)
+    pc, attn, loc, scale = orc.prepare_patched_context(cfg, ctx, None, torch.float32)
+    gpc, gattn, gloc, gscale = K().fused_preprocess(ctx.to(DEV), 16, cl, arcsinh)
+    gpc = gpc.cpu()
+    assert gpc.shape == pc.shape
+    assert torch.equal(gattn.cpu().bool(), attn)                      # bit-exact patch mask
+    assert torch.equal(gpc[..., 32:], pc[..., 32:])                    # bit-exact observed mask
+    assert torch.equal(gpc[..., :16], pc[..., :16])                    # bit-exact time encoding
+    assert torch.equal(torch.isnan(gpc), torch.isnan(pc))
+    assert torch.allclose(gloc.cpu(), loc, rtol=2e-7, atol=0)
+    assert torch.allclose(gscale.cpu(), scale, rtol=2e-6, atol=0)
+    assert torch.allclose(torch.nan_to_num(gpc[..., 16:32]), torch.nan_to_num(pc[..., 16:32]), rtol=0, atol=2e-6)
+
+
+def test_preprocess_bf16_and_explicit_mask(golden_small):
+    c = golden_small["explicit_mask"]
+    ctx, mask, _, _ = case_inputs(c)
+    cfg = oracle_config()
+    pc, attn, _, _ = orc.prepare_patched_context(cfg, ctx, mask, torch.bfloat16)
+    gpc, gattn, _, _ = K().fused_preprocess(ctx.to(DEV), 16, 512, True, context_mask=mask.to(DEV), dtype=torch.bfloat16)
+    assert torch.equal(gattn.cpu().bool(), attn)
+    assert torch.equal(gpc.cpu()[..., :16], pc[..., :16])
+    assert torch.equal(gpc.cpu()[..., 32:], pc[..., 32:])
+    d = (gpc.cpu()[..., 16:32].float() - pc[..., 16:32].float()).abs()
+    assert d.max().item() <= 2 ** -7 * max(1.0, pc[..., 16:32].float().abs().max().item())
+
+
+def test_preprocess_patch_size_1():
+    ctx = _ctx(2, 40, 0.2, 8)
+    cfg = orc.OracleConfig(context_length=512, input_patch_size=1, output_patch_size=1)
+    pc, attn, loc, scale = orc.prepare_patched_context(cfg, ctx, None, torch.float32)
+    gpc, gattn, _, _ = K().fused_preprocess(ctx.to(DEV), 1, 512, True)
+    assert torch.equal(gattn.cpu().bool(), attn)
+    assert torch.allclose(torch.nan_to_num(gpc.cpu()), torch.nan_to_num(pc), atol=2e-6, rtol=0)
+
+
+# ---------------------------------------------------------------------------
+# output transform / RMSNorm
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B,N", [(1, 1), (3, 4), (64, 8)])
+def test_output_transform(dtype, B, N):
+    g = torch.Generator().manual_seed(B * 10 + N)
+    x = (torch.randn(B, N, 21 * 16, generator=g) * 2).to(dtype)
+    loc, scale = torch.randn(B, 1, generator=g) * 100, torch.rand(B, 1, generator=g) * 10 + 0.1
+    ref = orc.output_transform(x, loc, scale, 21, 16)
+    out = K().fused_output_transform(x.to(DEV), loc.to(DEV), scale.to(DEV), 21, 16).cpu()
+    assert out.shape == (B, 21, N * 16) and out.dtype == dtype
+    tol = 1e-5 if dtype == torch.float32 else 2 ** -7
+    assert ((out.float() - ref.float()).abs() <= tol * ref.float().abs() + 1e-5 * scale.max()).all()
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(1, 34, 768), (4, 130, 768), (16, 514, 768)])
+def test_rms_layernorm(dtype, shape):
+    g = torch.Generator().manual_seed(sum(shape))
+    x = torch.randn(*shape, generator=g).to(dtype)
+    w = (torch.rand(shape[-1], generator=g) + 0.5).to(dtype)
+    ref = orc.rms_norm(x, w, 1e-6).float()
+    out = K().rms_layernorm(x.to(DEV), w.to(DEV), 1e-6).cpu().float()
+    tol = 1e-5 if dtype == torch.float32 else 1e-2
+    assert (out - ref).abs().max().item() <= tol * ref.abs().max().item()
+
+
+# ---------------------------------------------------------------------------
+# GEMM with fused epilogues (tcgen05 for bf16, FFMA for fp32)
+# ---------------------------------------------------------------------------
+GEMM_SHAPES = [(1, 16, 64), (37, 768, 768), (128, 2304, 768), (300, 336, 3840), (1000, 3072, 48),
+               (4257, 768, 3072), (133, 768, 3136), (2048, 256, 128)]
+
+
+def _gemm_ref(x, w, bias, relu, resid, ssq, dim, eps):
+    acc = x.double() @ w.double().T
+    if ssq is not None:
+        acc = acc * torch.rsqrt(ssq.double() / dim + eps)[:, None]
+    if bias is not None:
+        acc = acc + bias.double()
+    if relu:
+        acc = acc.clamp_min(0)
+    if resid is not None:
+        acc = acc + resid.double()
+    return acc
+
+
+@pytest.mark.parametrize("M,N,Kd", GEMM_SHAPES)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_linear_plain(M, N, Kd, dtype):
+    g = torch.Generator().manual_seed(M + N + Kd)
+    x = torch.randn(M, Kd, generator=g).to(dtype)
+    w = (torch.randn(N, Kd, generator=g) / math.sqrt(Kd)).to(dtype)
+    out = K().linear(x.to(DEV), w.to(DEV)).cpu().double()
+    ref = _gemm_ref(x, w, None, False, None, None, 0, 0)
+    tol = 1e-5 if dtype == torch.float32 else 8e-3
+    assert (out - ref).abs().max().item() <= tol * max(1.0, ref.abs().max().item())
+
+
+@pytest.mark.parametrize("M,N,Kd", [(37, 768, 768), (1000, 2304, 768), (257, 3072, 768), (4257, 768, 3072)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_linear_fused_epilogues(M, N, Kd, dtype):
+    g = torch.Generator().manual_seed(7 * M + N)
+    x = torch.randn(M, Kd, generator=g).to(dtype)
+    w = (torch.randn(N, Kd, generator=g) / math.sqrt(Kd)).to(dtype)
+    bias = torch.randn(N, generator=g)
+    resid = torch.randn(M, N, generator=g).to(dtype)
+    ssq = x.float().pow(2).sum(-1)
+    kk = K()
+    parts = kk.row_sumsq_parts(x)
+    # row scale + bias + relu
+    o1 = kk.linear(x.to(DEV), w.to(DEV), bias.to(DEV), relu=True, row_ssq=parts.to(DEV), norm_dim=Kd, eps=1e-6)
+    r1 = _gemm_ref(x, w, bias, True, None, ssq, Kd, 1e-6)
+    tol = 1e-5 if dtype == torch.float32 else 8e-3
+    assert (o1.cpu().double() - r1).abs().max().item() <= tol * max(1.0, r1.abs().max().item())
+    # residual (in place) + sum of squares of the stored result
+    out = resid.to(DEV).clone()
+    so = torch.full(((N + 63) // 64, M), float("nan"), device=DEV)
+    kk.linear(x.to(DEV), w.to(DEV), residual=out, ssq_out=so, out=out)
+    r2 = _gemm_ref(x, w, None, False, resid, None, 0, 0)
+    assert (out.cpu().double() - r2).abs().max().item() <= tol * max(1.0, r2.abs().max().item())
+    assert torch.allclose(so.cpu(), kk.row_sumsq_parts(out.cpu()), rtol=1e-4, atol=1e-3)
+
+
+# ---------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------
+def _rope_ref(q, k, S):
+    cos, sin = orc.rope_cos_sin(orc.OracleConfig(), S, torch.float32)
+    c, s = cos.unsqueeze(1), sin.unsqueeze(1)
+    return q * c + orc._rotate_half(q) * s, k * c + orc._rotate_half(k) * s
+
+
+@pytest.mark.parametrize("B,S", [(1, 37), (4, 133), (2, 521), (3, 64)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("rope", [True, False])
+def test_time_attention(B, S, dtype, rope):
+    g = torch.Generator().manual_seed(B * 1000 + S)
+    H = 12
+    q, k, v = (torch.randn(B, H, S, 64, generator=g) * 0.5 for _ in range(3))
+    q, k, v = q.to(dtype), k.to(dtype), v.to(dtype)
+    valid = torch.rand(B, S, generator=g) > 0.3
+    valid[:, -1] = True
+    qf, kf = q.float(), k.float()
+    if rope:
+        qf, kf = _rope_ref(qf, kf, S)
+    mask = (1.0 - valid.float())[:, None, None, :] * torch.finfo(torch.float32).min
+    ref = orc.unscaled_attention(qf, kf, v.float(), mask)
+    out = K().unscaled_attention(q.to(DEV), k.to(DEV), v.to(DEV), valid.to(DEV), rope=rope).cpu().float()
+    tol = 2e-5 if dtype == torch.float32 else 2e-2
+    assert (out - ref).abs().max().item() <= tol * max(1.0, ref.abs().max().item())
+
+
+def test_attention_uniform_known_answer():
+    # identical keys -> uniform weights -> output = mean of V (reference test_attention.py:199-213)
+    B, H, S = 2, 12, 70
+    q = torch.randn(B, H, S, 64)
+    k = torch.ones(B, H, S, 64)
+    v = torch.randn(B, H, S, 64)
+    out = K().unscaled_attention(q.to(DEV), k.to(DEV), v.to(DEV)).cpu()
+    assert torch.allclose(out, v.mean(dim=2, keepdim=True).expand_as(v), atol=1e-5)
+
+
+@pytest.mark.parametrize("gids,S", [([0, 0, 1, 1, 1, 2, 3, 3], 19), ([5] * 40 + [1] * 3, 9), (list(range(6)), 7),
+                                    ([0] * 100, 5)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_group_attention(gids, S, dtype):
+    B, H = len(gids), 12
+    g = torch.Generator().manual_seed(B + S)
+    qkv = (torch.randn(B, S, 3 * 768, generator=g) * 0.5).to(dtype)
+    tok = torch.rand(B, S, generator=g) > 0.2
+    gid = torch.tensor(gids)
+    # oracle: (T, H, B, D) attention with the group-time mask (model.py:561-569)
+    q, k, v = (qkv.float()[..., i * 768:(i + 1) * 768].transpose(0, 1).reshape(S, B, H, 64).permute(0, 2, 1, 3)
+               for i in range(3))
+    same = (gid[:, None] == gid[None, :]).float()
+    gm = torch.einsum("qb,bt->qbt", same, tok.float()).permute(2, 0, 1).unsqueeze(1)
+    ref = orc.unscaled_attention(q, k, v, (1.0 - gm) * torch.finfo(torch.float32).min)
+    ref = ref.permute(0, 2, 1, 3).reshape(S, B, 768).transpose(0, 1)
+    out = K().group_attention(qkv.to(DEV), tok.to(DEV), gid, H).cpu().float()
+    # queries whose whole group is masked at that step are padding: compare the rest
+    live = (same @ tok.float()) > 0
+    tol = 2e-5 if dtype == torch.float32 else 2e-2
+    d = (out - ref).abs()[live]
+    assert d.max().item() <= tol * max(1.0, ref.abs().max().item())
+    assert torch.isfinite(out).all()

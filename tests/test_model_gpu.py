@@ -1,0 +1,173 @@
+"""Whole-forward parity on the GPU: CuteChronos2Model (native engine) against
+fixtures from the reference module and against the CPU oracle.
+
+Tolerances: fp32 mode max-abs 1e-4 in the model's
+normalised output space (|y - ref| / scale_b, scale_b = the series' instance
+norm scale; for the reference's own test inputs the scale is ~0.1 and the
+bound holds in absolute terms as well); bf16 mode 2e-2 relative:
+max|y - ref| <= 2e-2 * max|ref|.
+"""
+
+import pytest
+import torch
+
+from conftest import case_inputs, oracle_config, small_config
+from cutechronos_b200.model import CuteChronos2Config, CuteChronos2Model
+from cutechronos_b200.workloads import config1, config2, config3, seeded_init_, seeded_state_dict
+from oracle import chronos2_oracle as orc
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+CASES = ["ragged_nan", "groups_2x2", "truncate_700", "edge_rows", "explicit_mask", "large_scale_groups"]
+
+
+def _model(cfg, dtype):
+    return seeded_init_(CuteChronos2Model(cfg), seed=0).to(DEV, dtype).eval()
+
+
+def _norm_err(y, ref, scale):
+    return ((y.float() - ref.float()).abs() / scale.view(-1, 1, 1)).max().item()
+
+
+def _rel_err(y, ref):
+    return (y.float() - ref.float()).abs().max().item() / ref.float().abs().max().item()
+
+
+@pytest.fixture(scope="module")
+def small_f32():
+    return _model(small_config(), torch.float32)
+
+
+@pytest.fixture(scope="module")
+def small_bf16():
+    return _model(small_config(), torch.bfloat16)
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_small_f32_vs_reference(golden_small, small_f32, case):
+    c = golden_small[case]
+    ctx, mask, N, gid = case_inputs(c)
+    y = small_f32(ctx.to(DEV), mask.to(DEV) if mask is not None else None, N, gid).cpu()
+    ref = torch.from_numpy(c["out_f32"])
+    assert y.shape == ref.shape and y.dtype == torch.float32
+    scale = torch.from_numpy(c["scale"]).view(-1)
+    assert _norm_err(y, ref, scale) <= 1e-4
+
+
+@pytest.mark.parametrize("case", CASES)
+def test_small_bf16_vs_reference(golden_small, small_bf16, case):
+    c = golden_small[case]
+    ctx, mask, N, gid = case_inputs(c)
+    y = small_bf16(ctx.to(DEV), mask.to(DEV) if mask is not None else None, N, gid).cpu()
+    assert y.dtype == torch.bfloat16
+    assert _rel_err(y, torch.from_numpy(c["out_f32"])) <= 2e-2
+    assert _rel_err(y, torch.from_numpy(c["out_bf16"])) <= 2e-2
+
+
+@pytest.fixture(scope="module")
+def base_weights():
+    m = CuteChronos2Model(CuteChronos2Config())
+    return seeded_state_dict([(n, tuple(p.shape)) for n, p in m.named_parameters()], seed=0)
+
+
+@pytest.fixture(scope="module")
+def base_f32():
+    return _model(CuteChronos2Config(), torch.float32)
+
+
+@pytest.fixture(scope="module")
+def base_bf16():
+    return _model(CuteChronos2Config(), torch.bfloat16)
+
+
+def test_base_cfg0_f32(golden_base, base_f32):
+    ctx = torch.from_numpy(golden_base["context"])
+    y = base_f32(ctx.to(DEV), num_output_patches=int(golden_base["N"])).cpu()
+    ref = torch.from_numpy(golden_base["out_f32"])
+    _, _, _, scale = orc.prepare_patched_context(orc.OracleConfig(), ctx, None, torch.float32)
+    assert _norm_err(y, ref, scale.view(-1)) <= 1e-4
+
+
+def test_base_cfg0_reference_style_input_f32(base_f32, base_weights):
+    # the reference's own parity input (test_model.py:31-55): randn*0.1 + 100, absolute max-abs 1e-4
+    g = torch.Generator().manual_seed(42)
+    ctx = torch.randn(2, 512, generator=g) * 0.1 + 100.0
+    y = base_f32(ctx.to(DEV), num_output_patches=4).cpu()
+    ref = orc.forward(orc.OracleConfig(), base_weights, ctx, None, 4)
+    assert (y - ref).abs().max().item() <= 1e-4
+
+
+def test_base_cfg0_bf16(golden_base, base_bf16):
+    ctx = torch.from_numpy(golden_base["context"])
+    y = base_bf16(ctx.to(DEV), num_output_patches=int(golden_base["N"])).cpu()
+    assert _rel_err(y, torch.from_numpy(golden_base["out_f32"])) <= 2e-2
+
+
+def _subset_check(model, weights, ctx, gid, N, idx, dtype=torch.float32):
+    """Forecasts of a subset (whole groups) from the full-batch GPU run vs the
+    CPU oracle run on that subset alone."""
+    y = model(ctx.to(DEV), num_output_patches=N, group_ids=gid).cpu()
+    assert torch.isfinite(y.float()).all()
+    sub_gid = gid[idx] if gid is not None else None
+    ref = orc.forward(orc.OracleConfig(), weights, ctx[idx], None, N, sub_gid, torch.float32)
+    return _rel_err(y[idx], ref)
+
+
+def test_cfg1_full_batch_subset_vs_oracle(base_bf16, base_weights):
+    w = config1()
+    err = _subset_check(base_bf16, base_weights, w.context, None, w.num_output_patches, torch.tensor([0, 77, 255]))
+    assert err <= 2e-2
+
+
+def test_cfg2_groups_subset_vs_oracle(base_bf16, base_weights):
+    w = config2()
+    idx = torch.arange(8, 24)  # groups 1 and 2 (8 variates each)
+    err = _subset_check(base_bf16, base_weights, w.context, w.group_ids, w.num_output_patches, idx)
+    assert err <= 2e-2
+
+
+def test_cfg3_left_padded_subset_vs_oracle(base_bf16, base_weights):
+    w = config3()
+    padded = torch.isnan(w.context[:, 0]).nonzero().view(-1)
+    full = (~torch.isnan(w.context[:, 0])).nonzero().view(-1)
+    idx = torch.stack([padded[0], full[0]])
+    err = _subset_check(base_bf16, base_weights, w.context, None, w.num_output_patches, idx)
+    assert err <= 2e-2
+
+
+def test_batch_composition_invariance_and_determinism(base_bf16):
+    # a series' forecast does not depend on the other (independent) series in
+    # the batch, bit for bit: every reduction has a fixed order (no atomics)
+    w = config1(B=300, L=2048)
+    full = base_bf16(w.context.to(DEV), num_output_patches=4).cpu()
+    again = base_bf16(w.context.to(DEV), num_output_patches=4).cpu()
+    part = base_bf16(w.context[5:9].to(DEV), num_output_patches=4).cpu()
+    assert torch.equal(full, again)
+    assert torch.equal(part, full[5:9])
+
+
+def test_group_ids_none_equals_arange(small_bf16):
+    ctx = torch.randn(6, 100)
+    a = small_bf16(ctx.to(DEV), num_output_patches=2)
+    b = small_bf16(ctx.to(DEV), num_output_patches=2, group_ids=torch.arange(6))
+    assert torch.equal(a, b)
+
+
+def test_repack_after_weight_change(small_f32, golden_small):
+    c = golden_small["ragged_nan"]
+    ctx, mask, N, gid = case_inputs(c)
+    y0 = small_f32(ctx.to(DEV), num_output_patches=N).clone()
+    with torch.no_grad():
+        small_f32.blocks[0].feed_forward.wo.weight.mul_(2.0)
+    y1 = small_f32(ctx.to(DEV), num_output_patches=N)
+    with torch.no_grad():
+        small_f32.blocks[0].feed_forward.wo.weight.mul_(0.5)
+    y2 = small_f32(ctx.to(DEV), num_output_patches=N)
+    assert not torch.equal(y0, y1)
+    assert torch.allclose(y0, y2, atol=1e-6)
+
+
+def test_cpu_model_raises():
+    m = CuteChronos2Model(small_config())
+    with pytest.raises(RuntimeError, match="CUDA"):
+        m(torch.randn(1, 32))
