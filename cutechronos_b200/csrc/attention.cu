@@ -19,7 +19,11 @@
 // a forecast.
 //
 // Kernels:
-//   attn_mma_kernel   bf16, flash-style: 64 queries per CTA (16 per warp),
+//   attn_set_kernel   bf16, the default: one CTA per (head, set) with the
+//                     set's Q, K and V resident in shared memory (sets up to
+//                     ~590 keys); warps own 16-row query tiles; mma.sync
+//                     m16n8k16, fp32 online softmax.
+//   attn_mma_kernel   bf16, blocked flash kernel for larger sets: 64 queries per CTA (16 per warp),
 //                     64-key blocks, mma.sync m16n8k16 with fp32 accumulation,
 //                     online softmax in fp32 (exp2 domain), P re-used from
 //                     registers as the A operand of P.V.  S x S never leaves
@@ -254,6 +258,214 @@ attn_mma_kernel(const bf16* __restrict__ qkv, int ld, int qcol, int kcol, int vc
 }
 
 // ---------------------------------------------------------------------------
+// whole-set tensor-core kernel (bf16): one CTA per (head, set).  Q, K and V
+// of the whole set are staged in shared memory with one wave of async copies,
+// RoPE is applied there once, and each warp then owns 16-row query tiles and
+// streams over the keys with no block-level barrier.  Key n-tiles past the end
+// of the set are skipped, so a set of n keys costs ceil(n/8) score tiles per
+// query tile.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
+constexpr int kSetMaxWarps = 8;
+constexpr size_t kSetSmemLimit = 225 * 1024;  // larger sets use the blocked kernel
+
+// Q, K, V tiles live in shared memory as [row][64] bf16 with 128-byte rows;
+// 16-byte chunk c of row r is stored at chunk c ^ (r & 7), so ldmatrix on 8
+// consecutive rows touches 8 distinct bank groups.
+__device__ __forceinline__ uint32_t swz(uint32_t base, int r, int chunk) {
+  return base + (uint32_t)r * 128u + ((uint32_t)(chunk ^ (r & 7)) << 4);
+}
+
+inline size_t set_kernel_smem(int npad) { return (size_t)npad * (3 * 128 + sizeof(float)); }
+
+// RoPE (rotate half) on rows [0, n) of the swizzled Q and K tiles, position =
+// row index.  Each (row, i) entry of the cos/sin table is read once for both
+// tiles, and table loads are issued in batches of kRopeBatch per thread so
+// their latency overlaps.
+constexpr int kRopeBatch = 8;
+__device__ __forceinline__ void rope_qk_swz(uint8_t* Qt, uint8_t* Kt, int n, const float2* __restrict__ cs) {
+  const int total = n * (DH / 2);
+  for (int base = threadIdx.x; base < total; base += blockDim.x * kRopeBatch) {
+    float2 c[kRopeBatch];
+#pragma unroll
+    for (int j = 0; j < kRopeBatch; ++j) {
+      const int idx = base + j * blockDim.x;
+      c[j] = idx < total ? __ldg(cs + idx) : make_float2(1.0f, 0.0f);
+    }
+#pragma unroll
+    for (int j = 0; j < kRopeBatch; ++j) {
+      const int idx = base + j * blockDim.x;
+      if (idx < total) {
+        const int r = idx / (DH / 2), i = idx % (DH / 2);
+        const int o1 = r * 128 + (((i >> 3) ^ (r & 7)) << 4) + (i & 7) * 2;
+        const int o2 = r * 128 + ((((i >> 3) + 4) ^ (r & 7)) << 4) + (i & 7) * 2;
+#pragma unroll
+        for (int t = 0; t < 2; ++t) {
+          uint8_t* T = t ? Kt : Qt;
+          bf16* p1 = reinterpret_cast<bf16*>(T + o1);
+          bf16* p2 = reinterpret_cast<bf16*>(T + o2);
+          const float x1 = __bfloat162float(*p1), x2 = __bfloat162float(*p2);
+          *p1 = __float2bfloat16_rn(x1 * c[j].x - x2 * c[j].y);
+          *p2 = __float2bfloat16_rn(x2 * c[j].x + x1 * c[j].y);
+        }
+      }
+    }
+  }
+}
+
+template <bool ROPE>
+__global__ void __launch_bounds__(kSetMaxWarps * 32, 2)
+attn_set_kernel(const bf16* __restrict__ qkv, int ld, int qcol, int kcol, int vcol, bf16* __restrict__ out,
+                int ldo, const uint8_t* __restrict__ tok, const float2* __restrict__ rope, SetInfo si) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const SetGeom g = set_geom(si, blockIdx.y);
+  const int h = blockIdx.x;
+  const int n = g.n;
+  if (n <= 0) return;
+  const int npad = (n + 15) & ~15;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, nwarps = blockDim.x >> 5;
+  uint8_t* Qs = smem_raw;
+  uint8_t* Ks = Qs + npad * 128;
+  uint8_t* Vs = Ks + npad * 128;
+  float* kbias = reinterpret_cast<float*>(Vs + npad * 128);
+  const uint32_t qb = (uint32_t)__cvta_generic_to_shared(Qs);
+  const uint32_t kb = (uint32_t)__cvta_generic_to_shared(Ks);
+  const uint32_t vb = (uint32_t)__cvta_generic_to_shared(Vs);
+  const int hq = qcol + h * DH, hk = kcol + h * DH, hv = vcol + h * DH;
+
+  for (int idx = tid; idx < npad * 8; idx += blockDim.x) {
+    const int r = idx >> 3, c = idx & 7;
+    if (r < n) {
+      const bf16* src = qkv + (size_t)g.row(r, si.S) * ld + c * 8;
+      cp_async16(swz(qb, r, c), src + hq);
+      cp_async16(swz(kb, r, c), src + hk);
+      cp_async16(swz(vb, r, c), src + hv);
+    } else {
+      const uint4 z = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(Qs + (swz(qb, r, c) - qb)) = z;
+      *reinterpret_cast<uint4*>(Ks + (swz(kb, r, c) - kb)) = z;
+      *reinterpret_cast<uint4*>(Vs + (swz(vb, r, c) - vb)) = z;
+    }
+  }
+  for (int r = tid; r < npad; r += blockDim.x)
+    kbias[r] = r < n ? (tok[g.row(r, si.S)] ? 0.0f : kMaskedScore) : -INFINITY;
+  cp_async_wait_all();
+  __syncthreads();
+  if (ROPE) {
+    rope_qk_swz(Qs, Ks, n, rope);
+    __syncthreads();
+  }
+
+  for (int q0 = warp * 16; q0 < n; q0 += nwarps * 16) {
+    uint32_t qf[4][4];
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+      ldsm_x4(swz(qb, q0 + (lane & 15), 2 * ks + (lane >> 4)), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+
+    for (int k0 = 0; k0 < n; k0 += KT) {
+      const int kvalid = n - k0;
+      float s[8][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+        if (nt * 8 < kvalid) {
+          const int kr = k0 + nt * 8 + (lane & 7);
+#pragma unroll
+          for (int ks = 0; ks < 4; ks += 2) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(swz(kb, kr, 2 * ks + (lane >> 3)), b0, b1, b2, b3);
+            mma16816(s[nt], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], b0, b1);
+            mma16816(s[nt], qf[ks + 1][0], qf[ks + 1][1], qf[ks + 1][2], qf[ks + 1][3], b2, b3);
+          }
+        }
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int c = nt * 8 + 2 * (lane & 3);
+        const float b0 = c < kvalid ? kbias[k0 + c] : -INFINITY;
+        const float b1 = c + 1 < kvalid ? kbias[k0 + c + 1] : -INFINITY;
+        s[nt][0] = b0 == 0.0f ? s[nt][0] * kLog2e : b0;
+        s[nt][1] = b1 == 0.0f ? s[nt][1] * kLog2e : b1;
+        s[nt][2] = b0 == 0.0f ? s[nt][2] * kLog2e : b0;
+        s[nt][3] = b1 == 0.0f ? s[nt][3] * kLog2e : b1;
+        mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
+        mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
+      m0 = mn0; m1 = mn1;
+      l0 *= c0; l1 *= c1;
+#pragma unroll
+      for (int dt = 0; dt < 8; ++dt) { o[dt][0] *= c0; o[dt][1] *= c0; o[dt][2] *= c1; o[dt][3] *= c1; }
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        s[nt][0] = exp2f(s[nt][0] - mn0); s[nt][1] = exp2f(s[nt][1] - mn0);
+        s[nt][2] = exp2f(s[nt][2] - mn1); s[nt][3] = exp2f(s[nt][3] - mn1);
+        l0 += s[nt][0] + s[nt][1];
+        l1 += s[nt][2] + s[nt][3];
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (j * 16 < kvalid) {
+          const uint32_t a0 = pack2(s[2 * j][0], s[2 * j][1]);
+          const uint32_t a1 = pack2(s[2 * j][2], s[2 * j][3]);
+          const uint32_t a2 = pack2(s[2 * j + 1][0], s[2 * j + 1][1]);
+          const uint32_t a3 = pack2(s[2 * j + 1][2], s[2 * j + 1][3]);
+          const int vr = k0 + 16 * j + (lane & 15);
+#pragma unroll
+          for (int dt = 0; dt < 8; dt += 2) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(swz(vb, vr, dt + (lane >> 4)), b0, b1, b2, b3);
+            mma16816(o[dt], a0, a1, a2, a3, b0, b1);
+            mma16816(o[dt + 1], a0, a1, a2, a3, b2, b3);
+          }
+        }
+      }
+    }
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+    // stage the 16 x 64 output in this warp's own (already consumed) Q rows
+    __syncwarp();
+    const int r0 = q0 + (lane >> 2);
+#pragma unroll
+    for (int dt = 0; dt < 8; ++dt) {
+      const uint32_t off = 4u * (lane & 3);
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(swz(qb, r0, dt) + off), "r"(pack2(o[dt][0] * i0, o[dt][1] * i0)));
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(swz(qb, r0 + 8, dt) + off), "r"(pack2(o[dt][2] * i1, o[dt][3] * i1)));
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = q0 + (lane >> 3) + 4 * i, c = lane & 7;
+      if (rr < n) {
+        uint4 v;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "r"(swz(qb, rr, c)));
+        *reinterpret_cast<uint4*>(out + (size_t)g.row(rr, si.S) * ldo + h * DH + c * 8) = v;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // SIMT kernel (fp32 mode, small groups)
 // ---------------------------------------------------------------------------
 constexpr int SQ = 16;  // queries per CTA (4 per warp)
@@ -376,10 +588,33 @@ int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int
   if (dtype == CC2_BF16) {
     CC2_REQUIRE(ld % 8 == 0 && ldo % 8 == 0 && qcol % 8 == 0 && kcol % 8 == 0 && vcol % 8 == 0,
                 "attention(bf16): columns/pitches must be multiples of 8");
+    const int npad = (nmax + 15) & ~15;
+    const int nqt = (nmax + 15) / 16;
+    const int rounds = (nqt + kSetMaxWarps - 1) / kSetMaxWarps;
+    const int warps = (nqt + rounds - 1) / rounds;
+    const size_t smem = set_kernel_smem(npad);
     if (mode == 1 && max_group <= SK) {
       dim3 grid((nmax + SQ - 1) / SQ, heads, num_sets);
       attn_simt_kernel<bf16, false><<<grid, 128, 0, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out,
                                                           ldo, tok, cs, si);
+    } else if (smem <= kSetSmemLimit) {
+      static unsigned long long attr_done = 0;  // one bit per device
+      int dev = 0;
+      CC2_CUDA(cudaGetDevice(&dev));
+      if (dev >= 64 || !((attr_done >> dev) & 1ull)) {
+        CC2_CUDA(cudaFuncSetAttribute(attn_set_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)kSetSmemLimit));
+        CC2_CUDA(cudaFuncSetAttribute(attn_set_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)kSetSmemLimit));
+        if (dev < 64) attr_done |= 1ull << dev;
+      }
+      dim3 grid(heads, num_sets);
+      if (mode == 0 && cs)
+        attn_set_kernel<true><<<grid, warps * 32, smem, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out,
+                                                              ldo, tok, cs, si);
+      else
+        attn_set_kernel<false><<<grid, warps * 32, smem, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol,
+                                                               (bf16*)out, ldo, tok, cs, si);
     } else {
       dim3 grid((nmax + QT - 1) / QT, heads, num_sets);
       if (mode == 0 && cs)
