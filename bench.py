@@ -344,6 +344,64 @@ def run_b200(args):
     return result
 
 
+def run_micro(args):
+    """Per-kernel micro-benchmark at the configs[1] shapes (M = B * 133 token
+    rows): each GEMM of the forward with its fused epilogue and the time
+    attention, timed with CUDA events; cuBLAS on the same GEMM shapes is timed
+    beside them as a yardstick (it is not used by the engine)."""
+    from cutechronos_b200 import kernels as kk
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    M, d, dff = args.batch * 133, 768, 3072
+    g = torch.Generator(device=dev).manual_seed(0)
+
+    def rnd(*shape, scale=1.0):
+        return (torch.randn(*shape, generator=g, device=dev) * scale).to(torch.bfloat16)
+
+    x, h = rnd(M, d), rnd(M, dff)
+    wqkv, wo, wi, wf = rnd(3 * d, d, scale=0.03), rnd(d, d, scale=0.03), rnd(dff, d, scale=0.03), rnd(d, dff, scale=0.02)
+    big = rnd(8192, 8192)
+    ssq = kk.row_sumsq_parts(x.float()).to(dev)
+    so = torch.empty_like(ssq)
+    res = x.clone()
+    qkvr = rnd(M, 3 * d, scale=0.5)
+    tok = torch.ones(M, dtype=torch.uint8, device=dev)
+    att = torch.empty(M, d, dtype=torch.bfloat16, device=dev)
+    cases = {
+        "qkv  N=2304 K=768 rowscale": (lambda: kk.linear(x, wqkv, row_ssq=ssq, norm_dim=d), 2 * M * 3 * d * d),
+        "o    N=768  K=768 resid+ssq": (lambda: kk.linear(x, wo, residual=res, ssq_out=so, out=res), 2 * M * d * d),
+        "ffn1 N=3072 K=768 rowscale+relu": (lambda: kk.linear(x, wi, row_ssq=ssq, norm_dim=d, relu=True),
+                                            2 * M * dff * d),
+        "ffn2 N=768  K=3072 resid+ssq": (lambda: kk.linear(h, wf, residual=res, ssq_out=so, out=res), 2 * M * d * dff),
+        "gemm 8192^3 plain": (lambda: kk.linear(big, big), 2 * 8192 ** 3),
+        "attn time S=133 (rope)": (lambda: kk.attention_rows(qkvr, tok, args.batch, 133, 12, True, att),
+                                   4 * args.batch * 12 * 133 * 133 * 64),
+        "cublas qkv  N=2304 K=768": (lambda: torch.matmul(x, wqkv.T), 2 * M * 3 * d * d),
+        "cublas o    N=768  K=768": (lambda: torch.matmul(x, wo.T), 2 * M * d * d),
+        "cublas ffn1 N=3072 K=768": (lambda: torch.matmul(x, wi.T), 2 * M * dff * d),
+        "cublas ffn2 N=768  K=3072": (lambda: torch.matmul(h, wf.T), 2 * M * d * dff),
+        "cublas 8192^3": (lambda: torch.matmul(big, big), 2 * 8192 ** 3),
+    }
+    out = {}
+    for name, (fn, flops) in cases.items():
+        if args.only and args.only not in name:
+            continue
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for a, b in evs:
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+        out[name] = {"us": round(ms * 1e3, 2), "tflops": round(flops / (ms / 1e3) / 1e12, 1)}
+        log(f"{name:36s} {ms * 1e3:9.1f} us  {flops / (ms / 1e3) / 1e12:7.1f} TFLOP/s")
+    print(json.dumps({"micro": out, "M": M}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -353,10 +411,18 @@ def main():
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-latency", action="store_true")
+    ap.add_argument("--micro", action="store_true", help="per-kernel micro-benchmark instead of the step")
+    ap.add_argument("--only", default="", help="with --micro: run only cases whose name contains this")
+    ap.add_argument("--gemm-variant", type=int, default=0, help="0: 2-SM GEMM tiles, 1: 1-SM tiles only")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    if args.impl == "reference":
+    if args.gemm_variant:
+        from cutechronos_b200 import _native as nat
+        nat.load().cc2_set_gemm_variant(args.gemm_variant)
+    if args.micro:
+        run_micro(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_b200(args)

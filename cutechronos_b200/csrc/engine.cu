@@ -65,6 +65,7 @@ int launch_rmsnorm_rows(int, const void*, int, const void*, void*, int, int, int
                         cudaStream_t);
 int launch_gemm_tc(const void*, int, const void*, int, void*, int, int, int, int, const cc2_epilogue*,
                    cudaStream_t);
+extern int g_gemm_variant;
 int launch_gemm_f32(const void*, int, const void*, int, void*, int, int, int, int, const cc2_epilogue*,
                     cudaStream_t);
 int launch_attention(int, int, const void*, int, int, int, int, void*, int, const uint8_t*, int, int, int, int,
@@ -601,6 +602,12 @@ int cc2_preprocess(const float* context, const float* context_mask, int B, int L
   return launch_preprocess(context, context_mask, B, L, patch_size, context_length, te_scale, use_arcsinh, use_reg,
                            N, dtype, patched, ld_patched, pad_cols, token_mask, attn_mask, loc, scale,
                            (cudaStream_t)stream);
+}
+
+int cc2_set_gemm_variant(int variant) {
+  const int old = g_gemm_variant;
+  g_gemm_variant = variant ? 1 : 0;
+  return old;
 }
 
 int cc2_gemm(int dtype, const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,

@@ -11,7 +11,9 @@
 //   warps 2..5  epilogue: tcgen05.ld the accumulator (warp w reads TMEM lanes
 //               32*(w%4) ..+31 = tile rows), apply the fused epilogue (RMS row
 //               scale, bias, ReLU, residual add, sum-of-squares for the next
-//               RMSNorm, REG-row substitution) and store bf16.
+//               RMSNorm, REG-row substitution) in 32x64 boxes staged in shared
+//               memory: the residual box arrives by TMA, the bf16 result leaves
+//               by a TMA bulk-tensor store.
 // Two accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
 //
 // This kernel replaces the reference's F.linear / cuBLAS calls and its
@@ -59,7 +61,7 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 8 * 32 * 64 * 2 + 1024 + 256;
 };
 
 struct Epi {
@@ -204,16 +206,116 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// TMA bulk-tensor store of a staged smem box, bulk-group completion.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"((uint64_t)map),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Epilogue staging box: 32 rows x 64 bf16 columns (4 KB) in 128-byte swizzle
+// (16-byte chunk c of row r lives at chunk c ^ (r & 7)).  A box is filled by
+// TMA with the residual tile (RESID), combined with the accumulator by its
+// warp, and written back to global memory by a TMA bulk-tensor store.
+constexpr int kEpiBox = 32 * 64 * 2;
+
+// Applies the fused epilogue to one 64-column group of one row (values r[64]
+// from TMEM) and writes the bf16 result into the swizzled box.  Returns the
+// group's sum of squares of the stored values (columns < N).
+__device__ __forceinline__ float epilogue_group(const Epi& ep, const uint32_t* r, float rs, bool special, int col0,
+                                                int N, uint32_t box, int lane, bool resid) {
+  const uint32_t rsw = (uint32_t)(lane & 7);
+  float ssq = 0.0f;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const int col = col0 + c * 8;
+    const uint32_t addr = box + (uint32_t)lane * 128u + (((uint32_t)c ^ rsw) << 4);
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[c * 8 + j]) * rs;
+    const bool col_ok = col < N;
+    if ((ep.flags & CC2_EPI_BIAS) && col_ok) {
+      const float4 b0 = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
+      const float4 b1 = __ldg(reinterpret_cast<const float4*>(ep.bias + col) + 1);
+      v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
+      v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+    }
+    if (ep.flags & CC2_EPI_RELU) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = fmaxf(v[j], 0.0f);
+    }
+    if (resid) {
+      uint4 u;
+      asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w) : "r"(addr));
+      const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(hh[e]);
+        v[2 * e] += f.x;
+        v[2 * e + 1] += f.y;
+      }
+    }
+    if (special && col_ok) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = ep.special[col + j];
+    }
+    uint4 o;
+    o.x = pack_bf16(v[0], v[1]); o.y = pack_bf16(v[2], v[3]);
+    o.z = pack_bf16(v[4], v[5]); o.w = pack_bf16(v[6], v[7]);
+    if ((ep.flags & CC2_EPI_SSQ) && col_ok) {
+      const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&o);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(hh[e]);
+        ssq = fmaf(f.x, f.x, ssq);
+        ssq = fmaf(f.y, f.y, ssq);
+      }
+    }
+    asm volatile("st.shared.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(o.x), "r"(o.y), "r"(o.z), "r"(o.w)
+                 : "memory");
+  }
+  return ssq;
+}
+
+__device__ __forceinline__ float row_scale(const Epi& ep, int row, bool row_ok) {
+  if (!(ep.flags & CC2_EPI_ROWSCALE) || !row_ok) return 1.0f;
+  float t = 0.0f;
+  for (int g = 0; g < ep.ssq_parts; ++g) t += ep.ssq_in[(size_t)g * ep.ssq_ld + row];
+  return rsqrtf(t * ep.inv_dim + ep.eps);
+}
+
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               bf16* __restrict__ out, int ldo, int M, int N, int K, Epi ep) {
+               const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, int M, int N,
+               int K, Epi ep) {
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* bars = (uint64_t*)(smem + C::STAGES * C::STAGE_BYTES);
-  // bars[0..S): full, [S..2S): empty, [2S..2S+2): tmem full, [2S+2..2S+4): tmem empty
-  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * C::STAGES + 4);
+  uint8_t* epi_smem = smem + C::STAGES * C::STAGE_BYTES;  // 4 warps x 2 boxes
+  uint64_t* bars = (uint64_t*)(epi_smem + 8 * kEpiBox);
+  // bars: [0,S) full, [S,2S) empty, [2S,2S+2) tmem full, [2S+2,2S+4) tmem empty,
+  //       [2S+4, 2S+12) residual box loaded (warp q, box b) at 2S+4+2q+b
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * C::STAGES + 12);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -223,6 +325,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
   auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + a); };
   auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + 2 + a); };
+  auto rbar = [&](int q, int b) { return bar0 + 8u * (2 * C::STAGES + 4 + 2 * q + b); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -233,10 +336,13 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       mbar_init(tfull_bar(a), 1);
       mbar_init(tempty_bar(a), 4);
     }
+    for (int i = 0; i < 8; ++i) mbar_init(bar0 + 8u * (2 * C::STAGES + 4 + i), 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+    tma_prefetch_desc(&tmR);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -289,10 +395,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
           const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            mma_bf16(d_tmem, sw128_desc(sa + 32u * k), sw128_desc(sb + 32u * k), idesc,
-                     (kb | k) != 0 ? 1u : 0u);
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16(d_tmem, sw128_desc(sa + 32u * k), sw128_desc(sb + 32u * k), idesc, (kb | k) != 0 ? 1u : 0u);
           mma_commit(empty_bar(stage));
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -301,93 +405,70 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     }
     __syncwarp();
   } else {
-    // epilogue warps 2..5 -> TMEM lane quarter q = warp % 4
+    // ---- epilogue warps 2..5: TMEM lane quarter q = warp % 4 = tile rows 32q..32q+31
     const int q = warp & 3;
+    const bool resid = (ep.flags & CC2_EPI_RESID) != 0;
+    const uint32_t box0 = smem_u32(epi_smem + (size_t)q * 2 * kEpiBox);
+    uint32_t rphase = 0;  // bit b: parity of the next wait on rbar(q, b)
+    uint32_t use = 0;     // running box counter (box = use & 1)
     int it = 0;
+    constexpr int G = BN / 64;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      const int mt = tile / n_tiles, nt = tile % n_tiles;
+      const int row0 = mt * BM + q * 32;
+      const int ng = min(G, (N - nt * BN + 63) / 64);
+      if (resid && lane == 0) {  // prefetch group 0's residual box (overlaps the MMA wait)
+        bulk_wait_read0();
+        const int b = use & 1;
+        mbar_arrive_expect_tx(rbar(q, b), kEpiBox);
+        tma_load_2d(box0 + b * kEpiBox, &tmR, rbar(q, b), nt * BN, row0);
+      }
       const int acc = it & 1;
       const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
       if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag)) break;
       tc_fence_after();
-      const int mt = tile / n_tiles, nt = tile % n_tiles;
-      const int row = mt * BM + q * 32 + lane;
+      const int row = row0 + lane;
       const bool row_ok = row < M;
-      float rs = 1.0f;
-      if ((ep.flags & CC2_EPI_ROWSCALE) && row_ok) {
-        float t = 0.0f;
-        for (int g = 0; g < ep.ssq_parts; ++g) t += ep.ssq_in[(size_t)g * ep.ssq_ld + row];
-        rs = rsqrtf(t * ep.inv_dim + ep.eps);
-      }
+      const float rs = row_scale(ep, row, row_ok);
       const bool special = (ep.flags & CC2_EPI_SPECIAL) && row_ok && (row % ep.sp_period) == ep.sp_offset;
-      float ssq = 0.0f;
-      const uint32_t taddr = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
-#pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        uint32_t r[16];
-        tmem_ld16(taddr + (uint32_t)c0, r);
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      bool aborted = false;
+      for (int g = 0; g < ng; ++g, ++use) {
+        const int b = use & 1;
+        const uint32_t box = box0 + b * kEpiBox;
+        const int col0 = nt * BN + g * 64;
+        uint32_t r[64];
+        tmem_ld32(tbase + g * 64, r);
+        tmem_ld32(tbase + g * 64 + 32, r + 32);
         tmem_ld_wait();
-        const int col = nt * BN + c0;
-        if (row_ok && col < N) {
-          float v[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) v[j] = __uint_as_float(r[j]) * rs;
-          if (ep.flags & CC2_EPI_BIAS) {
-            const float4* bp = reinterpret_cast<const float4*>(ep.bias + col);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              float4 b4 = __ldg(bp + j);
-              v[4 * j] += b4.x; v[4 * j + 1] += b4.y; v[4 * j + 2] += b4.z; v[4 * j + 3] += b4.w;
-            }
+        if (resid) {
+          if (!mbar_wait(rbar(q, b), (rphase >> b) & 1u, abort_flag)) { aborted = true; break; }
+          rphase ^= 1u << b;
+          if (lane == 0 && g + 1 < ng) {  // next group's residual into the other box
+            bulk_wait_read0();
+            mbar_arrive_expect_tx(rbar(q, b ^ 1), kEpiBox);
+            tma_load_2d(box0 + (b ^ 1) * kEpiBox, &tmR, rbar(q, b ^ 1), col0 + 64, row0);
           }
-          if (ep.flags & CC2_EPI_RELU) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = fmaxf(v[j], 0.0f);
-          }
-          if (ep.flags & CC2_EPI_RESID) {
-            const uint4* rp = reinterpret_cast<const uint4*>(ep.resid + (size_t)row * ep.ld_resid + col);
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              uint4 u = rp[j];
-              const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                float2 f = __bfloat1622float2(h[e]);
-                v[8 * j + 2 * e] += f.x;
-                v[8 * j + 2 * e + 1] += f.y;
-              }
-            }
-          }
-          if (special) {
-#pragma unroll
-            for (int j = 0; j < 16; ++j) v[j] = ep.special[col + j];
-          }
-          uint4 o[2];
-          uint32_t* ow = reinterpret_cast<uint32_t*>(o);
-#pragma unroll
-          for (int j = 0; j < 8; ++j) ow[j] = pack_bf16(v[2 * j], v[2 * j + 1]);
-          if (ep.flags & CC2_EPI_SSQ) {
-            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(o);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              float2 f = __bfloat1622float2(h[e]);
-              ssq = fmaf(f.x, f.x, ssq);
-              ssq = fmaf(f.y, f.y, ssq);
-            }
-          }
-          uint4* op = reinterpret_cast<uint4*>(out + (size_t)row * ldo + col);
-          op[0] = o[0];
-          op[1] = o[1];
+        } else if (lane == 0) {
+          bulk_wait_read1();  // the store that last used this box has finished reading it
         }
-        if ((c0 & 63) == 48) {  // end of a 64-column group: store its partial sum of squares
-          if ((ep.flags & CC2_EPI_SSQ) && row_ok && nt * BN + (c0 & ~63) < N)
-            ep.ssq_out[(size_t)((nt * BN + c0) >> 6) * ep.ssq_ld + row] = ssq;
-          ssq = 0.0f;
+        __syncwarp();
+        const float ssq = epilogue_group(ep, r, rs, special, col0, N, box, lane, resid);
+        if ((ep.flags & CC2_EPI_SSQ) && row_ok) ep.ssq_out[(size_t)(col0 >> 6) * ep.ssq_ld + row] = ssq;
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, box, col0, row0);
+          bulk_commit();
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(acc));
+      if (aborted) break;
     }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
   }
   tc_fence_before();
   __syncthreads();
@@ -396,6 +477,255 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tmem_dealloc(tmem_base, C::TMEM_COLS);
   }
 }
+
+// ---------------------------------------------------------------------------------
+// 2-SM variant: a cluster of two CTAs computes a 256 x 256 output tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256).  CTA r of the pair loads rows
+// [128 r, 128 r + 128) of the A tile and rows [128 r, 128 r + 128) of the W
+// tile (half of N) into its own shared memory; the leader (rank 0) issues the
+// MMAs, which read both CTAs' halves, and each CTA's TMEM receives its own 128
+// rows x 256 columns.  Per SM this moves 32 KB per 128x256x64 step instead of
+// 48 KB.  Barriers: the leader's full[s] collects both CTAs' TMA bytes; the
+// leader's MMA commits release empty[s] and tmem_full[a] in both CTAs (one
+// commit per CTA, addressed through the cluster window); both CTAs' epilogue
+// warps release the leader's tmem_empty[a] (count 8).  The residual tile of
+// a CTA's 128 x 256 output is prefetched whole (4 boxes per warp) while the
+// MMAs of that tile run.
+// ---------------------------------------------------------------------------------
+namespace pair {
+
+constexpr int STAGES = 5;
+constexpr int A_BYTES = 128 * BK * 2;
+constexpr int B_BYTES = 128 * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int BN = 256;
+constexpr int TMEM_COLS = 2 * BN;
+constexpr int BOXES = 4;
+constexpr int SMEM = STAGES * STAGE_BYTES + 4 * BOXES * kEpiBox + 1024 + 256;
+
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t map_to_rank(uint32_t saddr, uint32_t rank) {
+  uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(saddr), "r"(rank));
+  return out;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void arrive_expect_tx_cluster(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cluster.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void arrive_cluster(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void mma_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive (once) on the mbarrier at cluster address `bar` when all prior
+// tcgen05.mma of this thread have completed.
+__device__ __forceinline__ void commit_pair(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ constexpr uint32_t idesc_pair() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                 const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, int M, int N,
+                 int K, Epi ep) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* epi_smem = smem + STAGES * STAGE_BYTES;
+  uint64_t* bars = (uint64_t*)(epi_smem + 4 * BOXES * kEpiBox);
+  // bars: [0,S) full, [S,2S) empty, [2S,2S+2) tmem full, [2S+2,2S+4) tmem empty,
+  //       [2S+4, 2S+4+16) residual box loaded (warp q, group g) at 2S+4+4q+g
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES + 4 + 4 * BOXES);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const uint32_t bar0 = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+  auto rbar = [&](int q, int g) { return bar0 + 8u * (2 * STAGES + 4 + BOXES * q + g); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 8);
+    }
+    for (int i = 0; i < 4 * BOXES; ++i) mbar_init(bar0 + 8u * (2 * STAGES + 4 + i), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmC);
+    tma_prefetch_desc(&tmR);
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int m_tiles = (M + 255) / 256;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int kblocks = (K + BK - 1) / BK;
+  const int pair_id = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t lead_full0 = map_to_rank(full_bar(0), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
+        const int mt = tile / n_tiles, nt = tile % n_tiles;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) { ok = false; break; }
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t fb = lead_full0 + 8u * stage;
+          if (leader) arrive_expect_tx_cluster(fb, 2 * STAGE_BYTES);
+          tma_load_2d_pair(sa, &tmA, fb, kb * BK, mt * 256 + (int)rank * 128);
+          tma_load_2d_pair(sa + A_BYTES, &tmB, fb, kb * BK, nt * BN + (int)rank * 128);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_pair();
+      const uint32_t peer_empty0 = map_to_rank(empty_bar(0), 1), own_empty0 = map_to_rank(empty_bar(0), 0);
+      const uint32_t peer_tfull0 = map_to_rank(tfull_bar(0), 1), own_tfull0 = map_to_rank(tfull_bar(0), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
+        if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_pair(d_tmem, sw128_desc(sa + 32u * k), sw128_desc(sb + 32u * k), idesc, (kb | k) != 0 ? 1u : 0u);
+          commit_pair(own_empty0 + 8u * stage);
+          commit_pair(peer_empty0 + 8u * stage);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (ok) {
+          commit_pair(own_tfull0 + 8u * acc);
+          commit_pair(peer_tfull0 + 8u * acc);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue warps 2..5 -> TMEM lane quarter q = rows 32q..32q+31 of this CTA's half
+    const int q = warp & 3;
+    const bool resid = (ep.flags & CC2_EPI_RESID) != 0;
+    const uint32_t box0 = smem_u32(epi_smem + (size_t)q * BOXES * kEpiBox);
+    const uint32_t lead_tempty0 = map_to_rank(tempty_bar(0), 0);
+    int it = 0;
+    for (int tile = pair_id; tile < num_tiles; tile += num_pairs, ++it) {
+      const int mt = tile / n_tiles, nt = tile % n_tiles;
+      const int row0 = mt * 256 + (int)rank * 128 + q * 32;
+      const int ng = min(BOXES, (N - nt * BN + 63) / 64);
+      if (lane == 0) {
+        bulk_wait_read0();  // the previous tile's stores have left the boxes
+        if (resid) {        // prefetch the whole residual tile while the MMAs run
+          for (int g = 0; g < ng; ++g) {
+            mbar_arrive_expect_tx(rbar(q, g), kEpiBox);
+            tma_load_2d(box0 + g * kEpiBox, &tmR, rbar(q, g), nt * BN + g * 64, row0);
+          }
+        }
+      }
+      __syncwarp();
+      const int acc = it & 1;
+      const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
+      if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag)) break;
+      tc_fence_after();
+      const int row = row0 + lane;
+      const bool row_ok = row < M;
+      const float rs = row_scale(ep, row, row_ok);
+      const bool special = (ep.flags & CC2_EPI_SPECIAL) && row_ok && (row % ep.sp_period) == ep.sp_offset;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+      bool aborted = false;
+      for (int g = 0; g < ng; ++g) {
+        const uint32_t box = box0 + g * kEpiBox;
+        const int col0 = nt * BN + g * 64;
+        uint32_t r[64];
+        tmem_ld32(tbase + g * 64, r);
+        tmem_ld32(tbase + g * 64 + 32, r + 32);
+        tmem_ld_wait();
+        if (resid && !mbar_wait(rbar(q, g), (uint32_t)it & 1u, abort_flag)) { aborted = true; break; }
+        const float ssq = epilogue_group(ep, r, rs, special, col0, N, box, lane, resid);
+        if ((ep.flags & CC2_EPI_SSQ) && row_ok) ep.ssq_out[(size_t)(col0 >> 6) * ep.ssq_ld + row] = ssq;
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, box, col0, row0);
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) arrive_cluster(lead_tempty0 + 8u * acc);
+      if (aborted) break;
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal or read it
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+}  // namespace pair
 
 // ---- host side ------------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -409,8 +739,7 @@ static EncodeTiledFn encode_fn() {
   std::call_once(once, [] {
     void* p = nullptr;
     cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
         q == cudaDriverEntryPointSuccess)
       fn = (EncodeTiledFn)p;
   });
@@ -418,50 +747,83 @@ static EncodeTiledFn encode_fn() {
 }
 
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix with row pitch ld
-// (elements); box = 64 columns x box_rows rows, 128-byte swizzle, zero fill
-// outside the matrix.
-static int make_map(CUtensorMap* map, const void* ptr, int cols, int rows, int ld, int box_rows) {
+// (elements); box = box_cols x box_rows, 128-byte swizzle, zero fill outside
+// the matrix (loads) / clipping (stores).
+static int make_map_box(CUtensorMap* map, const void* ptr, int cols, int rows, int ld, int box_cols, int box_rows) {
   EncodeTiledFn fn = encode_fn();
   CC2_REQUIRE(fn != nullptr, "cuTensorMapEncodeTiled unavailable");
   CC2_REQUIRE(((uintptr_t)ptr & 15u) == 0, "gemm operand not 16-byte aligned");
   CC2_REQUIRE((ld * 2) % 16 == 0, "gemm row pitch must be a multiple of 8 elements");
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 2};
-  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
-                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_error("cuTensorMapEncodeTiled failed (%d): cols=%d rows=%d ld=%d", (int)r, cols, rows, ld);
     return CC2_E_CUDA;
   }
   return CC2_OK;
 }
+static int make_map(CUtensorMap* map, const void* ptr, int cols, int rows, int ld, int box_rows) {
+  return make_map_box(map, ptr, cols, rows, ld, BK, box_rows);
+}
 
 template <int BN>
-static int launch(const CUtensorMap& ma, const CUtensorMap& mb, bf16* out, int ldo, int M, int N,
-                  int K, const Epi& ep, cudaStream_t st) {
+static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mr, int M,
+                  int N, int K, const Epi& ep, cudaStream_t st) {
   using C = Cfg<BN>;
   static unsigned long long attr_set = 0;  // one bit per device
   int dev = 0;
   CC2_CUDA(cudaGetDevice(&dev));
   if (dev >= 64 || !((attr_set >> dev) & 1ull)) {
-    CC2_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  C::SMEM));
+    CC2_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
     if (dev < 64) attr_set |= 1ull << dev;
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_tc_kernel<BN><<<grid, kThreads, C::SMEM, st>>>(ma, mb, out, ldo, M, N, K, ep);
+  gemm_tc_kernel<BN><<<grid, kThreads, C::SMEM, st>>>(ma, mb, mc, mr, M, N, K, ep);
   CC2_CHECK_LAUNCH();
+  return CC2_OK;
+}
+
+static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mr,
+                       int M, int N, int K, const Epi& ep, cudaStream_t st) {
+  static unsigned long long attr_set = 0;  // one bit per device
+  int dev = 0;
+  CC2_CUDA(cudaGetDevice(&dev));
+  if (dev >= 64 || !((attr_set >> dev) & 1ull)) {
+    CC2_CUDA(cudaFuncSetAttribute(pair::gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::SMEM));
+    if (dev < 64) attr_set |= 1ull << dev;
+  }
+  const int tiles = ((M + 255) / 256) * ((N + pair::BN - 1) / pair::BN);
+  const int pairs = std::min(tiles, num_sms() / 2);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = pair::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CC2_CUDA(cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel, ma, mb, mc, mr, M, N, K, ep));
   return CC2_OK;
 }
 
 }  // namespace tc
 
-int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N,
-                   int K, const cc2_epilogue* e, cudaStream_t st) {
+// 0: 2-SM tiles when M > 128 (default); 1: single-SM tiles only (kept for A/B
+// measurement through cc2_set_gemm_variant).
+int g_gemm_variant = 0;
+
+int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,
+                   const cc2_epilogue* e, cudaStream_t st) {
   using namespace tc;
   CC2_REQUIRE(M > 0 && N > 0 && K > 0, "gemm: bad sizes M=%d N=%d K=%d", M, N, K);
   CC2_REQUIRE(N % 16 == 0, "gemm(bf16): N must be a multiple of 16 (got %d)", N);
@@ -485,22 +847,30 @@ int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, in
   CC2_REQUIRE(!(ep.flags & CC2_EPI_ROWSCALE) || (ep.ssq_in && e->norm_dim > 0), "gemm: rowscale args");
   CC2_REQUIRE(!(ep.flags & CC2_EPI_BIAS) || (ep.bias && ((uintptr_t)ep.bias & 15u) == 0),
               "gemm: bias must be non-null and 16-byte aligned");
-  CC2_REQUIRE(!(ep.flags & CC2_EPI_RESID) ||
-                  (ep.resid && ((uintptr_t)ep.resid & 15u) == 0 && ep.ld_resid % 8 == 0),
+  CC2_REQUIRE(!(ep.flags & CC2_EPI_RESID) || (ep.resid && ((uintptr_t)ep.resid & 15u) == 0 && ep.ld_resid % 8 == 0),
               "gemm: resid alignment");
   CC2_REQUIRE(!(ep.flags & CC2_EPI_SSQ) || ep.ssq_out, "gemm: ssq_out null");
   CC2_REQUIRE(!(ep.flags & (CC2_EPI_SSQ | CC2_EPI_ROWSCALE)) || ep.ssq_ld >= M, "gemm: ssq_ld must be >= M");
   CC2_REQUIRE(!(ep.flags & CC2_EPI_SPECIAL) || (ep.special && ep.sp_period > 0), "gemm: special args");
-  const int tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
-  const bool use256 = N >= 256 && tiles256 >= num_sms();
-  CUtensorMap ma, mb;
+  CUtensorMap ma, mb, mc, mr;
   CC2_TRY(make_map(&ma, A, K, M, lda, BM));
-  if (use256) {
+  CC2_TRY(make_map_box(&mc, out, N, M, ldo, 64, 32));
+  if (ep.flags & CC2_EPI_RESID) {
+    CC2_TRY(make_map_box(&mr, ep.resid, N, M, ep.ld_resid, 64, 32));
+  } else {
+    mr = mc;
+  }
+  if (g_gemm_variant == 0 && M > BM) {  // 2-SM tiles (256 x 256 per CTA pair)
+    CC2_TRY(make_map(&mb, W, K, N, ldw, 128));
+    return launch_pair(ma, mb, mc, mr, M, N, K, ep, st);
+  }
+  const int tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
+  if (N >= 256 && tiles256 >= num_sms()) {
     CC2_TRY(make_map(&mb, W, K, N, ldw, 256));
-    return launch<256>(ma, mb, (bf16*)out, ldo, M, N, K, ep, st);
+    return launch<256>(ma, mb, mc, mr, M, N, K, ep, st);
   }
   CC2_TRY(make_map(&mb, W, K, N, ldw, 128));
-  return launch<128>(ma, mb, (bf16*)out, ldo, M, N, K, ep, st);
+  return launch<128>(ma, mb, mc, mr, M, N, K, ep, st);
 }
 
 }  // namespace cc2

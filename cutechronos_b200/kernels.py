@@ -192,6 +192,23 @@ def unscaled_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: 
     return out.reshape(B, S, H, D).transpose(1, 2)
 
 
+def attention_rows(qkv: torch.Tensor, token_mask: torch.Tensor, num_sets: int, S: int, num_heads: int,
+                   rope: bool = True, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Time attention on token rows already packed as the engine keeps them:
+    qkv (num_sets*S, 3*H*64) [Q|K|V], token_mask (num_sets*S,) uint8 ->
+    (num_sets*S, H*64).  One kernel launch, no repacking."""
+    _cuda(qkv, token_mask)
+    HD = qkv.shape[1] // 3
+    if out is None:
+        out = torch.empty(qkv.shape[0], HD, dtype=qkv.dtype, device=qkv.device)
+    cs = rope_table(S, HD // num_heads, 10000.0, qkv.device) if rope else None
+    nat.check(nat.load().cc2_attention(_code(qkv.dtype), 0, qkv.data_ptr(), qkv.shape[1], 0, HD, 2 * HD,
+                                       out.data_ptr(), HD, token_mask.data_ptr(), num_sets, S, num_heads,
+                                       HD // num_heads, None, None, 0, 0,
+                                       cs.data_ptr() if cs is not None else None, _stream(qkv)), "cc2_attention")
+    return out
+
+
 def group_attention(qkv: torch.Tensor, token_mask: torch.Tensor, group_ids: torch.Tensor, num_heads: int,
                     ) -> torch.Tensor:
     """Group self-attention core over token rows: qkv (B, S, 3*H*64) packed

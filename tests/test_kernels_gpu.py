@@ -174,6 +174,31 @@ def test_linear_fused_epilogues(M, N, Kd, dtype):
     assert torch.allclose(so.cpu(), kk.row_sumsq_parts(out.cpu()), rtol=1e-4, atol=1e-3)
 
 
+@pytest.mark.parametrize("M,N,Kd", [(129, 768, 768), (34048, 768, 768), (1000, 2304, 768), (777, 336, 3840)])
+def test_gemm_pair_vs_single_sm_tiles(M, N, Kd):
+    # the 2-SM (cta_group::2) and 1-SM tile paths give the same result
+    from cutechronos_b200 import _native as nat
+    g = torch.Generator().manual_seed(M)
+    x = torch.randn(M, Kd, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(N, Kd, generator=g) / math.sqrt(Kd)).to(torch.bfloat16).to(DEV)
+    resid = torch.randn(M, N, generator=g).to(torch.bfloat16).to(DEV)
+    lib = nat.load()
+    outs = []
+    try:
+        for variant in (0, 1):
+            lib.cc2_set_gemm_variant(variant)
+            out = resid.clone()
+            so = torch.zeros(((N + 63) // 64, M), device=DEV)
+            K().linear(x, w, residual=out, ssq_out=so, out=out)
+            outs.append((out.float().cpu(), so.cpu()))
+    finally:
+        lib.cc2_set_gemm_variant(0)
+    assert (outs[0][0] - outs[1][0]).abs().max().item() <= 2 ** -7 * outs[1][0].abs().max().item()
+    assert torch.allclose(outs[0][1], outs[1][1], rtol=1e-2, atol=1e-2)
+    ref = _gemm_ref(x.cpu(), w.cpu(), None, False, resid.cpu(), None, 0, 0)
+    assert (outs[0][0].double() - ref).abs().max().item() <= 8e-3 * ref.abs().max().item()
+
+
 # ---------------------------------------------------------------------------
 # attention
 # ---------------------------------------------------------------------------
