@@ -594,7 +594,52 @@ int cc2_profile_read(int* kinds, float* ms, double* flops, double* bytes, int ca
   return CC2_OK;
 }
 
+// ---- forward without a caller-provided workspace ------------------------------------
+// Scratch for cc2_forward_noalloc: one static device array per GPU that loads
+// the library.  Host code must not pass the symbol itself to a kernel (on the
+// host it names a host-side stand-in); the device address comes from
+// cudaGetSymbolAddress, looked up once per device with that device current.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[CC2_NOALLOC_SCRATCH_BYTES];
+
+static int noalloc_scratch_ptr(void** out) {
+  static std::mutex mu;
+  static void* addr[64] = {nullptr};
+  int dev = 0;
+  CC2_CUDA(cudaGetDevice(&dev));
+  CC2_REQUIRE(dev >= 0 && dev < 64, "noalloc: device index %d out of range", dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error("cudaGetSymbolAddress(scratch) failed on device %d: %s", dev, cudaGetErrorString(e));
+      return CC2_E_CUDA;
+    }
+    addr[dev] = p;
+  }
+  *out = addr[dev];
+  return CC2_OK;
+}
+
 // ---- component entry points ---------------------------------------------------------
+int cc2_forward_noalloc(const cc2_model* m, const float* context, const float* context_mask, int B, int L, int N,
+                        const int64_t* group_ids, void* out, float* loc, float* scale, void* stream) {
+  clear_error();
+  CC2_REQUIRE(m && context && out, "forward_noalloc: null argument");
+  CC2_REQUIRE(B > 0 && L > 0 && N > 0, "forward_noalloc: B, L and N must be positive");
+  const size_t need = plan_ws(*m, B, L, N, nullptr, nullptr);
+  if (need > CC2_NOALLOC_SCRATCH_BYTES) {
+    set_error("forward_noalloc: B=%d L=%d N=%d needs %zu scratch bytes, the static scratch holds %zu; "
+              "use cc2_forward with a workspace",
+              B, L, N, need, (size_t)CC2_NOALLOC_SCRATCH_BYTES);
+    return CC2_E_WORKSPACE;
+  }
+  void* ws = nullptr;
+  CC2_TRY(noalloc_scratch_ptr(&ws));
+  return cc2_forward(m, context, context_mask, B, L, N, group_ids, out, loc, scale, ws,
+                     (size_t)CC2_NOALLOC_SCRATCH_BYTES, stream);
+}
+
 int cc2_preprocess(const float* context, const float* context_mask, int B, int L, int patch_size, int context_length,
                    float te_scale, int use_arcsinh, int use_reg, int N, int dtype, void* patched, int ld_patched,
                    int pad_cols, uint8_t* token_mask, float* attn_mask, float* loc, float* scale, void* stream) {

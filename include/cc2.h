@@ -151,6 +151,26 @@ CC2_API int cc2_profile_begin(int capacity);
 CC2_API int cc2_profile_read(int* kinds, float* ms, double* flops, double* bytes, int capacity,
                              int* count);
 
+/* cc2_forward without a caller-provided workspace (no counterpart in the
+ * reference).  For callers that cannot allocate device memory themselves:
+ * foreign-language front ends with no device allocator of their own, and
+ * latency-sensitive serving loops where a cudaMalloc would synchronise the
+ * device.  The scratch lives in one static device array of
+ * CC2_NOALLOC_SCRATCH_BYTES (32 MiB) that every GPU loading this library
+ * holds until the process exits; it fits about 2,300 token rows of the
+ * Chronos-2-base model (e.g. 16 series of context 2048 with N = 4).  Larger
+ * requests fail with CC2_E_WORKSPACE and a message giving the bytes needed.
+ * The first call on a device looks the array's device address up (once per
+ * device, with that device current); make that first call before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU (other
+ * streams, other host threads) race and corrupt each other.  The forward
+ * writes every scratch byte it reads, so nothing needs clearing between
+ * calls.  No allocation happens in this call. */
+#define CC2_NOALLOC_SCRATCH_BYTES ((size_t)32 << 20)
+CC2_API int cc2_forward_noalloc(const cc2_model* m, const float* context, const float* context_mask,
+                                int B, int L, int N, const int64_t* group_ids, void* out, float* loc,
+                                float* scale, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Component kernels (each is one stage of cc2_forward).                     */
 /* ------------------------------------------------------------------------ */
