@@ -488,9 +488,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // 48 KB.  Barriers: the leader's full[s] collects both CTAs' TMA bytes; the
 // leader's MMA commits release empty[s] and tmem_full[a] in both CTAs (one
 // commit per CTA, addressed through the cluster window); both CTAs' epilogue
-// warps release the leader's tmem_empty[a] (count 8).  The residual tile of
-// a CTA's 128 x 256 output is prefetched whole (4 boxes per warp) while the
-// MMAs of that tile run.
+// warps release the leader's tmem_empty[a] (count 16).  Eight epilogue warps
+// per CTA (two per TMEM lane quarter) split the 64-column groups; each
+// prefetches its residual boxes and row scales while the MMAs of the tile run.
 // ---------------------------------------------------------------------------------
 namespace pair {
 
@@ -500,8 +500,10 @@ constexpr int B_BYTES = 128 * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int BN = 256;
 constexpr int TMEM_COLS = 2 * BN;
-constexpr int BOXES = 4;
-constexpr int SMEM = STAGES * STAGE_BYTES + 4 * BOXES * kEpiBox + 1024 + 256;
+constexpr int EPI_WARPS = 8;               // two per TMEM lane quarter, each takes half the column groups
+constexpr int BOXES = 2;                    // epilogue boxes per warp (one per 64-column group it owns)
+constexpr int THREADS = 32 * (2 + EPI_WARPS);
+constexpr int SMEM = STAGES * STAGE_BYTES + EPI_WARPS * BOXES * kEpiBox + 1024 + 256;
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -547,17 +549,17 @@ __device__ __forceinline__ constexpr uint32_t idesc_pair() {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(THREADS, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, int M, int N,
                  int K, Epi ep) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* epi_smem = smem + STAGES * STAGE_BYTES;
-  uint64_t* bars = (uint64_t*)(epi_smem + 4 * BOXES * kEpiBox);
+  uint64_t* bars = (uint64_t*)(epi_smem + EPI_WARPS * BOXES * kEpiBox);
   // bars: [0,S) full, [S,2S) empty, [2S,2S+2) tmem full, [2S+2,2S+4) tmem empty,
-  //       [2S+4, 2S+4+16) residual box loaded (warp q, group g) at 2S+4+4q+g
-  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES + 4 + 4 * BOXES);
+  //       [2S+4, 2S+4+16) residual box loaded (epilogue warp e, box j) at 2S+4+2e+j
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES + 4 + EPI_WARPS * BOXES);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -569,7 +571,6 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
   auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
   auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
-  auto rbar = [&](int q, int g) { return bar0 + 8u * (2 * STAGES + 4 + BOXES * q + g); };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -578,9 +579,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 8);
+      mbar_init(tempty_bar(a), 2 * EPI_WARPS);
     }
-    for (int i = 0; i < 4 * BOXES; ++i) mbar_init(bar0 + 8u * (2 * STAGES + 4 + i), 1);
+    for (int i = 0; i < EPI_WARPS * BOXES; ++i) mbar_init(bar0 + 8u * (2 * STAGES + 4 + i), 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmA);
@@ -660,44 +661,49 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     }
     __syncwarp();
   } else {
-    // ---- epilogue warps 2..5 -> TMEM lane quarter q = rows 32q..32q+31 of this CTA's half
+    // ---- epilogue warps 2..9: TMEM lane quarter q = warp % 4 (rows 32q..32q+31 of
+    // this CTA's half); warps 2..5 take column groups 0-1, warps 6..9 groups 2-3.
+    const int ew = warp - 2;
     const int q = warp & 3;
+    const int g0 = (ew >> 2) * BOXES;
     const bool resid = (ep.flags & CC2_EPI_RESID) != 0;
-    const uint32_t box0 = smem_u32(epi_smem + (size_t)q * BOXES * kEpiBox);
+    const uint32_t box0 = smem_u32(epi_smem + (size_t)ew * BOXES * kEpiBox);
     const uint32_t lead_tempty0 = map_to_rank(tempty_bar(0), 0);
+    auto rbar = [&](int j) { return bar0 + 8u * (2 * STAGES + 4 + BOXES * ew + j); };
     int it = 0;
     for (int tile = pair_id; tile < num_tiles; tile += num_pairs, ++it) {
       const int mt = tile / n_tiles, nt = tile % n_tiles;
       const int row0 = mt * 256 + (int)rank * 128 + q * 32;
-      const int ng = min(BOXES, (N - nt * BN + 63) / 64);
+      const int ng = min(BOXES, max(0, (N - nt * BN + 63) / 64 - g0));  // groups of this warp inside N
       if (lane == 0) {
         bulk_wait_read0();  // the previous tile's stores have left the boxes
-        if (resid) {        // prefetch the whole residual tile while the MMAs run
-          for (int g = 0; g < ng; ++g) {
-            mbar_arrive_expect_tx(rbar(q, g), kEpiBox);
-            tma_load_2d(box0 + g * kEpiBox, &tmR, rbar(q, g), nt * BN + g * 64, row0);
+        if (resid) {        // prefetch this warp's residual boxes while the MMAs run
+          for (int j = 0; j < ng; ++j) {
+            mbar_arrive_expect_tx(rbar(j), kEpiBox);
+            tma_load_2d(box0 + j * kEpiBox, &tmR, rbar(j), nt * BN + (g0 + j) * 64, row0);
           }
         }
       }
       __syncwarp();
-      const int acc = it & 1;
-      const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
-      if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag)) break;
-      tc_fence_after();
+      // per-row terms that do not depend on the accumulator, also before the wait
       const int row = row0 + lane;
       const bool row_ok = row < M;
       const float rs = row_scale(ep, row, row_ok);
       const bool special = (ep.flags & CC2_EPI_SPECIAL) && row_ok && (row % ep.sp_period) == ep.sp_offset;
+      const int acc = it & 1;
+      const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
+      if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag)) break;
+      tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       bool aborted = false;
-      for (int g = 0; g < ng; ++g) {
-        const uint32_t box = box0 + g * kEpiBox;
-        const int col0 = nt * BN + g * 64;
+      for (int j = 0; j < ng; ++j) {
+        const uint32_t box = box0 + j * kEpiBox;
+        const int col0 = nt * BN + (g0 + j) * 64;
         uint32_t r[64];
-        tmem_ld32(tbase + g * 64, r);
-        tmem_ld32(tbase + g * 64 + 32, r + 32);
+        tmem_ld32(tbase + (g0 + j) * 64, r);
+        tmem_ld32(tbase + (g0 + j) * 64 + 32, r + 32);
         tmem_ld_wait();
-        if (resid && !mbar_wait(rbar(q, g), (uint32_t)it & 1u, abort_flag)) { aborted = true; break; }
+        if (resid && !mbar_wait(rbar(j), (uint32_t)it & 1u, abort_flag)) { aborted = true; break; }
         const float ssq = epilogue_group(ep, r, rs, special, col0, N, box, lane, resid);
         if ((ep.flags & CC2_EPI_SSQ) && row_ok) ep.ssq_out[(size_t)(col0 >> 6) * ep.ssq_ld + row] = ssq;
         fence_proxy_async_smem();
@@ -802,7 +808,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   const int pairs = std::min(tiles, num_sms() / 2);
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
-  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.blockDim = dim3(pair::THREADS, 1, 1);
   cfg.dynamicSmemBytes = pair::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
