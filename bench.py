@@ -377,6 +377,8 @@ def run_micro(args):
         "gemm 8192^3 plain": (lambda: kk.linear(big, big), 2 * 8192 ** 3),
         "attn time S=133 (rope)": (lambda: kk.attention_rows(qkvr, tok, args.batch, 133, 12, True, att),
                                    4 * args.batch * 12 * 133 * 133 * 64),
+        "attn time S=133 (no rope)": (lambda: kk.attention_rows(qkvr, tok, args.batch, 133, 12, False, att),
+                                      4 * args.batch * 12 * 133 * 133 * 64),
         "cublas qkv  N=2304 K=768": (lambda: torch.matmul(x, wqkv.T), 2 * M * 3 * d * d),
         "cublas o    N=768  K=768": (lambda: torch.matmul(x, wo.T), 2 * M * d * d),
         "cublas ffn1 N=3072 K=768": (lambda: torch.matmul(x, wi.T), 2 * M * dff * d),

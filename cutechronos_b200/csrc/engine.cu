@@ -10,9 +10,10 @@
 //     gemm  X @ Wqkv_t^T * rs(ssq[3l])              -> QKV             (RMSNorm folded)
 //     attention mode 0 (RoPE, key mask)             -> ATT
 //     gemm  ATT @ Wo_t^T + X, ssq[3l+1]             -> X
-//     group size 1: gemm X @ Wv_g^T * rs(ssq[3l+1]) -> ATT             (softmax over one key = V)
-//     else:         gemm X @ Wqkv_g^T * rs -> QKV; attention mode 1 -> ATT
-//     gemm  ATT @ Wo_g^T + X, ssq[3l+2]             -> X
+//     group size 1: gemm X @ (Wo_g Wv_g)^T * rs + X, ssq[3l+2] -> Y; swap X, Y
+//                   (softmax over one key = V, so the block is one projection)
+//     else:         gemm X @ Wqkv_g^T * rs -> QKV; attention mode 1 -> ATT;
+//                   gemm ATT @ Wo_g^T + X, ssq[3l+2] -> X
 //     gemm  X @ Wi^T * rs(ssq[3l+2]), ReLU          -> E (as [M, dff])
 //     gemm  E @ Wo^T + X, ssq[3l+3]                 -> X
 //   rmsnorm_rows (final norm of the N future rows)  -> O[:, dff:]
@@ -82,6 +83,23 @@ __global__ void pack_matrix_kernel(T* dst, int ldd, const T* src, int rows, int 
     dst[(size_t)r * ldd + c] = fromf<T>(v);
   }
 }
+// dst (fp32) = src * colscale[c], optionally transposed (dst[c][r]).
+template <typename T>
+__global__ void to_f32_kernel(float* dst, const T* src, int rows, int cols, const T* colscale, int transpose) {
+  const size_t total = (size_t)rows * cols;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(i / cols), c = (int)(i % cols);
+    float v = tof<T>(src[i]);
+    if (colscale) v *= tof<T>(colscale[c]);
+    dst[transpose ? (size_t)c * rows + r : i] = v;
+  }
+}
+template <typename T>
+__global__ void from_f32_kernel(T* dst, const float* src, size_t n) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = fromf<T>(src[i]);
+}
+
 template <typename T>
 __global__ void pack_bias_kernel(float* dst, const T* a, const T* b, int n) {
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x)
@@ -104,6 +122,34 @@ static int pack_matrix(int dtype, void* dst, int ldd, const void* src, int rows,
   return dtype == CC2_BF16 ? pack_matrix_t<__nv_bfloat16>(dst, ldd, src, rows, cols, colscale, st)
                            : pack_matrix_t<float>(dst, ldd, src, rows, cols, colscale, st);
 }
+// dst (dtype, d x d) = Wo . (Wv * ln)  -- the group block of a one-series group
+// as a single projection; the product is formed in fp32 and rounded once.
+static int pack_wov(int dtype, void* dst, const void* wo, const void* wv, const void* ln, int d, float* tmp,
+                    cudaStream_t st) {
+  CC2_REQUIRE(wo && wv && ln, "pack: null group weight");
+  float* wo32 = tmp;
+  float* wvt32 = tmp + (size_t)d * d;
+  float* out32 = tmp + 2 * (size_t)d * d;
+  const int blocks = std::min(4096, (d * d + 255) / 256);
+  if (dtype == CC2_BF16) {
+    to_f32_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(wo32, (const __nv_bfloat16*)wo, d, d, nullptr, 0);
+    to_f32_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(wvt32, (const __nv_bfloat16*)wv, d, d,
+                                                         (const __nv_bfloat16*)ln, 1);
+  } else {
+    to_f32_kernel<float><<<blocks, 256, 0, st>>>(wo32, (const float*)wo, d, d, nullptr, 0);
+    to_f32_kernel<float><<<blocks, 256, 0, st>>>(wvt32, (const float*)wv, d, d, (const float*)ln, 1);
+  }
+  CC2_CHECK_LAUNCH();
+  // out[n][k] = sum_j Wo[n][j] * WvT[k][j]
+  CC2_TRY(launch_gemm_f32(wo32, d, wvt32, d, out32, d, d, d, d, nullptr, st));
+  if (dtype == CC2_BF16)
+    from_f32_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>((__nv_bfloat16*)dst, out32, (size_t)d * d);
+  else
+    from_f32_kernel<float><<<blocks, 256, 0, st>>>((float*)dst, out32, (size_t)d * d);
+  CC2_CHECK_LAUNCH();
+  return CC2_OK;
+}
+
 static int pack_bias(int dtype, float* dst, const void* a, const void* b, int n, cudaStream_t st) {
   CC2_REQUIRE(a != nullptr, "pack: null bias pointer");
   if (dtype == CC2_BF16)
@@ -152,6 +198,7 @@ using namespace cc2;
 // ---- model handle ---------------------------------------------------------------
 struct cc2_layer_pack {
   void* wqkv_t; void* wo_t; void* wqkv_g; void* wo_g; void* wi; void* wo_f;
+  void* wov_g;  // Wo_g . diag-free (Wv_g * ln_g): the whole group block for groups of one series
 };
 
 struct cc2_model {
@@ -168,6 +215,7 @@ struct cc2_model {
   void* w1_in; float* b1_in; void* w23_in; float* b23_in; float* reg;
   void* final_ln; void* w1_out; float* b1_out; void* w23_out; float* b23_out;
   float* rope;
+  float* pack_tmp;
 };
 
 namespace {
@@ -213,24 +261,27 @@ size_t plan_pack(const cc2_config& c, int dtype, cc2_model* m, char* base) {
     lo.push_back(p.take(e * d * d));
     lo.push_back(p.take(e * (size_t)dff * d));
     lo.push_back(p.take(e * (size_t)d * dff));
+    lo.push_back(p.take(e * (size_t)d * d));
   }
   size_t o_w1_in = p.take(e * (size_t)dff * in), o_b1_in = p.take(4 * dff);
   size_t o_w23_in = p.take(e * (size_t)d * kin_pad), o_b23_in = p.take(4 * d), o_reg = p.take(4 * d);
   size_t o_fln = p.take(e * d), o_w1_out = p.take(e * (size_t)dff * d), o_b1_out = p.take(4 * dff);
   size_t o_w23_out = p.take(e * (size_t)qps * (dff + d)), o_b23_out = p.take(4 * qps);
   size_t o_rope = p.take(sizeof(float) * 2 * (size_t)max_pos * (c.d_kv / 2));
+  size_t o_tmp = p.take(sizeof(float) * 3 * (size_t)d * d);  // fp32 scratch used only while packing
   if (m && base) {
     m->layers.resize(c.num_layers);
     for (int l = 0; l < c.num_layers; ++l) {
       cc2_layer_pack& L = m->layers[l];
-      L.wqkv_t = base + lo[6 * l + 0]; L.wo_t = base + lo[6 * l + 1];
-      L.wqkv_g = base + lo[6 * l + 2]; L.wo_g = base + lo[6 * l + 3];
-      L.wi = base + lo[6 * l + 4]; L.wo_f = base + lo[6 * l + 5];
+      L.wqkv_t = base + lo[7 * l + 0]; L.wo_t = base + lo[7 * l + 1];
+      L.wqkv_g = base + lo[7 * l + 2]; L.wo_g = base + lo[7 * l + 3];
+      L.wi = base + lo[7 * l + 4]; L.wo_f = base + lo[7 * l + 5]; L.wov_g = base + lo[7 * l + 6];
     }
     m->w1_in = base + o_w1_in; m->b1_in = (float*)(base + o_b1_in);
     m->w23_in = base + o_w23_in; m->b23_in = (float*)(base + o_b23_in); m->reg = (float*)(base + o_reg);
     m->final_ln = base + o_fln; m->w1_out = base + o_w1_out; m->b1_out = (float*)(base + o_b1_out);
     m->w23_out = base + o_w23_out; m->b23_out = (float*)(base + o_b23_out); m->rope = (float*)(base + o_rope);
+    m->pack_tmp = (float*)(base + o_tmp);
     m->in_dim = in; m->kin = dff + in; m->kin_pad = kin_pad; m->kout = dff + d; m->qps = qps; m->max_pos = max_pos;
   }
   return p.off;
@@ -347,6 +398,7 @@ int cc2_model_create(const cc2_config* cfg, int dtype, const cc2_weights* w, voi
     PK(pack_matrix(dtype, (char*)L.wqkv_g + e * d * d, d, w->group_k[l], d, d, w->group_ln[l], st));
     PK(pack_matrix(dtype, (char*)L.wqkv_g + 2 * e * d * d, d, w->group_v[l], d, d, w->group_ln[l], st));
     PK(pack_matrix(dtype, L.wo_g, d, w->group_o[l], d, d, nullptr, st));
+    PK(pack_wov(dtype, L.wov_g, w->group_o[l], w->group_v[l], w->group_ln[l], d, m->pack_tmp, st));
     PK(pack_matrix(dtype, L.wi, d, w->ff_wi[l], dff, d, w->ff_ln[l], st));
     PK(pack_matrix(dtype, L.wo_f, dff, w->ff_wo[l], d, dff, nullptr, st));
   }
@@ -498,49 +550,59 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
     e2.special_offset = P;
     CC2_TRY(gemm(dt, w.E, m->kin_pad, m->w23_in, m->kin_pad, w.X, d, M, d, m->kin_pad, &e2, st));
   }
+  // residual stream X and scratch Y swap roles after a one-GEMM group block
+  char* X = w.X;
+  char* Y = w.ATT;
   for (int l = 0; l < c.num_layers; ++l) {
     const cc2_layer_pack& Lw = m->layers[l];
     // time attention
     cc2_epilogue a = epi_m(CC2_EPI_ROWSCALE, M);
     a.ssq_in = ssq(3 * l); a.norm_dim = d; a.eps = eps;
-    CC2_TRY(gemm(dt, w.X, d, Lw.wqkv_t, d, w.QKV, 3 * d, M, 3 * d, d, &a, st));
+    CC2_TRY(gemm(dt, X, d, Lw.wqkv_t, d, w.QKV, 3 * d, M, 3 * d, d, &a, st));
     {
       ProfScope ps_(CC2_K_ATTN_TIME, 4.0 * B * (double)S * S * d, 0.0, st);
-      CC2_TRY(launch_attention(dt, 0, w.QKV, 3 * d, 0, d, 2 * d, w.ATT, d, w.tok, B, S, c.num_heads, c.d_kv,
+      CC2_TRY(launch_attention(dt, 0, w.QKV, 3 * d, 0, d, 2 * d, Y, d, w.tok, B, S, c.num_heads, c.d_kv,
                                nullptr, nullptr, 0, 0, m->rope, st));
     }
     cc2_epilogue o = epi_m(CC2_EPI_RESID | CC2_EPI_SSQ, M);
-    o.resid = w.X; o.ld_resid = d; o.ssq_out = ssq(3 * l + 1);
-    CC2_TRY(gemm(dt, w.ATT, d, Lw.wo_t, d, w.X, d, M, d, d, &o, st));
+    o.resid = X; o.ld_resid = d; o.ssq_out = ssq(3 * l + 1);
+    CC2_TRY(gemm(dt, Y, d, Lw.wo_t, d, X, d, M, d, d, &o, st));
     // group attention
     cc2_epilogue g = epi_m(CC2_EPI_ROWSCALE, M);
     g.ssq_in = ssq(3 * l + 1); g.norm_dim = d; g.eps = eps;
     if (max_group == 1) {
-      // softmax over a single unmasked key is exactly 1: the output is V
-      CC2_TRY(gemm(dt, w.X, d, (const char*)Lw.wqkv_g + e * 2 * d * d, d, w.ATT, d, M, d, d, &g, st));
+      // softmax over a single unmasked key is exactly 1, so the block is
+      // X + Wo (Wv norm(X)): one GEMM with the pre-multiplied Wo.Wv.  It
+      // writes the other residual buffer (A and the output must differ).
+      g.flags |= CC2_EPI_RESID | CC2_EPI_SSQ;
+      g.resid = X; g.ld_resid = d; g.ssq_out = ssq(3 * l + 2);
+      CC2_TRY(gemm(dt, X, d, Lw.wov_g, d, Y, d, M, d, d, &g, st));
+      std::swap(X, Y);
     } else {
-      CC2_TRY(gemm(dt, w.X, d, Lw.wqkv_g, d, w.QKV, 3 * d, M, 3 * d, d, &g, st));
-      ProfScope ps_(CC2_K_ATTN_GROUP, 4.0 * (double)S * gsq * d, 0.0, st);
-      CC2_TRY(launch_attention(dt, 1, w.QKV, 3 * d, 0, d, 2 * d, w.ATT, d, w.tok, S * num_groups, S, c.num_heads,
-                               c.d_kv, w.members, w.offsets, num_groups, max_group, nullptr, st));
+      CC2_TRY(gemm(dt, X, d, Lw.wqkv_g, d, w.QKV, 3 * d, M, 3 * d, d, &g, st));
+      {
+        ProfScope ps_(CC2_K_ATTN_GROUP, 4.0 * (double)S * gsq * d, 0.0, st);
+        CC2_TRY(launch_attention(dt, 1, w.QKV, 3 * d, 0, d, 2 * d, Y, d, w.tok, S * num_groups, S, c.num_heads,
+                                 c.d_kv, w.members, w.offsets, num_groups, max_group, nullptr, st));
+      }
+      cc2_epilogue og = epi_m(CC2_EPI_RESID | CC2_EPI_SSQ, M);
+      og.resid = X; og.ld_resid = d; og.ssq_out = ssq(3 * l + 2);
+      CC2_TRY(gemm(dt, Y, d, Lw.wo_g, d, X, d, M, d, d, &og, st));
     }
-    cc2_epilogue og = epi_m(CC2_EPI_RESID | CC2_EPI_SSQ, M);
-    og.resid = w.X; og.ld_resid = d; og.ssq_out = ssq(3 * l + 2);
-    CC2_TRY(gemm(dt, w.ATT, d, Lw.wo_g, d, w.X, d, M, d, d, &og, st));
     // feed-forward
     cc2_epilogue f1 = epi_m(CC2_EPI_ROWSCALE | CC2_EPI_RELU, M);
     f1.ssq_in = ssq(3 * l + 2); f1.norm_dim = d; f1.eps = eps;
-    CC2_TRY(gemm(dt, w.X, d, Lw.wi, d, w.E, dff, M, dff, d, &f1, st));
+    CC2_TRY(gemm(dt, X, d, Lw.wi, d, w.E, dff, M, dff, d, &f1, st));
     cc2_epilogue f2 = epi_m(CC2_EPI_RESID | CC2_EPI_SSQ, M);
-    f2.resid = w.X; f2.ld_resid = d; f2.ssq_out = ssq(3 * l + 3);
-    CC2_TRY(gemm(dt, w.E, dff, Lw.wo_f, dff, w.X, d, M, d, dff, &f2, st));
+    f2.resid = X; f2.ld_resid = d; f2.ssq_out = ssq(3 * l + 3);
+    CC2_TRY(gemm(dt, w.E, dff, Lw.wo_f, dff, X, d, M, d, dff, &f2, st));
   }
   (void)KE;
   // final RMSNorm of the N future rows -> O[:, dff:]
   const int BN_rows = B * N;
   {
     ProfScope ps_(CC2_K_RMSNORM, 0.0, 2.0 * e * BN_rows * d, st);
-    CC2_TRY(launch_rmsnorm_rows(dt, w.X, d, m->final_ln, w.O + e * dff, m->kout, BN_rows, d, N, S, S - N, eps, st));
+    CC2_TRY(launch_rmsnorm_rows(dt, X, d, m->final_ln, w.O + e * dff, m->kout, BN_rows, d, N, S, S - N, eps, st));
   }
   // output ResidualBlock
   {

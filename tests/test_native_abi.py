@@ -51,8 +51,9 @@ def _cfg(**kw):
 def test_pack_bytes_base_model(lib):
     n = C.c_size_t()
     assert lib.cc2_model_pack_bytes(C.byref(_cfg()), nat.CC2_BF16, C.byref(n)) == 0
-    # 119,477,664 bf16 parameters + fused layouts, fp32 biases and the RoPE table
-    assert 2 * 119_477_664 <= n.value <= 2 * 119_477_664 + 8 * 2**20
+    # 119,477,664 bf16 parameters
+    # + the fused Wo.Wv group matrices, fp32 biases, RoPE table and packing scratch
+    assert 2 * 119_477_664 <= n.value <= 2 * 119_477_664 + 32 * 2**20
     n32 = C.c_size_t()
     assert lib.cc2_model_pack_bytes(C.byref(_cfg()), nat.CC2_F32, C.byref(n32)) == 0
     assert n32.value > 1.9 * n.value
