@@ -12,7 +12,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libcc2_b200.so"
 
 CC2_F32, CC2_BF16 = 0, 1
-EPI_ROWSCALE, EPI_BIAS, EPI_RELU, EPI_RESID, EPI_SSQ, EPI_SPECIAL = 1, 2, 4, 8, 16, 32
+EPI_ROWSCALE, EPI_BIAS, EPI_RELU, EPI_RESID, EPI_SSQ, EPI_SPECIAL, EPI_ROPE = 1, 2, 4, 8, 16, 32, 64
 
 EXPORTED = (
     "cc2_last_error", "cc2_version", "cc2_device_status", "cc2_model_pack_bytes", "cc2_model_create",
@@ -56,6 +56,7 @@ class Epilogue(C.Structure):
         ("flags", C.c_int), ("ssq_in", _VP), ("norm_dim", C.c_int), ("eps", C.c_float),
         ("bias", _VP), ("resid", _VP), ("ld_resid", C.c_int), ("ssq_out", _VP), ("ssq_ld", C.c_int),
         ("special", _VP), ("special_period", C.c_int), ("special_offset", C.c_int),
+        ("rope_cs", _VP), ("rope_period", C.c_int), ("rope_cols", C.c_int),
     ]
 
 

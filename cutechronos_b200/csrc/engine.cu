@@ -7,8 +7,9 @@
 //   gemm  E[:,dff:] @ W1^T + b1, ReLU               -> E[:, :dff]      (input ResidualBlock hidden)
 //   gemm  E @ [W2|W3]^T + (b2+b3), REG row := shared[1], ssq0 -> X    (hidden + skip in one GEMM)
 //   per layer l:
-//     gemm  X @ Wqkv_t^T * rs(ssq[3l])              -> QKV             (RMSNorm folded)
-//     attention mode 0 (RoPE, key mask)             -> ATT
+//     gemm  X @ Wqkv_t^T * rs(ssq[3l]), RoPE on Q,K -> QKV            (RMSNorm folded; RoPE in the
+//                                                                     epilogue in bf16 mode)
+//     attention mode 0 (key mask)                   -> ATT
 //     gemm  ATT @ Wo_t^T + X, ssq[3l+1]             -> X
 //     group size 1: gemm X @ (Wo_g Wv_g)^T * rs + X, ssq[3l+2] -> Y; swap X, Y
 //                   (softmax over one key = V, so the block is one projection)
@@ -216,6 +217,7 @@ struct cc2_model {
   void* final_ln; void* w1_out; float* b1_out; void* w23_out; float* b23_out;
   float* rope;
   float* pack_tmp;
+  uint32_t* rope_bf;  // [pos][d_kv/2] packed (cos, sin) bf16 pairs for the QKV epilogue
 };
 
 namespace {
@@ -269,6 +271,7 @@ size_t plan_pack(const cc2_config& c, int dtype, cc2_model* m, char* base) {
   size_t o_w23_out = p.take(e * (size_t)qps * (dff + d)), o_b23_out = p.take(4 * qps);
   size_t o_rope = p.take(sizeof(float) * 2 * (size_t)max_pos * (c.d_kv / 2));
   size_t o_tmp = p.take(sizeof(float) * 3 * (size_t)d * d);  // fp32 scratch used only while packing
+  size_t o_rope_bf = p.take(sizeof(uint32_t) * (size_t)max_pos * (c.d_kv / 2));
   if (m && base) {
     m->layers.resize(c.num_layers);
     for (int l = 0; l < c.num_layers; ++l) {
@@ -282,6 +285,7 @@ size_t plan_pack(const cc2_config& c, int dtype, cc2_model* m, char* base) {
     m->final_ln = base + o_fln; m->w1_out = base + o_w1_out; m->b1_out = (float*)(base + o_b1_out);
     m->w23_out = base + o_w23_out; m->b23_out = (float*)(base + o_b23_out); m->rope = (float*)(base + o_rope);
     m->pack_tmp = (float*)(base + o_tmp);
+    m->rope_bf = (uint32_t*)(base + o_rope_bf);
     m->in_dim = in; m->kin = dff + in; m->kin_pad = kin_pad; m->kout = dff + d; m->qps = qps; m->max_pos = max_pos;
   }
   return p.off;
@@ -433,7 +437,18 @@ int cc2_model_create(const cc2_config* cfg, int dtype, const cc2_weights* w, voi
       tab[((size_t)pos * half + i) * 2 + 1] = (float)std::sin((double)f);
     }
   }
-  if (cudaMemcpyAsync(m->rope, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+  // bf16 copy (round to nearest even) packed as cos | sin << 16
+  std::vector<uint32_t> tab_bf(tab.size() / 2);
+  auto to_bf = [](float f) -> uint32_t {
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return u >> 16;
+  };
+  for (size_t i = 0; i < tab_bf.size(); ++i) tab_bf[i] = to_bf(tab[2 * i]) | (to_bf(tab[2 * i + 1]) << 16);
+  if (cudaMemcpyAsync(m->rope_bf, tab_bf.data(), tab_bf.size() * sizeof(uint32_t), cudaMemcpyHostToDevice, st) !=
+          cudaSuccess ||
+      cudaMemcpyAsync(m->rope, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice, st) != cudaSuccess ||
       cudaStreamSynchronize(st) != cudaSuccess) {
     set_error("uploading the RoPE table failed");
     return fail(CC2_E_CUDA);
@@ -556,13 +571,17 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
   for (int l = 0; l < c.num_layers; ++l) {
     const cc2_layer_pack& Lw = m->layers[l];
     // time attention
-    cc2_epilogue a = epi_m(CC2_EPI_ROWSCALE, M);
+    // bf16: RoPE is applied to Q and K in the QKV epilogue (position = row % S);
+    // fp32: inside the attention kernel
+    const bool rope_in_gemm = dt == CC2_BF16;
+    cc2_epilogue a = epi_m(CC2_EPI_ROWSCALE | (rope_in_gemm ? CC2_EPI_ROPE : 0), M);
     a.ssq_in = ssq(3 * l); a.norm_dim = d; a.eps = eps;
+    a.rope_cs = m->rope_bf; a.rope_period = S; a.rope_cols = 2 * d;
     CC2_TRY(gemm(dt, X, d, Lw.wqkv_t, d, w.QKV, 3 * d, M, 3 * d, d, &a, st));
     {
       ProfScope ps_(CC2_K_ATTN_TIME, 4.0 * B * (double)S * S * d, 0.0, st);
       CC2_TRY(launch_attention(dt, 0, w.QKV, 3 * d, 0, d, 2 * d, Y, d, w.tok, B, S, c.num_heads, c.d_kv,
-                               nullptr, nullptr, 0, 0, m->rope, st));
+                               nullptr, nullptr, 0, 0, rope_in_gemm ? nullptr : m->rope, st));
     }
     cc2_epilogue o = epi_m(CC2_EPI_RESID | CC2_EPI_SSQ, M);
     o.resid = X; o.ld_resid = d; o.ssq_out = ssq(3 * l + 1);

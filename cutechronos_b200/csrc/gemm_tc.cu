@@ -78,6 +78,9 @@ struct Epi {
   const float* special;
   int sp_period;
   int sp_offset;
+  const uint32_t* rope_cs;  // [pos][32] packed (cos, sin) bf16 pairs
+  int rope_period;
+  int rope_cols;
 };
 
 // ---- PTX wrappers -------------------------------------------------------------
@@ -237,6 +240,26 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
 // TMA with the residual tile (RESID), combined with the accumulator by its
 // warp, and written back to global memory by a TMA bulk-tensor store.
 constexpr int kEpiBox = 32 * 64 * 2;
+
+// Loads the 32 packed (cos, sin) pairs of this row's token position.
+__device__ __forceinline__ void load_rope_row(const Epi& ep, int row, bool row_ok, uint32_t (&cs)[32]) {
+  const uint4* src = reinterpret_cast<const uint4*>(ep.rope_cs + (size_t)(row_ok ? row % ep.rope_period : 0) * 32);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint4 u = __ldg(src + j);
+    cs[4 * j] = u.x; cs[4 * j + 1] = u.y; cs[4 * j + 2] = u.z; cs[4 * j + 3] = u.w;
+  }
+}
+// Rotate-half RoPE on one 64-column head held in r (row-scaled first).
+__device__ __forceinline__ void rope_group(uint32_t* r, const uint32_t (&cs)[32], float rs) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float c = __uint_as_float(cs[i] << 16), sn = __uint_as_float(cs[i] & 0xffff0000u);
+    const float x1 = __uint_as_float(r[i]) * rs, x2 = __uint_as_float(r[i + 32]) * rs;
+    r[i] = __float_as_uint(x1 * c - x2 * sn);
+    r[i + 32] = __float_as_uint(x2 * c + x1 * sn);
+  }
+}
 
 // Applies the fused epilogue to one 64-column group of one row (values r[64]
 // from TMEM) and writes the bf16 result into the swizzled box.  Returns the
@@ -431,6 +454,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       const bool row_ok = row < M;
       const float rs = row_scale(ep, row, row_ok);
       const bool special = (ep.flags & CC2_EPI_SPECIAL) && row_ok && (row % ep.sp_period) == ep.sp_offset;
+      const bool rope_tile = (ep.flags & CC2_EPI_ROPE) && nt * BN < ep.rope_cols;
+      uint32_t cs[32];
+      if (rope_tile) load_rope_row(ep, row, row_ok, cs);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       bool aborted = false;
       for (int g = 0; g < ng; ++g, ++use) {
@@ -453,7 +479,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           bulk_wait_read1();  // the store that last used this box has finished reading it
         }
         __syncwarp();
-        const float ssq = epilogue_group(ep, r, rs, special, col0, N, box, lane, resid);
+        float rsg = rs;
+        if (rope_tile && col0 < ep.rope_cols) {
+          rope_group(r, cs, rs);
+          rsg = 1.0f;
+        }
+        const float ssq = epilogue_group(ep, r, rsg, special, col0, N, box, lane, resid);
         if ((ep.flags & CC2_EPI_SSQ) && row_ok) ep.ssq_out[(size_t)(col0 >> 6) * ep.ssq_ld + row] = ssq;
         fence_proxy_async_smem();
         __syncwarp();
@@ -549,6 +580,7 @@ __device__ __forceinline__ constexpr uint32_t idesc_pair() {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
+template <bool ROPE>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, int M, int N,
@@ -690,6 +722,11 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       const bool row_ok = row < M;
       const float rs = row_scale(ep, row, row_ok);
       const bool special = (ep.flags & CC2_EPI_SPECIAL) && row_ok && (row % ep.sp_period) == ep.sp_offset;
+      const bool rope_tile = ROPE && nt * BN + g0 * 64 < ep.rope_cols;
+      uint32_t cs[ROPE ? 32 : 1];
+      if constexpr (ROPE) {
+        if (rope_tile) load_rope_row(ep, row, row_ok, cs);
+      }
       const int acc = it & 1;
       const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
       if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag)) break;
@@ -704,7 +741,14 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         tmem_ld32(tbase + (g0 + j) * 64 + 32, r + 32);
         tmem_ld_wait();
         if (resid && !mbar_wait(rbar(j), (uint32_t)it & 1u, abort_flag)) { aborted = true; break; }
-        const float ssq = epilogue_group(ep, r, rs, special, col0, N, box, lane, resid);
+        float rsg = rs;
+        if constexpr (ROPE) {
+          if (rope_tile && col0 < ep.rope_cols) {
+            rope_group(r, cs, rs);
+            rsg = 1.0f;
+          }
+        }
+        const float ssq = epilogue_group(ep, r, rsg, special, col0, N, box, lane, resid);
         if ((ep.flags & CC2_EPI_SSQ) && row_ok) ep.ssq_out[(size_t)(col0 >> 6) * ep.ssq_ld + row] = ssq;
         fence_proxy_async_smem();
         __syncwarp();
@@ -801,7 +845,10 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   int dev = 0;
   CC2_CUDA(cudaGetDevice(&dev));
   if (dev >= 64 || !((attr_set >> dev) & 1ull)) {
-    CC2_CUDA(cudaFuncSetAttribute(pair::gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, pair::SMEM));
+    CC2_CUDA(cudaFuncSetAttribute(pair::gemm_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  pair::SMEM));
+    CC2_CUDA(cudaFuncSetAttribute(pair::gemm_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  pair::SMEM));
     if (dev < 64) attr_set |= 1ull << dev;
   }
   const int tiles = ((M + 255) / 256) * ((N + pair::BN - 1) / pair::BN);
@@ -818,7 +865,10 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  CC2_CUDA(cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel, ma, mb, mc, mr, M, N, K, ep));
+  if (ep.flags & CC2_EPI_ROPE)
+    CC2_CUDA(cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<true>, ma, mb, mc, mr, M, N, K, ep));
+  else
+    CC2_CUDA(cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<false>, ma, mb, mc, mr, M, N, K, ep));
   return CC2_OK;
 }
 
@@ -849,7 +899,13 @@ int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, in
     ep.special = e->special;
     ep.sp_period = e->special_period;
     ep.sp_offset = e->special_offset;
+    ep.rope_cs = e->rope_cs;
+    ep.rope_period = e->rope_period;
+    ep.rope_cols = e->rope_cols;
   }
+  CC2_REQUIRE(!(ep.flags & CC2_EPI_ROPE) ||
+                  (ep.rope_cs && ((uintptr_t)ep.rope_cs & 15u) == 0 && ep.rope_period > 0 && ep.rope_cols % 64 == 0),
+              "gemm: rope args (16-byte aligned table, period > 0, cols multiple of 64)");
   CC2_REQUIRE(!(ep.flags & CC2_EPI_ROWSCALE) || (ep.ssq_in && e->norm_dim > 0), "gemm: rowscale args");
   CC2_REQUIRE(!(ep.flags & CC2_EPI_BIAS) || (ep.bias && ((uintptr_t)ep.bias & 15u) == 0),
               "gemm: bias must be non-null and 16-byte aligned");

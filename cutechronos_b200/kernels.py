@@ -109,11 +109,14 @@ def row_sumsq_parts(x: torch.Tensor) -> torch.Tensor:
 
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *, relu: bool = False,
            residual: torch.Tensor | None = None, row_ssq: torch.Tensor | None = None, norm_dim: int = 0,
-           eps: float = 1e-6, ssq_out: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+           eps: float = 1e-6, ssq_out: torch.Tensor | None = None, out: torch.Tensor | None = None,
+           rope_period: int = 0, rope_cols: int = 0) -> torch.Tensor:
     """out = epilogue(x @ weight^T): optional row scale
     rsqrt(row_ssq.sum(0) / norm_dim + eps) with ``row_ssq`` (G, M) partial sums
     per 64-column group, + bias (fp32), ReLU, + residual, and ``ssq_out``
-    (G', M) <- partial sums of squares of the stored output."""
+    (G', M) <- partial sums of squares of the stored output.  ``rope_period``
+    > 0 (bf16 only) rotates every 64-column head below ``rope_cols`` at
+    position row % rope_period with bf16 cos/sin, as the engine does for Q, K."""
     _cuda(x, weight, bias, residual, row_ssq, ssq_out)
     K = x.shape[-1]
     x2 = x.reshape(-1, K).contiguous()
@@ -146,6 +149,11 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
         flags |= nat.EPI_SSQ
         e.ssq_out = ssq_out.data_ptr()
         e.ssq_ld = ssq_out.shape[-1]
+    if rope_period > 0:
+        flags |= nat.EPI_ROPE
+        tab = rope_table_bf16(rope_period, 64, 10000.0, x.device)
+        keep.append(tab)
+        e.rope_cs, e.rope_period, e.rope_cols = tab.data_ptr(), rope_period, rope_cols
     e.flags = flags
     nat.check(nat.load().cc2_gemm(_code(x.dtype), x2.data_ptr(), K, w.data_ptr(), K, out.data_ptr(), N, M, N, K,
                                   C.byref(e), _stream(x)), "cc2_gemm")
@@ -165,6 +173,12 @@ def rope_table(S: int, d_kv: int = 64, theta: float = 10000.0, device=None) -> t
         tab = torch.stack([ang.cos(), ang.sin()], dim=-1).float()
         _ROPE_CACHE[key] = tab.to(device)
     return _ROPE_CACHE[key]
+
+
+def rope_table_bf16(S: int, d_kv: int = 64, theta: float = 10000.0, device=None) -> torch.Tensor:
+    """(S, d_kv/2) int32 of packed bf16 (cos | sin << 16), the QKV-epilogue table."""
+    t = rope_table(S, d_kv, theta, "cpu").to(torch.bfloat16).view(torch.int16).to(torch.int32) & 0xFFFF
+    return (t[..., 0] | (t[..., 1] << 16)).to(torch.int32).contiguous().to(device)
 
 
 def unscaled_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: torch.Tensor | None = None, *,

@@ -199,7 +199,10 @@ enum {
   CC2_EPI_SSQ = 16,      /* ssq_out[g*ssq_ld + row] = sum over the 64 columns
                             64g..64g+63 of out[row, col]^2 (partial sums per
                             64-column group: deterministic, no atomics)        */
-  CC2_EPI_SPECIAL = 32   /* rows with row % period == offset get special[]     */
+  CC2_EPI_SPECIAL = 32,  /* rows with row % period == offset get special[]     */
+  CC2_EPI_ROPE = 64      /* bf16 only: rotate-half RoPE on every 64-column head
+                            with col < rope_cols at position row % rope_period,
+                            rope_cs[pos*32 + i] = (cos | sin << 16) as bf16 */
 };
 
 typedef struct {
@@ -210,6 +213,7 @@ typedef struct {
   float* ssq_out;
   int ssq_ld;            /* row stride between 64-column groups of ssq_in / ssq_out */
   const float* special; int special_period; int special_offset;
+  const uint32_t* rope_cs; int rope_period; int rope_cols;
 } cc2_epilogue;
 
 /* Tile variant of the bf16 GEMM: 0 (default) = 2-SM tcgen05 tiles of 256 x 256

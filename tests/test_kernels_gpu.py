@@ -199,6 +199,25 @@ def test_gemm_pair_vs_single_sm_tiles(M, N, Kd):
     assert (outs[0][0].double() - ref).abs().max().item() <= 8e-3 * ref.abs().max().item()
 
 
+@pytest.mark.parametrize("M,S", [(133 * 3, 133), (37, 37), (521 * 2, 521)])
+def test_qkv_epilogue_rope(M, S):
+    # RoPE applied in the QKV GEMM epilogue (Q and K columns, position = row % S)
+    g = torch.Generator().manual_seed(M + S)
+    x = torch.randn(M, 768, generator=g).to(torch.bfloat16)
+    w = (torch.randn(2304, 768, generator=g) / 28).to(torch.bfloat16)
+    out = K().linear(x.to(DEV), w.to(DEV), rope_period=S, rope_cols=1536).float().cpu()
+    y = (x.double() @ w.double().T).float()
+    tab = K().rope_table(S, 64, 10000.0, "cpu").to(torch.bfloat16).float()  # bf16 cos/sin, as the engine
+    pos = torch.arange(M) % S
+    c, sn = tab[pos, :, 0], tab[pos, :, 1]
+    ref = y.clone()
+    for h in range(24):  # Q and K heads
+        a, b = y[:, 64 * h:64 * h + 32], y[:, 64 * h + 32:64 * h + 64]
+        ref[:, 64 * h:64 * h + 32] = a * c - b * sn
+        ref[:, 64 * h + 32:64 * h + 64] = b * c + a * sn
+    assert (out - ref).abs().max().item() <= 8e-3 * ref.abs().max().item()
+
+
 # ---------------------------------------------------------------------------
 # attention
 # ---------------------------------------------------------------------------
