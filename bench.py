@@ -415,7 +415,7 @@ def main():
     ap.add_argument("--no-latency", action="store_true")
     ap.add_argument("--micro", action="store_true", help="per-kernel micro-benchmark instead of the step")
     ap.add_argument("--only", default="", help="with --micro: run only cases whose name contains this")
-    ap.add_argument("--gemm-variant", type=int, default=0, help="0: 2-SM GEMM tiles, 1: 1-SM tiles only")
+    ap.add_argument("--gemm-variant", type=int, default=0, help="0: 2-SM GEMM tiles, 1: 1-SM tiles only, 3: mainloop only (no output)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

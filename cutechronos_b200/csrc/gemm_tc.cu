@@ -112,8 +112,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 // Bounded wait: false when the CTA is aborting or the limit ran out.
-__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-  if (mbar_try_wait(bar, parity)) return true;
+__device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t n = 1;; ++n) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -126,6 +125,9 @@ __device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile i
       }
     }
   }
+}
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  return mbar_try_wait(bar, parity) || mbar_wait_slow(bar, parity, abort_flag);
 }
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int x, int y) {
@@ -264,7 +266,7 @@ __device__ __forceinline__ void rope_group(uint32_t* r, const uint32_t (&cs)[32]
 // Applies the fused epilogue to one 64-column group of one row (values r[64]
 // from TMEM) and writes the bf16 result into the swizzled box.  Returns the
 // group's sum of squares of the stored values (columns < N).
-__device__ __forceinline__ float epilogue_group(const Epi& ep, const uint32_t* r, float rs, bool special, int col0,
+__device__ __forceinline__ float epilogue_group(const Epi& ep, const int flags, const uint32_t* r, float rs, bool special, int col0,
                                                 int N, uint32_t box, int lane, bool resid) {
   const uint32_t rsw = (uint32_t)(lane & 7);
   float ssq = 0.0f;
@@ -276,13 +278,13 @@ __device__ __forceinline__ float epilogue_group(const Epi& ep, const uint32_t* r
 #pragma unroll
     for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[c * 8 + j]) * rs;
     const bool col_ok = col < N;
-    if ((ep.flags & CC2_EPI_BIAS) && col_ok) {
+    if ((flags & CC2_EPI_BIAS) && col_ok) {
       const float4 b0 = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
       const float4 b1 = __ldg(reinterpret_cast<const float4*>(ep.bias + col) + 1);
       v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
       v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
     }
-    if (ep.flags & CC2_EPI_RELU) {
+    if (flags & CC2_EPI_RELU) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) v[j] = fmaxf(v[j], 0.0f);
     }
@@ -304,7 +306,7 @@ __device__ __forceinline__ float epilogue_group(const Epi& ep, const uint32_t* r
     uint4 o;
     o.x = pack_bf16(v[0], v[1]); o.y = pack_bf16(v[2], v[3]);
     o.z = pack_bf16(v[4], v[5]); o.w = pack_bf16(v[6], v[7]);
-    if ((ep.flags & CC2_EPI_SSQ) && col_ok) {
+    if ((flags & CC2_EPI_SSQ) && col_ok) {
       const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&o);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -319,8 +321,8 @@ __device__ __forceinline__ float epilogue_group(const Epi& ep, const uint32_t* r
   return ssq;
 }
 
-__device__ __forceinline__ float row_scale(const Epi& ep, int row, bool row_ok) {
-  if (!(ep.flags & CC2_EPI_ROWSCALE) || !row_ok) return 1.0f;
+__device__ __forceinline__ float row_scale(const Epi& ep, const int flags, int row, bool row_ok) {
+  if (!(flags & CC2_EPI_ROWSCALE) || !row_ok) return 1.0f;
   float t = 0.0f;
   for (int g = 0; g < ep.ssq_parts; ++g) t += ep.ssq_in[(size_t)g * ep.ssq_ld + row];
   return rsqrtf(t * ep.inv_dim + ep.eps);
@@ -452,7 +454,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       tc_fence_after();
       const int row = row0 + lane;
       const bool row_ok = row < M;
-      const float rs = row_scale(ep, row, row_ok);
+      const float rs = row_scale(ep, ep.flags, row, row_ok);
       const bool special = (ep.flags & CC2_EPI_SPECIAL) && row_ok && (row % ep.sp_period) == ep.sp_offset;
       const bool rope_tile = (ep.flags & CC2_EPI_ROPE) && nt * BN < ep.rope_cols;
       uint32_t cs[32];
@@ -484,7 +486,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           rope_group(r, cs, rs);
           rsg = 1.0f;
         }
-        const float ssq = epilogue_group(ep, r, rsg, special, col0, N, box, lane, resid);
+        const float ssq = epilogue_group(ep, ep.flags, r, rsg, special, col0, N, box, lane, resid);
         if ((ep.flags & CC2_EPI_SSQ) && row_ok) ep.ssq_out[(size_t)(col0 >> 6) * ep.ssq_ld + row] = ssq;
         fence_proxy_async_smem();
         __syncwarp();
@@ -525,16 +527,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // ---------------------------------------------------------------------------------
 namespace pair {
 
-constexpr int STAGES = 5;
 constexpr int A_BYTES = 128 * BK * 2;
 constexpr int B_BYTES = 128 * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int BN = 256;
 constexpr int TMEM_COLS = 2 * BN;
 constexpr int EPI_WARPS = 8;               // two per TMEM lane quarter, each takes half the column groups
-constexpr int BOXES = 2;                    // epilogue boxes per warp (one per 64-column group it owns)
+constexpr int GPW = 2;                      // 64-column groups per epilogue warp
 constexpr int THREADS = 32 * (2 + EPI_WARPS);
-constexpr int SMEM = STAGES * STAGE_BYTES + EPI_WARPS * BOXES * kEpiBox + 1024 + 256;
+// STAGES: depth of the TMA ring; BOXES: epilogue staging boxes per warp (2 =
+// one per group, needed for the residual prefetch; 1 = boxes reused, which
+// frees shared memory for a deeper ring).
+template <int STAGES, int BOXES>
+constexpr int smem_bytes() { return STAGES * STAGE_BYTES + EPI_WARPS * BOXES * kEpiBox + 1024 + 256; }
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -580,7 +585,9 @@ __device__ __forceinline__ constexpr uint32_t idesc_pair() {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
-template <bool ROPE>
+// F >= 0: the epilogue flags, fixed at compile time (only the work a GEMM
+// needs is emitted); F = -1: flags read at run time (RoPE not supported).
+template <int F, int STAGES, int BOXES, bool SKIP_EPI = false>
 __global__ void __launch_bounds__(THREADS, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, int M, int N,
@@ -594,6 +601,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   uint32_t* tmem_slot = (uint32_t*)(bars + 2 * STAGES + 4 + EPI_WARPS * BOXES);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
 
+  constexpr bool ROPE = F >= 0 && (F & CC2_EPI_ROPE);
+  const int flags = F >= 0 ? F : ep.flags;
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_rank();
@@ -697,8 +706,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     // this CTA's half); warps 2..5 take column groups 0-1, warps 6..9 groups 2-3.
     const int ew = warp - 2;
     const int q = warp & 3;
-    const int g0 = (ew >> 2) * BOXES;
-    const bool resid = (ep.flags & CC2_EPI_RESID) != 0;
+    const int g0 = (ew >> 2) * GPW;
+    const bool resid = (flags & CC2_EPI_RESID) != 0;
     const uint32_t box0 = smem_u32(epi_smem + (size_t)ew * BOXES * kEpiBox);
     const uint32_t lead_tempty0 = map_to_rank(tempty_bar(0), 0);
     auto rbar = [&](int j) { return bar0 + 8u * (2 * STAGES + 4 + BOXES * ew + j); };
@@ -706,7 +715,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
     for (int tile = pair_id; tile < num_tiles; tile += num_pairs, ++it) {
       const int mt = tile / n_tiles, nt = tile % n_tiles;
       const int row0 = mt * 256 + (int)rank * 128 + q * 32;
-      const int ng = min(BOXES, max(0, (N - nt * BN + 63) / 64 - g0));  // groups of this warp inside N
+      const int ng = min(GPW, max(0, (N - nt * BN + 63) / 64 - g0));  // groups of this warp inside N
       if (lane == 0) {
         bulk_wait_read0();  // the previous tile's stores have left the boxes
         if (resid) {        // prefetch this warp's residual boxes while the MMAs run
@@ -720,8 +729,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       // per-row terms that do not depend on the accumulator, also before the wait
       const int row = row0 + lane;
       const bool row_ok = row < M;
-      const float rs = row_scale(ep, row, row_ok);
-      const bool special = (ep.flags & CC2_EPI_SPECIAL) && row_ok && (row % ep.sp_period) == ep.sp_offset;
+      const float rs = row_scale(ep, flags, row, row_ok);
+      const bool special = (flags & CC2_EPI_SPECIAL) && row_ok && (row % ep.sp_period) == ep.sp_offset;
       const bool rope_tile = ROPE && nt * BN + g0 * 64 < ep.rope_cols;
       uint32_t cs[ROPE ? 32 : 1];
       if constexpr (ROPE) {
@@ -733,9 +742,13 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       bool aborted = false;
-      for (int j = 0; j < ng; ++j) {
-        const uint32_t box = box0 + j * kEpiBox;
+      for (int j = 0; j < (SKIP_EPI ? 0 : ng); ++j) {
+        const uint32_t box = box0 + (j % BOXES) * kEpiBox;
         const int col0 = nt * BN + (g0 + j) * 64;
+        if (j >= BOXES) {  // reusing a box: its previous store must have read it
+          if (lane == 0) bulk_wait_read0();
+          __syncwarp();
+        }
         uint32_t r[64];
         tmem_ld32(tbase + (g0 + j) * 64, r);
         tmem_ld32(tbase + (g0 + j) * 64 + 32, r + 32);
@@ -748,8 +761,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             rsg = 1.0f;
           }
         }
-        const float ssq = epilogue_group(ep, r, rsg, special, col0, N, box, lane, resid);
-        if ((ep.flags & CC2_EPI_SSQ) && row_ok) ep.ssq_out[(size_t)(col0 >> 6) * ep.ssq_ld + row] = ssq;
+        const float ssq = epilogue_group(ep, flags, r, rsg, special, col0, N, box, lane, resid);
+        if ((flags & CC2_EPI_SSQ) && row_ok) ep.ssq_out[(size_t)(col0 >> 6) * ep.ssq_ld + row] = ssq;
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) {
@@ -839,16 +852,16 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMa
   return CC2_OK;
 }
 
-static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mr,
-                       int M, int N, int K, const Epi& ep, cudaStream_t st) {
+template <int F, int STAGES, int BOXES, bool SKIP_EPI = false>
+static int launch_pair_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mr,
+                         int M, int N, int K, const Epi& ep, cudaStream_t st) {
+  constexpr int SMEM = pair::smem_bytes<STAGES, BOXES>();
   static unsigned long long attr_set = 0;  // one bit per device
   int dev = 0;
   CC2_CUDA(cudaGetDevice(&dev));
   if (dev >= 64 || !((attr_set >> dev) & 1ull)) {
-    CC2_CUDA(cudaFuncSetAttribute(pair::gemm_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  pair::SMEM));
-    CC2_CUDA(cudaFuncSetAttribute(pair::gemm_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  pair::SMEM));
+    CC2_CUDA(cudaFuncSetAttribute(pair::gemm_pair_kernel<F, STAGES, BOXES, SKIP_EPI>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
     if (dev < 64) attr_set |= 1ull << dev;
   }
   const int tiles = ((M + 255) / 256) * ((N + pair::BN - 1) / pair::BN);
@@ -856,7 +869,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(pair::THREADS, 1, 1);
-  cfg.dynamicSmemBytes = pair::SMEM;
+  cfg.dynamicSmemBytes = SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -865,17 +878,45 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (ep.flags & CC2_EPI_ROPE)
-    CC2_CUDA(cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<true>, ma, mb, mc, mr, M, N, K, ep));
-  else
-    CC2_CUDA(cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<false>, ma, mb, mc, mr, M, N, K, ep));
+  CC2_CUDA(cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<F, STAGES, BOXES, SKIP_EPI>, ma, mb, mc, mr, M, N, K,
+                              ep));
   return CC2_OK;
+}
+
+static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mr,
+                       int M, int N, int K, const Epi& ep, cudaStream_t st, int variant) {
+  constexpr int RS = CC2_EPI_ROWSCALE, BI = CC2_EPI_BIAS, RL = CC2_EPI_RELU, RE = CC2_EPI_RESID,
+                SQ = CC2_EPI_SSQ, SP = CC2_EPI_SPECIAL, RP = CC2_EPI_ROPE;
+  if (variant == 3)  // measurement only: mainloop with the epilogue reduced to releasing TMEM (no output)
+    return launch_pair_t<0, 5, 2, true>(ma, mb, mc, mr, M, N, K, ep, st);
+#define CC2_PAIR(FL) \
+  case (FL): return launch_pair_t<(FL), 5, 2>(ma, mb, mc, mr, M, N, K, ep, st);
+  switch (ep.flags) {  // the epilogues the forward uses, specialised at compile time
+    CC2_PAIR(RS | RP)            // time-attention QKV (RMSNorm + RoPE)
+    CC2_PAIR(RS)                 // group QKV
+    CC2_PAIR(RS | RL)            // FFN up
+    CC2_PAIR(RE | SQ)            // O-projections, FFN down
+    CC2_PAIR(RS | RE | SQ)       // one-series group block
+    CC2_PAIR(BI | RL)            // ResidualBlock hidden
+    CC2_PAIR(BI | SQ | SP)       // input ResidualBlock output (+REG row)
+    CC2_PAIR(BI)                 // output ResidualBlock output
+    CC2_PAIR(0)                  // plain
+    default:
+      break;
+  }
+#undef CC2_PAIR
+  if (ep.flags & RP) {
+    set_error("gemm: CC2_EPI_ROPE is only supported with CC2_EPI_ROWSCALE alone");
+    return CC2_E_UNSUPPORTED;
+  }
+  return launch_pair_t<-1, 5, 2>(ma, mb, mc, mr, M, N, K, ep, st);
 }
 
 }  // namespace tc
 
-// 0: 2-SM tiles when M > 128 (default); 1: single-SM tiles only (kept for A/B
-// measurement through cc2_set_gemm_variant).
+// 0: 2-SM tiles when M > 128 (default); 1: single-SM tiles only; 3: 2-SM
+// mainloop with the epilogue skipped (measurement only, output not written).
+// Set through cc2_set_gemm_variant.
 int g_gemm_variant = 0;
 
 int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,
@@ -922,9 +963,9 @@ int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, in
   } else {
     mr = mc;
   }
-  if (g_gemm_variant == 0 && M > BM) {  // 2-SM tiles (256 x 256 per CTA pair)
+  if (g_gemm_variant != 1 && M > BM) {  // 2-SM tiles (256 x 256 per CTA pair)
     CC2_TRY(make_map(&mb, W, K, N, ldw, 128));
-    return launch_pair(ma, mb, mc, mr, M, N, K, ep, st);
+    return launch_pair(ma, mb, mc, mr, M, N, K, ep, st, g_gemm_variant);
   }
   const int tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
   if (N >= 256 && tiles256 >= num_sms()) {

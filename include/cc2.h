@@ -218,7 +218,8 @@ typedef struct {
 
 /* Tile variant of the bf16 GEMM: 0 (default) = 2-SM tcgen05 tiles of 256 x 256
  * per CTA pair when M > 128, else 1-SM 128 x 256 / 128 x 128 tiles; 1 = 1-SM
- * tiles only.  Process-wide; returns the previous value. */
+ * tiles only; 3 = measurement only: the 2-SM mainloop with the epilogue
+ * skipped (nothing is written).  Process-wide; returns the previous value. */
 CC2_API int cc2_set_gemm_variant(int variant);
 
 /* out[M, N] = epilogue(A[M, K] @ W[N, K]^T); A, W, out, resid of `dtype`,
