@@ -893,6 +893,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   case (FL): return launch_pair_t<(FL), 5, 2>(ma, mb, mc, mr, M, N, K, ep, st);
   switch (ep.flags) {  // the epilogues the forward uses, specialised at compile time
     CC2_PAIR(RS | RP)            // time-attention QKV (RMSNorm + RoPE)
+    CC2_PAIR(RP)                 // RoPE alone (component use)
     CC2_PAIR(RS)                 // group QKV
     CC2_PAIR(RS | RL)            // FFN up
     CC2_PAIR(RE | SQ)            // O-projections, FFN down
@@ -906,7 +907,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   }
 #undef CC2_PAIR
   if (ep.flags & RP) {
-    set_error("gemm: CC2_EPI_ROPE is only supported with CC2_EPI_ROWSCALE alone");
+    set_error("gemm: CC2_EPI_ROPE combines with CC2_EPI_ROWSCALE only");
     return CC2_E_UNSUPPORTED;
   }
   return launch_pair_t<-1, 5, 2>(ma, mb, mc, mr, M, N, K, ep, st);
