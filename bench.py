@@ -170,6 +170,65 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def graph_latency_ms(model, x, N, reps=50):
+    """p50 latency of one forward replayed from a CUDA graph (batch-1 serving)."""
+    model(x, num_output_patches=N)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        model(x, num_output_patches=N)
+        with torch.cuda.graph(g, stream=s):
+            model(x, num_output_patches=N)
+    torch.cuda.synchronize()
+    lats = []
+    for _ in range(reps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        b.synchronize()
+        lats.append(a.elapsed_time(b))
+    return statistics.median(lats)
+
+
+def forecasts_per_s(model, ctx, N, gid, flush, steps=5, warmup=2):
+    for _ in range(warmup):
+        model(ctx, num_output_patches=N, group_ids=gid)
+    torch.cuda.synchronize()
+    tot = 0.0
+    for i in range(steps):
+        flush.fill_(i & 0xFF)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        model(ctx, num_output_patches=N, group_ids=gid)
+        b.record()
+        b.synchronize()
+        tot += a.elapsed_time(b)
+    return ctx.shape[0] * steps / (tot / 1e3)
+
+
+def other_configs(model_bf16, dev, flush):
+    """The other BASELINE.json configs on one GPU (their own workloads; not the
+    headline line): configs[0] fp32 batch-1 latency (CUDA graph) and
+    forecasts/s for configs[2], [3], [4]."""
+    from cutechronos_b200.model import CuteChronos2Config, CuteChronos2Model
+    from cutechronos_b200.workloads import config0, config2, config3, config4, seeded_init_
+
+    out = {}
+    w0 = config0()
+    m32 = seeded_init_(CuteChronos2Model(CuteChronos2Config()), seed=0).to(dev, torch.float32).eval()
+    out["cfg0_b1_ctx512_f32_p50_ms"] = graph_latency_ms(m32, w0.context.to(dev), w0.num_output_patches)
+    del m32
+    torch.cuda.empty_cache()
+    for name, w in (("cfg2_g64x8_ctx2048", config2()), ("cfg3_b32_ctx8192", config3()),
+                    ("cfg4_b4096_ctx512", config4())):
+        out[name + "_forecasts_per_s"] = forecasts_per_s(model_bf16, w.context.to(dev), w.num_output_patches,
+                                                         w.group_ids, flush)
+    return out
+
+
 def run_b200(args):
     import torch.distributed as dist
 
@@ -259,26 +318,10 @@ def run_b200(args):
         # ---- p50 batch-1 latency (CUDA graph of one B=1 forward) ---------------
         lat_p50 = None
         if rank == 0 and not args.no_latency:
-            x1 = ctx[:1].clone()
-            model(x1, num_output_patches=N)
-            torch.cuda.synchronize()
-            g = torch.cuda.CUDAGraph()
-            s = torch.cuda.Stream()
-            s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s):
-                model(x1, num_output_patches=N)
-                with torch.cuda.graph(g, stream=s):
-                    model(x1, num_output_patches=N)
-            torch.cuda.synchronize()
-            lats = []
-            for _ in range(50):
-                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                a.record()
-                g.replay()
-                b.record()
-                b.synchronize()
-                lats.append(a.elapsed_time(b))
-            lat_p50 = statistics.median(lats)
+            lat_p50 = graph_latency_ms(model, ctx[:1].clone(), N)
+        other = None
+        if rank == 0 and not args.no_configs:
+            other = other_configs(model, dev, flush)
 
     # ---- roofline of the dominant kernel (tcgen05 GEMM), live from the timed region
     n = cnt.value
@@ -331,6 +374,7 @@ def run_b200(args):
             "model_flops_frac": value / world * gflop * 1e9 / (tf_sus * 1e12),
             "gflop_per_forecast": gflop,
             "latency_b1_p50_ms": lat_p50,
+            "other_configs": other,
             "kernels": kernels,
             "clocks": clk,
             "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads, "kind": "port",
@@ -413,6 +457,7 @@ def main():
     ap.add_argument("--batch", type=int, default=256)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-latency", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the configs[0,2,3,4] measurements")
     ap.add_argument("--micro", action="store_true", help="per-kernel micro-benchmark instead of the step")
     ap.add_argument("--only", default="", help="with --micro: run only cases whose name contains this")
     ap.add_argument("--gemm-variant", type=int, default=0, help="0: 2-SM GEMM tiles, 1: 1-SM tiles only, 3: mainloop only (no output)")

@@ -28,9 +28,10 @@
 //                     online softmax in fp32 (exp2 domain), P re-used from
 //                     registers as the A operand of P.V.  S x S never leaves
 //                     registers.
-//   attn_simt_kernel  float or bf16 storage, fp32 math on CUDA cores: used for
-//                     the fp32 model mode and for small groups (<= 32 members),
-//                     where a 64-row MMA tile would be mostly empty.
+//   attn_group_small_kernel  groups of <= 16 series: one CTA per (time step,
+//                     group) over all heads, CUDA cores, fp32 math.
+//   attn_simt_kernel  float or bf16 storage, fp32 math on CUDA cores: the fp32
+//                     time attention and groups of 17..32 series.
 #include "common.cuh"
 
 namespace cc2 {
@@ -571,6 +572,87 @@ attn_simt_kernel(const T* __restrict__ qkv, int ld, int qcol, int kcol, int vcol
   }
 }
 
+// ---------------------------------------------------------------------------
+// small groups (<= 16 series): one CTA per (time step, group) covering every
+// head.  The group's Q/K/V rows (contiguous, 3 x heads*64 elements each) are
+// staged in shared memory once; scores, softmax and P.V run on CUDA cores in
+// fp32.  Replaces a launch of (sets x heads) tiny CTAs.
+// ---------------------------------------------------------------------------
+constexpr int kSmallGroupMax = 16;
+
+template <typename T>
+__global__ void __launch_bounds__(256)
+attn_group_small_kernel(const T* __restrict__ qkv, int ld, int qcol, int kcol, int vcol, T* __restrict__ out,
+                        int ldo, const uint8_t* __restrict__ tok, SetInfo si, int heads) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const SetGeom g = set_geom(si, blockIdx.x);
+  const int n = g.n;
+  if (n <= 0) return;
+  const int HD = heads * DH;
+  T* Qs = reinterpret_cast<T*>(smem_raw);
+  T* Ks = Qs + (size_t)n * HD;
+  T* Vs = Ks + (size_t)n * HD;
+  float* P = reinterpret_cast<float*>(Vs + (size_t)n * HD);  // [heads][n][n]
+  float* kb = P + (size_t)heads * n * n;                     // [n]
+  const int tid = threadIdx.x;
+  constexpr int V = 16 / sizeof(T);  // elements per 16-byte vector
+  const int nvec = HD / V;
+  for (int idx = tid; idx < n * nvec; idx += blockDim.x) {
+    const int i = idx / nvec, c = (idx % nvec) * V;
+    const T* src = qkv + (size_t)g.row(i, si.S) * ld;
+    *reinterpret_cast<uint4*>(Qs + (size_t)i * HD + c) = *reinterpret_cast<const uint4*>(src + qcol + c);
+    *reinterpret_cast<uint4*>(Ks + (size_t)i * HD + c) = *reinterpret_cast<const uint4*>(src + kcol + c);
+    *reinterpret_cast<uint4*>(Vs + (size_t)i * HD + c) = *reinterpret_cast<const uint4*>(src + vcol + c);
+  }
+  for (int i = tid; i < n; i += blockDim.x) kb[i] = tok[g.row(i, si.S)] ? 0.0f : kMaskedScore;
+  __syncthreads();
+  // scores: one (head, query, key) dot product per thread iteration
+  for (int idx = tid; idx < heads * n * n; idx += blockDim.x) {
+    const int h = idx / (n * n), qi = (idx / n) % n, kj = idx % n;
+    const T* q = Qs + (size_t)qi * HD + h * DH;
+    const T* k = Ks + (size_t)kj * HD + h * DH;
+    float acc = 0.0f;
+#pragma unroll 16
+    for (int d = 0; d < DH; ++d) acc = fmaf(tof<T>(q[d]), tof<T>(k[d]), acc);
+    P[idx] = kb[kj] == 0.0f ? acc : kb[kj];
+  }
+  __syncthreads();
+  // softmax over the keys of each (head, query) row
+  for (int idx = tid; idx < heads * n; idx += blockDim.x) {
+    float* row = P + (size_t)idx * n;
+    float m = -INFINITY;
+    for (int j = 0; j < n; ++j) m = fmaxf(m, row[j]);
+    float sum = 0.0f;
+    for (int j = 0; j < n; ++j) {
+      const float e = expf(row[j] - m);
+      row[j] = e;
+      sum += e;
+    }
+    const float inv = 1.0f / sum;
+    for (int j = 0; j < n; ++j) row[j] *= inv;
+  }
+  __syncthreads();
+  // out[qi][c] = sum_j P[h][qi][j] V[j][c]
+  for (int idx = tid; idx < n * HD; idx += blockDim.x) {
+    const int qi = idx / HD, c = idx % HD, h = c / DH;
+    const float* prow = P + ((size_t)h * n + qi) * n;
+    float acc = 0.0f;
+    for (int j = 0; j < n; ++j) acc = fmaf(prow[j], tof<T>(Vs[(size_t)j * HD + c]), acc);
+    out[(size_t)g.row(qi, si.S) * ldo + c] = fromf<T>(acc);
+  }
+}
+
+inline size_t small_group_smem(int n, int heads, size_t esz) {
+  return 3 * (size_t)n * heads * DH * esz + ((size_t)heads * n * n + n) * sizeof(float);
+}
+
+template <typename T>
+int set_small_group_attr(size_t bytes) {
+  if (bytes <= 48 * 1024) return CC2_OK;
+  CC2_CUDA(cudaFuncSetAttribute(attn_group_small_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+  return CC2_OK;
+}
+
 }  // namespace
 
 int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int kcol, int vcol, void* out,
@@ -593,7 +675,12 @@ int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int
     const int rounds = (nqt + kSetMaxWarps - 1) / kSetMaxWarps;
     const int warps = (nqt + rounds - 1) / rounds;
     const size_t smem = set_kernel_smem(npad);
-    if (mode == 1 && max_group <= SK) {
+    if (mode == 1 && max_group <= kSmallGroupMax) {
+      const size_t sm = small_group_smem(max_group, heads, sizeof(bf16));
+      CC2_TRY(set_small_group_attr<bf16>(sm));
+      attn_group_small_kernel<bf16><<<num_sets, 256, sm, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out,
+                                                               ldo, tok, si, heads);
+    } else if (mode == 1 && max_group <= SK) {
       dim3 grid((nmax + SQ - 1) / SQ, heads, num_sets);
       attn_simt_kernel<bf16, false><<<grid, 128, 0, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out,
                                                           ldo, tok, cs, si);
@@ -624,6 +711,11 @@ int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int
         attn_mma_kernel<false><<<grid, 128, 0, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out, ldo,
                                                      tok, cs, si);
     }
+  } else if (dtype == CC2_F32 && mode == 1 && max_group <= kSmallGroupMax) {
+    const size_t sm = small_group_smem(max_group, heads, sizeof(float));
+    CC2_TRY(set_small_group_attr<float>(sm));
+    attn_group_small_kernel<float><<<num_sets, 256, sm, st>>>((const float*)qkv, ld, qcol, kcol, vcol, (float*)out,
+                                                              ldo, tok, si, heads);
   } else if (dtype == CC2_F32) {
     dim3 grid((nmax + SQ - 1) / SQ, heads, num_sets);
     if (mode == 0 && cs)

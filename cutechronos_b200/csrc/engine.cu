@@ -69,7 +69,7 @@ int launch_gemm_tc(const void*, int, const void*, int, void*, int, int, int, int
                    cudaStream_t);
 extern int g_gemm_variant;
 int launch_gemm_f32(const void*, int, const void*, int, void*, int, int, int, int, const cc2_epilogue*,
-                    cudaStream_t);
+                    cudaStream_t, float* scratch = nullptr, size_t scratch_floats = 0);
 int launch_attention(int, int, const void*, int, int, int, int, void*, int, const uint8_t*, int, int, int, int,
                      const int32_t*, const int32_t*, int, int, const float*, cudaStream_t);
 
@@ -294,6 +294,7 @@ size_t plan_pack(const cc2_config& c, int dtype, cc2_model* m, char* base) {
 struct Workspace {
   char* E; char* X; char* QKV; char* ATT; float* ssq; uint8_t* tok; float* loc; float* scale;
   int32_t* members; int32_t* offsets; char* O; char* PRED;
+  float* splitk; size_t splitk_floats;  // fp32 mode: K-slice partial sums of the small-M GEMMs
 };
 
 size_t plan_ws(const cc2_model& m, int B, int L, int N, Workspace* w, char* base) {
@@ -311,22 +312,34 @@ size_t plan_ws(const cc2_model& m, int B, int L, int N, Workspace* w, char* base
   size_t oSSQ = p.take(4 * M * groups * 2), oTOK = p.take(M);
   size_t oLOC = p.take(4 * B), oSC = p.take(4 * B), oMEM = p.take(4 * B), oOFF = p.take(4 * (B + 1));
   size_t oO = p.take(e * (size_t)B * N * m.kout), oPRED = p.take(e * (size_t)B * N * m.qps);
+  const size_t splitk_floats = m.dtype == CC2_F32 ? ((size_t)8 << 20) : 0;
+  size_t oSPLIT = p.take(4 * splitk_floats);
   if (w && base) {
     w->E = base + oE; w->X = base + oX; w->QKV = base + oQKV; w->ATT = base + oATT;
     w->ssq = (float*)(base + oSSQ); w->tok = (uint8_t*)(base + oTOK);
     w->loc = (float*)(base + oLOC); w->scale = (float*)(base + oSC);
     w->members = (int32_t*)(base + oMEM); w->offsets = (int32_t*)(base + oOFF);
     w->O = base + oO; w->PRED = base + oPRED;
+    w->splitk = (float*)(base + oSPLIT); w->splitk_floats = splitk_floats;
   }
   return p.off;
 }
+
+// fp32 split-K scratch of the forward being issued on this thread (null outside a forward)
+thread_local float* t_splitk = nullptr;
+thread_local size_t t_splitk_floats = 0;
 
 int gemm(int dtype, const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,
          const cc2_epilogue* e, cudaStream_t st) {
   ProfScope ps_(CC2_K_GEMM, 2.0 * M * N * K, 0.0, st);
   if (dtype == CC2_BF16) return launch_gemm_tc(A, lda, W, ldw, out, ldo, M, N, K, e, st);
-  return launch_gemm_f32(A, lda, W, ldw, out, ldo, M, N, K, e, st);
+  return launch_gemm_f32(A, lda, W, ldw, out, ldo, M, N, K, e, st, t_splitk, t_splitk_floats);
 }
+
+struct SplitKScope {
+  SplitKScope(float* p, size_t n) { t_splitk = p; t_splitk_floats = n; }
+  ~SplitKScope() { t_splitk = nullptr; t_splitk_floats = 0; }
+};
 
 cc2_epilogue epi(int flags) {
   cc2_epilogue e;
@@ -513,6 +526,7 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
   }
   Workspace w;
   plan_ws(*m, B, L, N, &w, (char*)workspace);
+  SplitKScope splitk_scope(w.splitk, w.splitk_floats);
   const int dt = m->dtype;
   const size_t e = m->esz;
   const int d = c.d_model, dff = c.d_ff, ps = c.input_patch_size;

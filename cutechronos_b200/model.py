@@ -248,7 +248,12 @@ class CuteChronos2Model(nn.Module):
         return self.shared.weight.device
 
     def _weights_key(self):
-        return tuple((p.data_ptr(), p._version, p.dtype) for p in self.parameters())
+        def version(p):
+            try:
+                return p._version
+            except RuntimeError:  # inference tensors carry no version counter
+                return -1
+        return tuple((p.data_ptr(), version(p), p.dtype) for p in self.parameters())
 
     def engine(self) -> _Engine:
         """The packed native model for the current parameters (re-packed when
