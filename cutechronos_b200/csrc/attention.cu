@@ -580,6 +580,31 @@ attn_simt_kernel(const T* __restrict__ qkv, int ld, int qcol, int kcol, int vcol
 // ---------------------------------------------------------------------------
 constexpr int kSmallGroupMax = 16;
 
+// 8 consecutive elements (16 bytes of bf16, 32 of float) <-> fp32 registers
+__device__ __forceinline__ void load8(const bf16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 f = __bfloat1622float2(h[e]);
+    v[2 * e] = f.x;
+    v[2 * e + 1] = f.y;
+  }
+}
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void store8(bf16* p, const float (&v)[8]) {
+  uint4 u;
+  u.x = pack2(v[0], v[1]); u.y = pack2(v[2], v[3]); u.z = pack2(v[4], v[5]); u.w = pack2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256)
 attn_group_small_kernel(const T* __restrict__ qkv, int ld, int qcol, int kcol, int vcol, T* __restrict__ out,
@@ -589,10 +614,11 @@ attn_group_small_kernel(const T* __restrict__ qkv, int ld, int qcol, int kcol, i
   const int n = g.n;
   if (n <= 0) return;
   const int HD = heads * DH;
+  const int HP = HD + 16 / (int)sizeof(T);  // staged row pitch: +16 bytes keeps rows on distinct banks
   T* Qs = reinterpret_cast<T*>(smem_raw);
-  T* Ks = Qs + (size_t)n * HD;
-  T* Vs = Ks + (size_t)n * HD;
-  float* P = reinterpret_cast<float*>(Vs + (size_t)n * HD);  // [heads][n][n]
+  T* Ks = Qs + (size_t)n * HP;
+  T* Vs = Ks + (size_t)n * HP;
+  float* P = reinterpret_cast<float*>(Vs + (size_t)n * HP);  // [heads][n][n]
   float* kb = P + (size_t)heads * n * n;                     // [n]
   const int tid = threadIdx.x;
   constexpr int V = 16 / sizeof(T);  // elements per 16-byte vector
@@ -600,20 +626,26 @@ attn_group_small_kernel(const T* __restrict__ qkv, int ld, int qcol, int kcol, i
   for (int idx = tid; idx < n * nvec; idx += blockDim.x) {
     const int i = idx / nvec, c = (idx % nvec) * V;
     const T* src = qkv + (size_t)g.row(i, si.S) * ld;
-    *reinterpret_cast<uint4*>(Qs + (size_t)i * HD + c) = *reinterpret_cast<const uint4*>(src + qcol + c);
-    *reinterpret_cast<uint4*>(Ks + (size_t)i * HD + c) = *reinterpret_cast<const uint4*>(src + kcol + c);
-    *reinterpret_cast<uint4*>(Vs + (size_t)i * HD + c) = *reinterpret_cast<const uint4*>(src + vcol + c);
+    *reinterpret_cast<uint4*>(Qs + (size_t)i * HP + c) = *reinterpret_cast<const uint4*>(src + qcol + c);
+    *reinterpret_cast<uint4*>(Ks + (size_t)i * HP + c) = *reinterpret_cast<const uint4*>(src + kcol + c);
+    *reinterpret_cast<uint4*>(Vs + (size_t)i * HP + c) = *reinterpret_cast<const uint4*>(src + vcol + c);
   }
   for (int i = tid; i < n; i += blockDim.x) kb[i] = tok[g.row(i, si.S)] ? 0.0f : kMaskedScore;
   __syncthreads();
-  // scores: one (head, query, key) dot product per thread iteration
+  // scores: one (head, query, key) dot product per thread iteration, 8 elements per 16-byte load
   for (int idx = tid; idx < heads * n * n; idx += blockDim.x) {
     const int h = idx / (n * n), qi = (idx / n) % n, kj = idx % n;
-    const T* q = Qs + (size_t)qi * HD + h * DH;
-    const T* k = Ks + (size_t)kj * HD + h * DH;
+    const T* q = Qs + (size_t)qi * HP + h * DH;
+    const T* k = Ks + (size_t)kj * HP + h * DH;
     float acc = 0.0f;
-#pragma unroll 16
-    for (int d = 0; d < DH; ++d) acc = fmaf(tof<T>(q[d]), tof<T>(k[d]), acc);
+#pragma unroll
+    for (int d = 0; d < DH; d += 8) {
+      float qa[8], ka[8];
+      load8(q + d, qa);
+      load8(k + d, ka);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc = fmaf(qa[e], ka[e], acc);
+    }
     P[idx] = kb[kj] == 0.0f ? acc : kb[kj];
   }
   __syncthreads();
@@ -632,18 +664,24 @@ attn_group_small_kernel(const T* __restrict__ qkv, int ld, int qcol, int kcol, i
     for (int j = 0; j < n; ++j) row[j] *= inv;
   }
   __syncthreads();
-  // out[qi][c] = sum_j P[h][qi][j] V[j][c]
-  for (int idx = tid; idx < n * HD; idx += blockDim.x) {
-    const int qi = idx / HD, c = idx % HD, h = c / DH;
+  // out[qi][c..c+7] = sum_j P[h][qi][j] V[j][c..c+7]
+  for (int idx = tid; idx < n * (HD / 8); idx += blockDim.x) {
+    const int qi = idx / (HD / 8), c = (idx % (HD / 8)) * 8, h = c / DH;
     const float* prow = P + ((size_t)h * n + qi) * n;
-    float acc = 0.0f;
-    for (int j = 0; j < n; ++j) acc = fmaf(prow[j], tof<T>(Vs[(size_t)j * HD + c]), acc);
-    out[(size_t)g.row(qi, si.S) * ldo + c] = fromf<T>(acc);
+    float acc[8] = {};
+    for (int j = 0; j < n; ++j) {
+      float va[8];
+      load8(Vs + (size_t)j * HP + c, va);
+      const float pj = prow[j];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = fmaf(pj, va[e], acc[e]);
+    }
+    store8(out + (size_t)g.row(qi, si.S) * ldo + c, acc);
   }
 }
 
 inline size_t small_group_smem(int n, int heads, size_t esz) {
-  return 3 * (size_t)n * heads * DH * esz + ((size_t)heads * n * n + n) * sizeof(float);
+  return 3 * (size_t)n * (heads * DH * esz + 16) + ((size_t)heads * n * n + n) * sizeof(float);
 }
 
 template <typename T>
