@@ -32,9 +32,26 @@
 //                     group) over all heads, CUDA cores, fp32 math.
 //   attn_simt_kernel  float or bf16 storage, fp32 math on CUDA cores: the fp32
 //                     time attention and groups of 17..32 series.
+#include <cuda.h>
+
 #include "common.cuh"
 
 namespace cc2 {
+
+int encode_bf16_map(CUtensorMap* map, const void* ptr, int cols, int rows, int ld, int box_cols, int box_rows);
+
+// Error word of the attention kernels' bounded waits (1 = a wait ran out).
+__device__ int g_attn_error = 0;
+
+int read_attention_error(int clear, int* value) {
+  CC2_CUDA(cudaMemcpyFromSymbol(value, g_attn_error, sizeof(int)));
+  if (clear) {
+    int z = 0;
+    CC2_CUDA(cudaMemcpyToSymbol(g_attn_error, &z, sizeof(int)));
+  }
+  return CC2_OK;
+}
+
 namespace {
 
 typedef __nv_bfloat16 bf16;
@@ -680,6 +697,255 @@ attn_group_small_kernel(const T* __restrict__ qkv, int ld, int qcol, int kcol, i
   }
 }
 
+// ---------------------------------------------------------------------------
+// persistent time attention (bf16, Q/K already rotated): one CTA of 16 warps
+// per SM walks its share of the (series, head) items.  Up to kPBufs items are
+// resident in shared memory; each is loaded by three TMA boxes (Q, K, V: the
+// item's rows x 64 columns, 128-byte swizzle) on an mbarrier.  Warps take
+// (item, 16-row query tile) units from a shared counter in order, so no warp
+// idles at an item boundary; the warp that finishes an item's last tile
+// refills that buffer with the item kBufs ahead (TMA + key mask), so loads
+// overlap compute.  A warp waiting for an item first waits until that item's
+// load has been issued (warps may run more than one buffer generation ahead
+// when an item has few tiles), then on the buffer's mbarrier.  All waits are
+// bounded.
+// ---------------------------------------------------------------------------
+constexpr int kPWarps = 16;
+constexpr int kPBufs = 4;
+constexpr size_t kPSmemLimit = 220 * 1024;
+
+__device__ __forceinline__ bool pmbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n\t.reg .pred p;\n\tmbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+               : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait (about 2 s); false when it ran out.
+__device__ __noinline__ bool pmbar_wait_slow(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t n = 1;; ++n) {
+    if (pmbar_try(bar, parity)) return true;
+    if ((n & 63u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+__device__ __forceinline__ bool pmbar_wait(uint32_t bar, uint32_t parity) {
+  return pmbar_try(bar, parity) || pmbar_wait_slow(bar, parity);
+}
+
+struct PersistArgs {
+  int S;          // tokens per series (= set size)
+  int npad;       // S rounded up to 16
+  int heads;
+  int items;      // B * heads
+  int qcol, kcol, vcol;
+  int box_rows;   // rows per TMA box (<= 256)
+  int nboxes;     // boxes per operand
+  int nbufs;
+  size_t buf_bytes;
+};
+
+__global__ void __launch_bounds__(kPWarps * 32, 1)
+attn_persist_kernel(const __grid_constant__ CUtensorMap tmQKV, bf16* __restrict__ out, int ldo,
+                    const uint8_t* __restrict__ tok, PersistArgs a, int* __restrict__ err) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  __shared__ __align__(8) uint64_t full_bar[kPBufs];
+  __shared__ int done[kPBufs];
+  __shared__ int next_unit;
+  __shared__ int failed;
+  // local item whose load was last issued into each buffer: a warp waits for
+  // its item's load to be issued before it waits on the buffer's mbarrier, so
+  // the parity it waits for always names that load's phase
+  __shared__ volatile int buf_item[kPBufs];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n = a.S, npad = a.npad;
+  const int nqt = (n + 15) / 16;
+  const int my_items = a.items > (int)blockIdx.x ? (a.items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int units = my_items * nqt;
+  auto buf_base = [&](int b) { return smem + (size_t)b * a.buf_bytes; };
+  auto kbias_of = [&](int b) { return reinterpret_cast<float*>(buf_base(b) + (size_t)3 * npad * 128); };
+  auto full_addr = [&](int b) { return (uint32_t)__cvta_generic_to_shared(&full_bar[b]); };
+
+  // issue the loads (and key mask) of local item li into its buffer; called by one full warp
+  auto issue = [&](int li) {
+    const int item = (int)blockIdx.x + li * (int)gridDim.x;
+    const int b = li % a.nbufs;
+    const int bser = item / a.heads, h = item % a.heads;
+    float* kb = kbias_of(b);
+    if (lane == 0) buf_item[b] = li;
+    for (int r = lane; r < npad; r += 32)
+      kb[r] = r < n ? (tok[(size_t)bser * n + r] ? 0.0f : kMaskedScore) : -INFINITY;
+    __syncwarp();
+    if (lane == 0) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      const uint32_t bar = full_addr(b);
+      const uint32_t bytes = (uint32_t)(3 * a.nboxes * a.box_rows * 128);
+      asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+      const uint32_t dst0 = (uint32_t)__cvta_generic_to_shared(buf_base(b));
+      const int cols[3] = {a.qcol + h * DH, a.kcol + h * DH, a.vcol + h * DH};
+      for (int t = 0; t < 3; ++t)
+        for (int x = 0; x < a.nboxes; ++x) {
+          const uint32_t dst = dst0 + (uint32_t)t * npad * 128 + (uint32_t)x * a.box_rows * 128;
+          asm volatile(
+              "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+              " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+              "l"((uint64_t)&tmQKV), "r"(bar), "r"(cols[t]), "r"(bser * n + x * a.box_rows)
+              : "memory");
+        }
+    }
+  };
+
+  if (tid == 0) {
+    for (int b = 0; b < kPBufs; ++b) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(full_addr(b)) : "memory");
+      done[b] = 0;
+      buf_item[b] = -1;
+    }
+    next_unit = 0;
+    failed = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  if (warp < a.nbufs && warp < my_items) issue(warp);
+
+  while (true) {
+    int u = 0;
+    if (lane == 0) u = atomicAdd(&next_unit, 1);
+    u = __shfl_sync(0xffffffffu, u, 0);
+    if (u >= units || failed) break;
+    const int li = u / nqt, qt = u % nqt;
+    const int b = li % a.nbufs;
+    bool issued = buf_item[b] == li;
+    if (!issued) {  // bounded spin until this item's load has been issued
+      const unsigned long long t0 = globaltimer_ns();
+      while (!(issued = buf_item[b] == li) && globaltimer_ns() - t0 < kWaitLimitNs) __nanosleep(64);
+    }
+    if (!issued || !pmbar_wait(full_addr(b), (uint32_t)(li / a.nbufs) & 1u)) {
+      if (lane == 0) {
+        failed = 1;
+        atomicOr(err, 1);
+      }
+      break;
+    }
+    const int item = (int)blockIdx.x + li * (int)gridDim.x;
+    const int bser = item / a.heads, h = item % a.heads;
+    const uint32_t qb = (uint32_t)__cvta_generic_to_shared(buf_base(b));
+    const uint32_t kb = qb + (uint32_t)npad * 128, vb = kb + (uint32_t)npad * 128;
+    const float* kbias = kbias_of(b);
+    const int q0 = qt * 16;
+
+    uint32_t qf[4][4];
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks)
+      ldsm_x4(swz(qb, q0 + (lane & 15), 2 * ks + (lane >> 4)), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
+    float o[8][4];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
+    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+    for (int k0 = 0; k0 < n; k0 += KT) {
+      const int kvalid = n - k0;
+      float s[8][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
+        if (nt * 8 < kvalid) {
+          const int kr = k0 + nt * 8 + (lane & 7);
+#pragma unroll
+          for (int ks = 0; ks < 4; ks += 2) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4(swz(kb, kr, 2 * ks + (lane >> 3)), b0, b1, b2, b3);
+            mma16816(s[nt], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], b0, b1);
+            mma16816(s[nt], qf[ks + 1][0], qf[ks + 1][1], qf[ks + 1][2], qf[ks + 1][3], b2, b3);
+          }
+        }
+      }
+      float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int c = nt * 8 + 2 * (lane & 3);
+        const float b0 = c < kvalid ? kbias[k0 + c] : -INFINITY;
+        const float b1 = c + 1 < kvalid ? kbias[k0 + c + 1] : -INFINITY;
+        s[nt][0] = b0 == 0.0f ? s[nt][0] * kLog2e : b0;
+        s[nt][1] = b1 == 0.0f ? s[nt][1] * kLog2e : b1;
+        s[nt][2] = b0 == 0.0f ? s[nt][2] * kLog2e : b0;
+        s[nt][3] = b1 == 0.0f ? s[nt][3] * kLog2e : b1;
+        mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
+        mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
+      }
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
+      const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
+      m0 = mn0; m1 = mn1;
+      l0 *= c0; l1 *= c1;
+#pragma unroll
+      for (int dt = 0; dt < 8; ++dt) { o[dt][0] *= c0; o[dt][1] *= c0; o[dt][2] *= c1; o[dt][3] *= c1; }
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        s[nt][0] = exp2f(s[nt][0] - mn0); s[nt][1] = exp2f(s[nt][1] - mn0);
+        s[nt][2] = exp2f(s[nt][2] - mn1); s[nt][3] = exp2f(s[nt][3] - mn1);
+        l0 += s[nt][0] + s[nt][1];
+        l1 += s[nt][2] + s[nt][3];
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (j * 16 < kvalid) {
+          const uint32_t a0 = pack2(s[2 * j][0], s[2 * j][1]);
+          const uint32_t a1 = pack2(s[2 * j][2], s[2 * j][3]);
+          const uint32_t a2 = pack2(s[2 * j + 1][0], s[2 * j + 1][1]);
+          const uint32_t a3 = pack2(s[2 * j + 1][2], s[2 * j + 1][3]);
+          const int vr = k0 + 16 * j + (lane & 15);
+#pragma unroll
+          for (int dt = 0; dt < 8; dt += 2) {
+            uint32_t b0, b1, b2, b3;
+            ldsm_x4_t(swz(vb, vr, dt + (lane >> 4)), b0, b1, b2, b3);
+            mma16816(o[dt], a0, a1, a2, a3, b0, b1);
+            mma16816(o[dt + 1], a0, a1, a2, a3, b2, b3);
+          }
+        }
+      }
+    }
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+    const float i0 = 1.0f / l0, i1 = 1.0f / l1;
+    // this warp's 16 rows of Q are no longer read by anyone: stage the output there
+    const int r0 = q0 + (lane >> 2);
+#pragma unroll
+    for (int dt = 0; dt < 8; ++dt) {
+      const uint32_t off = 4u * (lane & 3);
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(swz(qb, r0, dt) + off), "r"(pack2(o[dt][0] * i0, o[dt][1] * i0)));
+      asm volatile("st.shared.b32 [%0], %1;" ::"r"(swz(qb, r0 + 8, dt) + off), "r"(pack2(o[dt][2] * i1, o[dt][3] * i1)));
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int rr = q0 + (lane >> 3) + 4 * i, c = lane & 7;
+      if (rr < n) {
+        uint4 v;
+        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                     : "r"(swz(qb, rr, c)));
+        *reinterpret_cast<uint4*>(out + ((size_t)bser * n + rr) * ldo + h * DH + c * 8) = v;
+      }
+    }
+    __syncwarp();
+    // the warp that completes an item's last tile refills its buffer
+    int last = 0;
+    if (lane == 0) {
+      __threadfence_block();
+      last = atomicAdd(&done[b], 1) == nqt - 1;
+    }
+    last = __shfl_sync(0xffffffffu, last, 0);
+    if (last) {
+      if (lane == 0) done[b] = 0;
+      if (li + a.nbufs < my_items) issue(li + a.nbufs);
+    }
+  }
+}
+
 inline size_t small_group_smem(int n, int heads, size_t esz) {
   return 3 * (size_t)n * (heads * DH * esz + 16) + ((size_t)heads * n * n + n) * sizeof(float);
 }
@@ -713,7 +979,31 @@ int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int
     const int rounds = (nqt + kSetMaxWarps - 1) / kSetMaxWarps;
     const int warps = (nqt + rounds - 1) / rounds;
     const size_t smem = set_kernel_smem(npad);
-    if (mode == 1 && max_group <= kSmallGroupMax) {
+    // persistent TMA kernel: time mode with RoPE already applied (the forward's case)
+    const int nbox = (S + 255) / 256;
+    const int npad_t = (S + 16 * nbox - 1) / (16 * nbox) * (16 * nbox);
+    const size_t pbuf = align_up((size_t)npad_t * (3 * 128 + sizeof(float)), 1024);
+    const int pbufs = (int)std::min<size_t>(kPBufs, kPSmemLimit / pbuf);
+    const bool aligned = ((uintptr_t)qkv & 15u) == 0 && (ld * 2) % 16 == 0;
+    // (sets of fewer than 8 query tiles run faster in the whole-set kernel below)
+    if (mode == 0 && !cs && pbufs >= 1 && aligned && (S + 15) / 16 >= 8) {
+      CUtensorMap map;
+      CC2_TRY(encode_bf16_map(&map, qkv, ld, num_sets * S, ld, 64, npad_t / nbox));
+      PersistArgs pa{S, npad_t, heads, num_sets * heads, qcol, kcol, vcol, npad_t / nbox, nbox, pbufs, pbuf};
+      const size_t smem_p = (size_t)pbufs * pbuf + 1024;
+      static unsigned long long attr_p = 0;  // one bit per device
+      int dev = 0;
+      CC2_CUDA(cudaGetDevice(&dev));
+      if (dev >= 64 || !((attr_p >> dev) & 1ull)) {
+        CC2_CUDA(cudaFuncSetAttribute(attn_persist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)(kPSmemLimit + 1024)));
+        if (dev < 64) attr_p |= 1ull << dev;
+      }
+      int* err = nullptr;
+      CC2_CUDA(cudaGetSymbolAddress((void**)&err, g_attn_error));
+      const int grid = std::min(num_sets * heads, num_sms());
+      attn_persist_kernel<<<grid, kPWarps * 32, smem_p, st>>>(map, (bf16*)out, ldo, tok, pa, err);
+    } else if (mode == 1 && max_group <= kSmallGroupMax) {
       const size_t sm = small_group_smem(max_group, heads, sizeof(bf16));
       CC2_TRY(set_small_group_attr<bf16>(sm));
       attn_group_small_kernel<bf16><<<num_sets, 256, sm, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out,

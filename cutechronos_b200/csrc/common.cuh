@@ -56,9 +56,11 @@ int num_sms();
 // Bit flags written by kernels whose bounded waits gave up.
 enum : int {
   DEV_ERR_GEMM_TIMEOUT = 1,
+  DEV_ERR_ATTN_TIMEOUT = 2,
 };
-// Reads (and optionally clears) the device error word of the current device.
+// Read (and optionally clear) the device error words of the current device.
 int read_device_error(int clear, int* value);
+int read_attention_error(int clear, int* value);
 
 // Wall-clock limit for any spin-wait inside a kernel (nanoseconds).
 constexpr unsigned long long kWaitLimitNs = 2000ull * 1000ull * 1000ull;

@@ -364,9 +364,10 @@ const char* cc2_version(void) { return "cc2-b200 0.1 (sm_100a)"; }
 int cc2_device_status(int clear) {
   clear_error();
   CC2_CUDA(cudaDeviceSynchronize());
-  int v = 0;
+  int v = 0, a = 0;
   CC2_TRY(read_device_error(clear, &v));
-  return v;
+  CC2_TRY(read_attention_error(clear, &a));
+  return v | (a ? DEV_ERR_ATTN_TIMEOUT : 0);
 }
 
 int cc2_model_pack_bytes(const cc2_config* cfg, int dtype, size_t* bytes) {

@@ -915,6 +915,11 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
 
 }  // namespace tc
 
+// bf16 2-D tensor map with 128-byte swizzle (shared with the attention kernels).
+int encode_bf16_map(CUtensorMap* map, const void* ptr, int cols, int rows, int ld, int box_cols, int box_rows) {
+  return tc::make_map_box(map, ptr, cols, rows, ld, box_cols, box_rows);
+}
+
 // 0: 2-SM tiles when M > 128 (default); 1: single-SM tiles only; 3: 2-SM
 // mainloop with the epilogue skipped (measurement only, output not written).
 // Set through cc2_set_gemm_variant.

@@ -227,7 +227,9 @@ def _rope_ref(q, k, S):
     return q * c + orc._rotate_half(q) * s, k * c + orc._rotate_half(k) * s
 
 
-@pytest.mark.parametrize("B,S", [(1, 37), (4, 133), (2, 521), (3, 64)])
+# (256, 37) and (24, 521): many items per CTA in the persistent kernel (buffer reloads,
+# few query tiles per item; a single buffer for long sets)
+@pytest.mark.parametrize("B,S", [(1, 37), (4, 133), (2, 521), (3, 64), (256, 37), (24, 521)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("rope", [True, False])
 def test_time_attention(B, S, dtype, rope):
