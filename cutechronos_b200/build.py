@@ -1,6 +1,7 @@
 """Build the in-tree shared library ``cutechronos_b200/_lib/libcc2_b200.so``.
 
-Compiles every ``csrc/*.cu`` for sm_100a with nvcc (cross-compiles without a
+Compiles every ``csrc/*.cu`` for sm_100a with nvcc (and the host-only
+``csrc/*.cpp``, the native bridge) (cross-compiles without a
 GPU) and links a C-ABI shared library.  Usage: ``python -m cutechronos_b200.build``.
 """
 
@@ -30,14 +31,14 @@ def nvcc() -> str:
 
 
 def sources() -> list[Path]:
-    return sorted(CSRC.glob("*.cu"))
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cpp"))
 
 
 def _stale() -> bool:
     if not LIB.exists():
         return True
     t = LIB.stat().st_mtime
-    deps = sources() + sorted(CSRC.glob("*.cuh")) + [PKG.parent / "include" / "cc2.h", Path(__file__)]
+    deps = sources() + sorted(CSRC.glob("*.cuh")) + sorted((PKG.parent / "include").glob("*.h")) + [Path(__file__)]
     return any(p.stat().st_mtime > t for p in deps if p.exists())
 
 

@@ -71,3 +71,41 @@ def case_inputs(c):
     mask = torch.from_numpy(c["context_mask"]) if "context_mask" in c else None
     gid = torch.from_numpy(c["group_ids"]) if "group_ids" in c else None
     return ctx, mask, int(c["N"]), gid
+
+
+def hf_state_dict(model) -> dict:
+    """The HuggingFace Chronos-2 key layout of a CuteChronos2Model's weights."""
+    sd = {"shared.weight": model.shared.weight, "encoder.final_layer_norm.weight": model.final_layer_norm_weight}
+    for name in ("input_patch_embedding", "output_patch_embedding"):
+        for layer in ("hidden_layer", "output_layer", "residual_layer"):
+            for prm in ("weight", "bias"):
+                sd[f"{name}.{layer}.{prm}"] = getattr(getattr(getattr(model, name), layer), prm)
+    for i, b in enumerate(model.blocks):
+        pre = f"encoder.block.{i}.layer"
+        for j, att in ((0, b.time_attn), (1, b.group_attn)):
+            sd[f"{pre}.{j}.layer_norm.weight"] = att.layer_norm_weight
+            for prj in "qkvo":
+                sd[f"{pre}.{j}.self_attention.{prj}.weight"] = getattr(att, prj).weight
+        sd[f"{pre}.2.layer_norm.weight"] = b.feed_forward.layer_norm_weight
+        sd[f"{pre}.2.mlp.wi.weight"] = b.feed_forward.wi.weight
+        sd[f"{pre}.2.mlp.wo.weight"] = b.feed_forward.wo.weight
+    return {k: v.detach().contiguous() for k, v in sd.items()}
+
+
+def write_checkpoint(model, path, dtype=torch.float32) -> None:
+    """config.json + model.safetensors of a CuteChronos2Model, as a HF checkpoint directory."""
+    from safetensors.torch import save_file
+    path = Path(path)
+    path.mkdir(parents=True, exist_ok=True)
+    cfg = model.config
+    save_file({k: v.to(dtype) for k, v in hf_state_dict(model).items()}, str(path / "model.safetensors"))
+    (path / "config.json").write_text(json.dumps({
+        "d_model": cfg.d_model, "d_kv": cfg.d_kv, "d_ff": cfg.d_ff, "num_layers": cfg.num_layers,
+        "num_heads": cfg.num_heads, "layer_norm_epsilon": cfg.layer_norm_epsilon, "rope_theta": cfg.rope_theta,
+        "dense_act_fn": "relu", "vocab_size": cfg.vocab_size, "reg_token_id": cfg.reg_token_id,
+        "chronos_config": {"context_length": cfg.context_length, "input_patch_size": cfg.input_patch_size,
+                           "input_patch_stride": cfg.input_patch_stride,
+                           "output_patch_size": cfg.output_patch_size, "quantiles": list(cfg.quantiles),
+                           "use_reg_token": cfg.use_reg_token, "use_arcsinh": cfg.use_arcsinh,
+                           "time_encoding_scale": cfg.time_encoding_scale,
+                           "max_output_patches": cfg.max_output_patches}}, indent=1))

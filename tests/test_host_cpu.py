@@ -11,7 +11,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-from conftest import small_config
+from conftest import hf_state_dict, small_config
 from cutechronos_b200.model import CuteChronos2Model
 from cutechronos_b200.pipeline import CuteChronos2Pipeline, _select_quantiles
 from cutechronos_b200.sharding import gather_forecasts, partition_groups
@@ -112,20 +112,7 @@ def test_checkpoint_and_lora_loading(tmp_path):
     sf = pytest.importorskip("safetensors.torch")
     cfg = small_config()
     src = seeded_init_(CuteChronos2Model(cfg), seed=3)
-    sd = {"shared.weight": src.shared.weight, "encoder.final_layer_norm.weight": src.final_layer_norm_weight}
-    for name in ("input_patch_embedding", "output_patch_embedding"):
-        for layer in ("hidden_layer", "output_layer", "residual_layer"):
-            for prm in ("weight", "bias"):
-                sd[f"{name}.{layer}.{prm}"] = getattr(getattr(getattr(src, name), layer), prm)
-    for i, b in enumerate(src.blocks):
-        pre = f"encoder.block.{i}.layer"
-        for j, att in ((0, b.time_attn), (1, b.group_attn)):
-            sd[f"{pre}.{j}.layer_norm.weight"] = att.layer_norm_weight
-            for prj in "qkvo":
-                sd[f"{pre}.{j}.self_attention.{prj}.weight"] = getattr(att, prj).weight
-        sd[f"{pre}.2.layer_norm.weight"] = b.feed_forward.layer_norm_weight
-        sd[f"{pre}.2.mlp.wi.weight"] = b.feed_forward.wi.weight
-        sd[f"{pre}.2.mlp.wo.weight"] = b.feed_forward.wo.weight
+    sd = hf_state_dict(src)
     sf.save_file({k: v.detach().contiguous() for k, v in sd.items()}, str(tmp_path / "model.safetensors"))
     (tmp_path / "config.json").write_text(json.dumps({
         "d_model": cfg.d_model, "d_kv": cfg.d_kv, "d_ff": cfg.d_ff, "num_layers": cfg.num_layers,
