@@ -36,6 +36,7 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
+import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 METRIC = "forecasts/sec/GPU, Chronos-2-base shape ctx2048 bf16; p50 batch-1 latency"
@@ -229,6 +230,40 @@ def other_configs(model_bf16, dev, flush):
     return out
 
 
+def pipeline_rates(model_bf16, dev, steps=3, warmup=1):
+    """The user-facing pipeline on configs[1] inputs, host to host, wall clock
+    around synchronised calls: predict_quantiles on a list of 256 CPU series
+    (default levels) and predict_df on the same series as a long DataFrame."""
+    import pandas as pd
+
+    from cutechronos_b200.pipeline import CuteChronos2Pipeline
+    from cutechronos_b200.workloads import series_cfg1
+
+    pipe = CuteChronos2Pipeline(model_bf16, device=str(dev))
+    x = series_cfg1(256, 2048, 1)
+    series = list(x.unbind(0))
+    n, L = x.shape
+    df = pd.DataFrame({"item_id": np.repeat(np.arange(n), L), "timestamp": np.tile(np.arange(L), n),
+                       "target": x.reshape(-1).numpy()})
+
+    def rate(fn):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            fn()
+        torch.cuda.synchronize()
+        return n * steps / (time.perf_counter() - t0)
+
+    return {
+        "predict_quantiles_list_forecasts_per_s": rate(
+            lambda: pipe.predict_quantiles(series, prediction_length=64)),
+        "predict_df_forecasts_per_s": rate(
+            lambda: pipe.predict_df(df, prediction_length=64, quantile_levels=[0.1, 0.5, 0.9])),
+    }
+
+
 def run_b200(args):
     import torch.distributed as dist
 
@@ -319,9 +354,10 @@ def run_b200(args):
         lat_p50 = None
         if rank == 0 and not args.no_latency:
             lat_p50 = graph_latency_ms(model, ctx[:1].clone(), N)
-        other = None
+        other = pipe_rates = None
         if rank == 0 and not args.no_configs:
             other = other_configs(model, dev, flush)
+            pipe_rates = pipeline_rates(model, dev)
 
     # ---- roofline of the dominant kernel (tcgen05 GEMM), live from the timed region
     n = cnt.value
@@ -375,6 +411,7 @@ def run_b200(args):
             "gflop_per_forecast": gflop,
             "latency_b1_p50_ms": lat_p50,
             "other_configs": other,
+            "pipeline": pipe_rates,
             "kernels": kernels,
             "clocks": clk,
             "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads, "kind": "port",

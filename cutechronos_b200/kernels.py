@@ -246,3 +246,62 @@ def group_attention(qkv: torch.Tensor, token_mask: torch.Tensor, group_ids: torc
                                 tok.data_ptr(), S * ng.value, S, num_heads, HD // num_heads, mem_t.data_ptr(),
                                 off_t.data_ptr(), ng.value, mg.value, None, _stream(qkv)), "cc2_attention")
     return out.reshape(B, S, HD)
+
+
+def stack_series(values: torch.Tensor, offsets: torch.Tensor, L: int) -> torch.Tensor:
+    """Ragged series -> (B, L) float32, right-aligned, NaN-left-padded, each
+    row's last L values kept (pipeline.py:221-243).  values (T,) float32 and
+    offsets (B+1,) int64 on the device."""
+    _cuda(values, offsets)
+    B = offsets.numel() - 1
+    out = torch.empty(B, L, dtype=torch.float32, device=values.device)
+    nat.check(nat.load().cc2_stack_series(values.data_ptr(), offsets.data_ptr(), B, L, out.data_ptr(),
+                                          _stream(values)), "cc2_stack_series")
+    return out
+
+
+def quantile_table(training_quantiles: list[float], levels: list[float]):
+    """Per requested level: (lo, hi, w_lo, w_hi) as the reference's
+    _select_quantiles (pipeline.py:24-58) picks them: a trained level is
+    gathered (lo == hi); another level interpolates between the trained
+    neighbours found by searchsorted (clamped to [1, Q-1]) with weights
+    1 - frac and frac rounded to fp32."""
+    index = {q: i for i, q in enumerate(training_quantiles)}
+    tq = torch.tensor(training_quantiles, dtype=torch.float32)
+    lo, hi, wl, wh = [], [], [], []
+    for ql in levels:
+        di = index.get(ql)
+        if di is not None:
+            lo.append(di), hi.append(di), wl.append(1.0), wh.append(0.0)
+            continue
+        h = int(torch.searchsorted(tq, torch.tensor(ql, dtype=torch.float32)).clamp(1, len(tq) - 1))
+        frac = (ql - tq[h - 1].item()) / max(tq[h].item() - tq[h - 1].item(), 1e-9)
+        lo.append(h - 1), hi.append(h), wl.append(1 - frac), wh.append(frac)
+    return lo, hi, wl, wh
+
+
+def select_quantiles(preds: torch.Tensor, H: int, training_quantiles: list[float], levels: list[float], *,
+                     layout: int = 1, median_level: int | None = None, out: torch.Tensor | None = None):
+    """preds (B, Q, ld) -> float32 levels: layout 0 (B, nq, H), layout 1
+    (B, H, nq); with ``median_level`` also the gathered (B, H) row of that
+    trained level.  ``out`` (optional) is a flat float32 device buffer that
+    receives the levels followed by the median."""
+    _cuda(preds)
+    B, Q, ld = preds.shape
+    if preds.stride(2) != 1 or preds.stride(1) != ld or preds.stride(0) != Q * ld:
+        preds = preds.contiguous()
+    nq = len(levels)
+    lo, hi, wl, wh = quantile_table(training_quantiles, levels)
+    n_lv, n_med = B * H * nq, (B * H if median_level is not None else 0)
+    if out is None:
+        out = torch.empty(n_lv + n_med, dtype=torch.float32, device=preds.device)
+    ai = C.c_int * max(nq, 1)
+    af = C.c_float * max(nq, 1)
+    med_ptr = out.data_ptr() + 4 * n_lv if median_level is not None else None
+    nat.check(nat.load().cc2_select_quantiles(
+        _code(preds.dtype), preds.data_ptr(), B, Q, ld, H, nq, ai(*lo), ai(*hi), af(*wl), af(*wh), layout,
+        out.data_ptr(), median_level if median_level is not None else 0, med_ptr, _stream(preds)),
+        "cc2_select_quantiles")
+    shape = (B, nq, H) if layout == 0 else (B, H, nq)
+    lv = out[:n_lv].view(shape)
+    return (lv, out[n_lv:n_lv + n_med].view(B, H)) if median_level is not None else lv

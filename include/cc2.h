@@ -254,6 +254,26 @@ CC2_API int cc2_output_transform(int dtype, const void* preds, int ld_preds, con
                          const float* scale, void* out, int B, int N, int Q, int ps,
                          int use_arcsinh, void* stream);
 
+/* ------------------------------------------------------------------------ */
+/* Pipeline steps on the device (pipeline.py:221-322, 24-58).                 */
+/* ------------------------------------------------------------------------ */
+/* Ragged series -> (B, L) batch: row b is values[offsets[b] .. offsets[b+1])
+ * (dev float32, dev int64 offsets, B+1 entries), its last L values
+ * right-aligned, NaN before them (_left_pad_and_stack_rows, pipeline.py:221-231;
+ * truncation of _finalize_context_batch, :239-243).  out (dev) float32 (B, L). */
+CC2_API int cc2_stack_series(const float* values, const int64_t* offsets, int B, int L, float* out,
+                             void* stream);
+
+/* Quantile levels of forecasts (_select_quantiles, pipeline.py:24-58).
+ *   preds  (dev) dtype (B, Q, ld); the first H columns of each row are used
+ *   level j (nq <= 64; host arrays): lo[j] == hi[j] gathers trained level
+ *          lo[j]; otherwise fl(fl(a_lo * w_lo[j]) + fl(a_hi * w_hi[j]))
+ *   layout 0: out (dev) float32 (B, nq, H); 1: out (B, H, nq)
+ *   median (dev) float32 (B, H) or NULL: trained level median_q, gathered. */
+CC2_API int cc2_select_quantiles(int dtype, const void* preds, int B, int Q, int ld, int H, int nq,
+                                 const int* lo, const int* hi, const float* w_lo, const float* w_hi,
+                                 int layout, float* out, int median_q, float* median, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

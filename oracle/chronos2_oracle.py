@@ -305,3 +305,41 @@ def forecast_flops(S: int, P: int, N: int, d=768, dff=3072, layers=12, g=1, out_
 def num_patches(cfg: OracleConfig, L: int) -> int:
     L = min(L, cfg.context_length)
     return math.ceil(L / cfg.input_patch_size)
+
+
+# ---- pipeline host steps around the forward ---------------------------------------------------
+def left_pad_and_stack(values: torch.Tensor, lens, context_length: int) -> torch.Tensor:
+    """Ragged series (concatenated in ``values``, lengths ``lens``) -> (B, L)
+    float32, each row right-aligned and NaN-left-padded to the longest row,
+    then cut to the last ``context_length`` steps
+    (cutechronos/pipeline.py:221-231 _left_pad_and_stack_rows, 239-243
+    _finalize_context_batch)."""
+    lens = [int(n) for n in lens]
+    n = max(lens)
+    out = torch.full((len(lens), n), float("nan"), dtype=torch.float32)
+    pos = 0
+    for i, k in enumerate(lens):
+        if k:
+            out[i, n - k:] = values[pos:pos + k]
+        pos += k
+    return out[:, -context_length:] if n > context_length else out
+
+
+def select_quantiles(preds: torch.Tensor, training_quantiles, requested_quantiles) -> torch.Tensor:
+    """(B, Q, H) float32 -> (B, H, len(requested)): a trained level is
+    gathered; another level is ``a * (1 - frac) + b * frac`` between the
+    trained neighbours found by searchsorted, clamped to [1, Q-1]
+    (cutechronos/pipeline.py:24-58)."""
+    bhq = preds.float().permute(0, 2, 1)
+    tq = torch.tensor(training_quantiles, dtype=torch.float32)
+    cols = []
+    for ql in requested_quantiles:
+        ql = float(ql)
+        if ql in training_quantiles:
+            cols.append(bhq[..., list(training_quantiles).index(ql)])
+            continue
+        hi = int(torch.searchsorted(tq, torch.tensor(ql, dtype=torch.float32)).clamp(1, len(tq) - 1))
+        lo = hi - 1
+        frac = (ql - tq[lo].item()) / max(tq[hi].item() - tq[lo].item(), 1e-9)
+        cols.append(bhq[..., lo] * (1 - frac) + bhq[..., hi] * frac)
+    return torch.stack(cols, dim=-1)

@@ -16,6 +16,7 @@ from cutechronos_b200.model import CuteChronos2Model
 from cutechronos_b200.pipeline import CuteChronos2Pipeline, _select_quantiles
 from cutechronos_b200.sharding import gather_forecasts, partition_groups
 from cutechronos_b200.workloads import CONFIGS, config2, config3, seeded_init_
+from oracle import chronos2_oracle as orc
 
 
 class FakeModel:
@@ -31,74 +32,89 @@ class FakeModel:
         self.calls.append((ctx.shape[0], group_ids.clone() if group_ids is not None else None))
         B = ctx.shape[0]
         last = torch.nan_to_num(ctx, nan=0.0).sum(-1)
-        gid = group_ids if group_ids is not None else torch.arange(B)
+        gid = (group_ids if group_ids is not None else torch.arange(B)).to(ctx.device)
         gmean = torch.stack([last[gid == g].mean() for g in gid])
         H = 16 * num_output_patches
-        q = torch.arange(21, dtype=torch.float32).view(1, 21, 1)
-        h = torch.arange(H, dtype=torch.float32).view(1, 1, H)
+        q = torch.arange(21, dtype=torch.float32, device=ctx.device).view(1, 21, 1)
+        h = torch.arange(H, dtype=torch.float32, device=ctx.device).view(1, 1, H)
         return (last.view(B, 1, 1) + 0.01 * gmean.view(B, 1, 1) + q + 0.1 * h)
 
 
-def pipe():
-    return CuteChronos2Pipeline(FakeModel(), device="cpu")
+def pipe(device="cpu"):
+    return CuteChronos2Pipeline(FakeModel(), device=device)
 
 
-def test_prepare_context_shapes_and_groups():
+def test_plan_context_shapes_and_groups():
     p = pipe()
-    ctx, gid, rng = p._prepare_context(torch.randn(5))
-    assert ctx.shape == (1, 5) and gid.tolist() == [0] and rng == [(0, 1)]
-    ctx, gid, rng = p._prepare_context(torch.randn(3, 7))
+    rows, gid, rng = p._plan_context(torch.randn(5))
+    assert rows.shape == (1, 5) and gid.tolist() == [0] and rng == [(0, 1)]
+    rows, gid, rng = p._plan_context(torch.randn(3, 7))
     assert gid.tolist() == [0, 1, 2] and rng == [(0, 1), (1, 2), (2, 3)]
-    ctx, gid, rng = p._prepare_context(torch.randn(2, 4, 9))
-    assert ctx.shape == (8, 9) and gid.tolist() == [0] * 4 + [1] * 4 and rng == [(0, 4), (4, 8)]
-    ctx, gid, rng = p._prepare_context([torch.randn(3), torch.randn(2, 5)])
-    assert ctx.shape == (3, 5) and gid.tolist() == [0, 1, 1]
-    assert torch.isnan(ctx[0, :2]).all() and not torch.isnan(ctx[0, 2:]).any()  # left padding
+    rows, gid, rng = p._plan_context(torch.randn(2, 4, 9))
+    assert rows.shape == (8, 9) and gid.tolist() == [0] * 4 + [1] * 4 and rng == [(0, 4), (4, 8)]
+    a, b = torch.randn(3), torch.randn(2, 5)
+    rows, gid, rng = p._plan_context([a, b])
+    assert [r.shape[-1] for r in rows] == [3, 5, 5] and gid.tolist() == [0, 1, 1] and rng == [(0, 1), (1, 3)]
+    assert torch.equal(rows[0], a) and torch.equal(rows[2], b[1])
     with pytest.raises(NotImplementedError):
-        p._prepare_context([{"target": torch.randn(4)}])
+        p._plan_context([{"target": torch.randn(4)}])
     with pytest.raises(ValueError):
-        p._prepare_context(torch.randn(2, 2, 2, 2))
+        p._plan_context(torch.randn(2, 2, 2, 2))
+    with pytest.raises(ValueError):
+        p._plan_context([torch.randn(2, 2, 2)])
 
 
 def test_truncation_to_model_context_length():
-    p = pipe()
-    ctx, _, _ = p._prepare_context(torch.arange(600, dtype=torch.float32))
-    assert ctx.shape == (1, 512) and ctx[0, 0].item() == 88.0
-
-
-def test_predict_chunking_equals_single_batch():
-    x = torch.randn(10, 40)
-    a = pipe().predict(x, prediction_length=20)
-    b = pipe().predict(x, prediction_length=20, batch_size=3)
-    assert len(a) == 10 and a[0].shape == (1, 21, 20)
-    for u, v in zip(a, b):
-        assert torch.allclose(u, v)
-
-
-def test_cross_learning_uses_one_group_and_disables_chunking():
-    p = pipe()
-    p.predict(torch.randn(6, 30), prediction_length=16, cross_learning=True, batch_size=2)
-    assert len(p.model.calls) == 1 and p.model.calls[0][1].tolist() == [0] * 6
+    rows, _, _ = pipe()._plan_context(torch.arange(600, dtype=torch.float32))
+    assert rows.shape == (1, 512) and rows[0, 0].item() == 88.0
 
 
 def test_prediction_length_limit():
     p = pipe()
-    with pytest.raises(ValueError):
+    with pytest.raises(ValueError, match="Set limit_prediction_length=False"):
         p.predict(torch.randn(1, 30), prediction_length=64 * 16 + 1)
+    with pytest.raises(ValueError, match="Set limit_prediction_length=False"):
+        p.predict_quantiles(torch.randn(1, 30), prediction_length=64 * 16 + 1)
 
 
-def test_select_quantiles_gather_and_interpolate():
+def test_oracle_select_quantiles_known_answers():
     tq = [0.1, 0.5, 0.9]
     preds = torch.tensor([[[1.0, 2.0], [3.0, 4.0], [5.0, 8.0]]])  # (1, Q=3, H=2)
-    out = _select_quantiles(preds, tq, [0.5, 0.1])
-    assert out.tolist() == [[[3.0, 1.0], [4.0, 2.0]]]
-    out = _select_quantiles(preds, tq, [0.3, 0.7])
+    assert orc.select_quantiles(preds, tq, [0.5, 0.1]).tolist() == [[[3.0, 1.0], [4.0, 2.0]]]
+    out = orc.select_quantiles(preds, tq, [0.3, 0.7])
     assert torch.allclose(out, torch.tensor([[[2.0, 4.0], [3.0, 6.0]]]))
 
 
+# The same host logic through the device kernels (stack_series, select_quantiles).
+@pytest.mark.gpu
+def test_predict_chunking_equals_single_batch():
+    x = torch.randn(10, 40)
+    a = pipe("cuda").predict(x, prediction_length=20)
+    b = pipe("cuda").predict(x, prediction_length=20, batch_size=3)
+    assert len(a) == 10 and a[0].shape == (1, 21, 20) and a[0].device.type == "cpu"
+    for u, v in zip(a, b):
+        assert torch.allclose(u, v)
+
+
+@pytest.mark.gpu
+def test_cross_learning_uses_one_group_and_disables_chunking():
+    p = pipe("cuda")
+    p.predict(torch.randn(6, 30), prediction_length=16, cross_learning=True, batch_size=2)
+    assert len(p.model.calls) == 1 and p.model.calls[0][1].tolist() == [0] * 6
+
+
+@pytest.mark.gpu
+def test_select_quantiles_gather_and_interpolate():
+    tq = [0.1, 0.5, 0.9]
+    preds = torch.tensor([[[1.0, 2.0], [3.0, 4.0], [5.0, 8.0]]])
+    assert _select_quantiles(preds, tq, [0.5, 0.1]).tolist() == [[[3.0, 1.0], [4.0, 2.0]]]
+    assert torch.allclose(_select_quantiles(preds, tq, [0.3, 0.7]), torch.tensor([[[2.0, 4.0], [3.0, 6.0]]]))
+
+
+@pytest.mark.gpu
 def test_predict_quantiles_and_df():
     pd = pytest.importorskip("pandas")
-    p = pipe()
+    p = pipe("cuda")
     q, mean = p.predict_quantiles(torch.randn(2, 32), prediction_length=16, quantile_levels=[0.1, 0.5])
     assert q[0].shape == (1, 16, 2) and mean[0].shape == (1, 16)
     assert torch.equal(mean[0], q[0][..., 1])
@@ -106,6 +122,8 @@ def test_predict_quantiles_and_df():
                        "target": torch.randn(50).tolist()})
     out = p.predict_df(df, prediction_length=16, quantile_levels=[0.5])
     assert list(out.columns) == ["item_id", "step", "0.5"] and len(out) == 32
+    assert out["item_id"].tolist() == ["a"] * 16 + ["b"] * 16 and out["step"].tolist() == list(range(16)) * 2
+    assert out["0.5"].dtype == "float64"
 
 
 def test_checkpoint_and_lora_loading(tmp_path):
@@ -193,3 +211,20 @@ def test_two_rank_gloo_sharding_and_gather():
         assert p.exitcode == 0
     for r in range(2):
         assert torch.allclose(results[r], expect)
+
+
+def test_group_series_matches_groupby():
+    pd = pytest.importorskip("pandas")
+    from cutechronos_b200.pipeline import _group_series
+    g = torch.Generator().manual_seed(0)
+    n = 500
+    ids = torch.randint(0, 7, (n,), generator=g).tolist()
+    df = pd.DataFrame({"item_id": [f"s{i}" if i != 6 else None for i in ids],
+                       "timestamp": torch.randperm(n, generator=g).tolist(),
+                       "target": torch.randn(n, generator=g).tolist()})
+    got_ids, rag = _group_series(df, "item_id", "timestamp", "target")
+    groups = df.sort_values("timestamp").groupby("item_id", sort=False)
+    assert got_ids == list(groups.groups.keys())
+    ref = [torch.tensor(grp["target"].values, dtype=torch.float32) for _, grp in groups]
+    assert rag.lens == [len(r) for r in ref]
+    assert torch.equal(rag.values, torch.cat(ref))

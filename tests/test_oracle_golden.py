@@ -5,9 +5,10 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import SMALL, case_inputs, oracle_config, small_config
+from conftest import GOLDEN, SMALL, case_inputs, oracle_config, small_config
 from cutechronos_b200.model import CuteChronos2Config, CuteChronos2Model
 from cutechronos_b200.workloads import seeded_init_, seeded_state_dict
+from oracle import chronos2_oracle as orc
 from oracle.chronos2_oracle import OracleConfig, forward, prepare_patched_context
 
 
@@ -70,3 +71,29 @@ def test_oracle_base_cfg0(golden_base):
     y = forward(OracleConfig(), W, ctx, None, int(golden_base["N"]))
     ref = torch.from_numpy(golden_base["out_f32"])
     assert (y - ref).abs().max().item() <= 2e-4
+
+
+# ---- pipeline host steps (fixtures from the reference pipeline: make_pipeline_golden.py) -------
+def _pipeline_golden():
+    return dict(np.load(GOLDEN / "pipeline_host.npz"))
+
+
+def test_oracle_select_quantiles_matches_reference():
+    z = _pipeline_golden()
+    tq = z["levels_all"].tolist()
+    for kind in ("f32", "bf16"):
+        preds = torch.from_numpy(z["preds_f32" if kind == "f32" else "preds_bf16_as_f32"])
+        for name in ("default", "mixed", "median", "all"):
+            got = orc.select_quantiles(preds, tq, z[f"levels_{name}"].tolist())
+            assert np.array_equal(got.numpy(), z[f"sel_{kind}_{name}"]), (kind, name)
+
+
+def test_oracle_left_pad_and_stack_matches_reference():
+    z = _pipeline_golden()
+    ci = 0
+    while f"stack{ci}_out" in z:
+        got = orc.left_pad_and_stack(torch.from_numpy(z[f"stack{ci}_values"]), z[f"stack{ci}_lens"],
+                                     int(z[f"stack{ci}_ctxlen"]))
+        assert np.array_equal(got.numpy(), z[f"stack{ci}_out"], equal_nan=True), ci
+        ci += 1
+    assert ci == 4
