@@ -430,6 +430,7 @@ def run_micro(args):
     rows): each GEMM of the forward with its fused epilogue and the time
     attention, timed with CUDA events; cuBLAS on the same GEMM shapes is timed
     beside them as a yardstick (it is not used by the engine)."""
+    from cutechronos_b200 import _native as nat
     from cutechronos_b200 import kernels as kk
 
     dev = torch.device("cuda", 0)
@@ -449,6 +450,19 @@ def run_micro(args):
     qkvr = rnd(M, 3 * d, scale=0.5)
     tok = torch.ones(M, dtype=torch.uint8, device=dev)
     att = torch.empty(M, d, dtype=torch.bfloat16, device=dev)
+    lib = nat.load()
+
+    def variant(v, fn):
+        def run():
+            old = lib.cc2_set_attention_variant(v)
+            fn()
+            lib.cc2_set_attention_variant(old)
+        return run
+
+    B4 = 4096
+    qkv4 = rnd(B4 * 37, 3 * d, scale=0.5)
+    tok4 = torch.ones(B4 * 37, dtype=torch.uint8, device=dev)
+    att4 = torch.empty(B4 * 37, d, dtype=torch.bfloat16, device=dev)
     cases = {
         "qkv  N=2304 K=768 rowscale": (lambda: kk.linear(x, wqkv, row_ssq=ssq, norm_dim=d), 2 * M * 3 * d * d),
         "o    N=768  K=768 resid+ssq": (lambda: kk.linear(x, wo, residual=res, ssq_out=so, out=res), 2 * M * d * d),
@@ -460,6 +474,13 @@ def run_micro(args):
                                    4 * args.batch * 12 * 133 * 133 * 64),
         "attn time S=133 (no rope)": (lambda: kk.attention_rows(qkvr, tok, args.batch, 133, 12, False, att),
                                       4 * args.batch * 12 * 133 * 133 * 64),
+        "attn time S=133 (no rope, mma.sync)": (
+            variant(1, lambda: kk.attention_rows(qkvr, tok, args.batch, 133, 12, False, att)),
+            4 * args.batch * 12 * 133 * 133 * 64),
+        "attn time S=37 B=4096": (lambda: kk.attention_rows(qkv4, tok4, B4, 37, 12, False, att4),
+                                  4 * B4 * 12 * 37 * 37 * 64),
+        "attn time S=37 B=4096 (tcgen05)": (
+            variant(2, lambda: kk.attention_rows(qkv4, tok4, B4, 37, 12, False, att4)), 4 * B4 * 12 * 37 * 37 * 64),
         "cublas qkv  N=2304 K=768": (lambda: torch.matmul(x, wqkv.T), 2 * M * 3 * d * d),
         "cublas o    N=768  K=768": (lambda: torch.matmul(x, wo.T), 2 * M * d * d),
         "cublas ffn1 N=3072 K=768": (lambda: torch.matmul(x, wi.T), 2 * M * dff * d),

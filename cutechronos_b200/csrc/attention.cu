@@ -39,6 +39,15 @@
 namespace cc2 {
 
 int encode_bf16_map(CUtensorMap* map, const void* ptr, int cols, int rows, int ld, int box_cols, int box_rows);
+bool attn_tc_supported(int S, int ld, int ldo, const void* qkv);
+int launch_attn_tc(const void* qkv, int ld, int qcol, int kcol, int vcol, void* out, int ldo, const uint8_t* tok,
+                   int num_sets, int S, int heads, int* err, cudaStream_t st);
+
+// 0 (default): tcgen05 time attention for sets of 112..144 tokens, where it
+// is faster than the mma.sync kernels; 1: the mma.sync kernels only; 2:
+// tcgen05 for every set it supports (17..144 tokens).  Set through
+// cc2_set_attention_variant.
+int g_attn_variant = 0;
 
 // Error word of the attention kernels' bounded waits (1 = a wait ran out).
 __device__ int g_attn_error = 0;
@@ -986,7 +995,12 @@ int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int
     const int pbufs = (int)std::min<size_t>(kPBufs, kPSmemLimit / pbuf);
     const bool aligned = ((uintptr_t)qkv & 15u) == 0 && (ld * 2) % 16 == 0;
     // (sets of fewer than 8 query tiles run faster in the whole-set kernel below)
-    if (mode == 0 && !cs && pbufs >= 1 && aligned && (S + 15) / 16 >= 8) {
+    const bool tc_pick = g_attn_variant == 2 || (g_attn_variant == 0 && S >= 112);
+    if (mode == 0 && !cs && tc_pick && ((uintptr_t)out & 15u) == 0 && attn_tc_supported(S, ld, ldo, qkv)) {
+      int* err = nullptr;
+      CC2_CUDA(cudaGetSymbolAddress((void**)&err, g_attn_error));
+      return launch_attn_tc(qkv, ld, qcol, kcol, vcol, out, ldo, tok, num_sets, S, heads, err, st);
+    } else if (mode == 0 && !cs && pbufs >= 1 && aligned && (S + 15) / 16 >= 8) {
       CUtensorMap map;
       CC2_TRY(encode_bf16_map(&map, qkv, ld, num_sets * S, ld, 64, npad_t / nbox));
       PersistArgs pa{S, npad_t, heads, num_sets * heads, qcol, kcol, vcol, npad_t / nbox, nbox, pbufs, pbuf};

@@ -68,6 +68,8 @@ int launch_rmsnorm_rows(int, const void*, int, const void*, void*, int, int, int
 int launch_gemm_tc(const void*, int, const void*, int, void*, int, int, int, int, const cc2_epilogue*,
                    cudaStream_t);
 extern int g_gemm_variant;
+extern int g_attn_variant;
+int set_attn_trace(void* buf);
 int launch_gemm_f32(const void*, int, const void*, int, void*, int, int, int, int, const cc2_epilogue*,
                     cudaStream_t, float* scratch = nullptr, size_t scratch_floats = 0);
 int launch_attention(int, int, const void*, int, int, int, int, void*, int, const uint8_t*, int, int, int, int,
@@ -749,6 +751,17 @@ int cc2_set_gemm_variant(int variant) {
   const int old = g_gemm_variant;
   g_gemm_variant = (variant == 1 || variant == 3) ? variant : 0;
   return old;
+}
+
+int cc2_set_attention_variant(int variant) {
+  const int old = g_attn_variant;
+  g_attn_variant = (variant == 1 || variant == 2) ? variant : 0;
+  return old;
+}
+
+int cc2_set_attention_trace(void* device_buffer) {
+  clear_error();
+  return set_attn_trace(device_buffer);
 }
 
 int cc2_gemm(int dtype, const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,

@@ -222,6 +222,20 @@ typedef struct {
  * skipped (nothing is written).  Process-wide; returns the previous value. */
 CC2_API int cc2_set_gemm_variant(int variant);
 
+/* Time-attention kernel choice for bf16 sets (RoPE applied beforehand):
+ * 0 (default) = tcgen05 (scores and outputs in TMEM) for 112..144 tokens,
+ * the mma.sync kernels otherwise; 1 = the mma.sync kernels only; 2 = tcgen05
+ * for every set of 17..144 tokens.  Process-wide; returns the previous value. */
+CC2_API int cc2_set_attention_variant(int variant);
+
+/* Event trace of the tcgen05 time-attention kernel: with a device buffer of
+ * 16 x 12 uint64 (zeroed by the caller), CTA 0 of every later launch writes
+ * %globaltimer stamps (ns) of its first 16 query tiles, 12 per tile: load
+ * issued, MMA saw the load, S MMAs issued, MMA saw P, O MMAs issued, softmax
+ * saw S, P written, softmax saw O, O stored, scores in registers, row max
+ * done (one slot unused).  NULL turns it off. */
+CC2_API int cc2_set_attention_trace(void* device_buffer);
+
 /* out[M, N] = epilogue(A[M, K] @ W[N, K]^T); A, W, out, resid of `dtype`,
  * row-major with the given row pitches (elements).  bf16 runs on tcgen05
  * tensor cores (TMEM accumulators, TMA-fed); f32 runs on CUDA cores. */

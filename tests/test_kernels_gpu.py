@@ -249,6 +249,40 @@ def test_time_attention(B, S, dtype, rope):
     assert (out - ref).abs().max().item() <= tol * max(1.0, ref.abs().max().item())
 
 
+@pytest.fixture
+def attn_variant():
+    from cutechronos_b200 import _native as nat
+    lib = nat.load()
+    old = lib.cc2_set_attention_variant(0)
+    yield lib.cc2_set_attention_variant
+    lib.cc2_set_attention_variant(old)
+
+
+# tcgen05 kernel (variant 2: wherever it runs, 17..144 tokens), the default
+# choice (0) and the mma.sync kernels (1) on bf16 sets: one or two query
+# tiles, 64/128/144-key widths, one or two buffer stages, many items per CTA,
+# a series whose keys are all masked
+@pytest.mark.parametrize("B,S", [(1, 17), (3, 37), (2, 64), (5, 128), (4, 129), (7, 133), (2, 144), (3, 160),
+                                 (2, 160), (2, 192), (300, 133), (700, 37)])
+@pytest.mark.parametrize("variant", [0, 1, 2])
+def test_time_attention_bf16_variants(attn_variant, B, S, variant):
+    attn_variant(variant)
+    g = torch.Generator().manual_seed(B * 7 + S)
+    H = 12
+    q, k, v = ((torch.randn(B, H, S, 64, generator=g) * 0.5).to(torch.bfloat16) for _ in range(3))
+    valid = torch.rand(B, S, generator=g) > 0.3
+    valid[:, -1] = True
+    if B > 2:
+        valid[1] = False  # every key of series 1 masked: its queries average V with equal weights
+    mask = (1.0 - valid.float())[:, None, None, :] * torch.finfo(torch.float32).min
+    ref = orc.unscaled_attention(q.float(), k.float(), v.float(), mask)
+    if B > 2:
+        ref[1] = v[1].float().mean(dim=1, keepdim=True).expand(H, S, 64)
+    out = K().unscaled_attention(q.to(DEV), k.to(DEV), v.to(DEV), valid.to(DEV)).cpu().float()
+    assert torch.isfinite(out).all()
+    assert (out - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+
+
 def test_attention_uniform_known_answer():
     # identical keys -> uniform weights -> output = mean of V (reference test_attention.py:199-213)
     B, H, S = 2, 12, 70
