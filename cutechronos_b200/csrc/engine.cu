@@ -70,6 +70,7 @@ int launch_gemm_tc(const void*, int, const void*, int, void*, int, int, int, int
 extern int g_gemm_variant;
 extern int g_attn_variant;
 int set_attn_trace(void* buf);
+int set_gemm_trace(void* buf);
 int launch_gemm_f32(const void*, int, const void*, int, void*, int, int, int, int, const cc2_epilogue*,
                     cudaStream_t, float* scratch = nullptr, size_t scratch_floats = 0);
 int launch_attention(int, int, const void*, int, int, int, int, void*, int, const uint8_t*, int, int, int, int,
@@ -757,6 +758,11 @@ int cc2_set_attention_variant(int variant) {
   const int old = g_attn_variant;
   g_attn_variant = (variant == 1 || variant == 2) ? variant : 0;
   return old;
+}
+
+int cc2_set_gemm_trace(void* device_buffer) {
+  clear_error();
+  return set_gemm_trace(device_buffer);
 }
 
 int cc2_set_attention_trace(void* device_buffer) {

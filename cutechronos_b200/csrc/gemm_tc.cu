@@ -527,6 +527,19 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 // ---------------------------------------------------------------------------------
 namespace pair {
 
+// Optional event trace (cc2_set_gemm_trace): CTA 0 records %globaltimer stamps
+// of its first kTraceTiles tiles, kTraceEv per tile:
+//   0 MMA: accumulator free   1 MMA: first stage loaded   2 MMA: last k-block
+//   issued   3 epilogue warp 2: accumulator full   4 epilogue warp 2: done
+//   5 producer: first load of the tile issued   6 MMA: ns spent waiting for
+//   loaded stages during the tile
+constexpr int kTraceTiles = 32, kTraceEv = 8;
+__device__ unsigned long long* g_gemm_trace = nullptr;
+
+__device__ __forceinline__ void gtrace(unsigned long long* tr, int tile_it, int ev, unsigned long long v) {
+  if (tr != nullptr && tile_it < kTraceTiles) tr[tile_it * kTraceEv + ev] = v;
+}
+
 constexpr int A_BYTES = 128 * BK * 2;
 constexpr int B_BYTES = 128 * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -646,6 +659,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   const int num_tiles = m_tiles * n_tiles;
   const int kblocks = (K + BK - 1) / BK;
   const int pair_id = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+  unsigned long long* const gtr = blockIdx.x == 0 ? g_gemm_trace : nullptr;
 
   if (warp == 0) {
     if (lane == 0) {
@@ -653,9 +667,11 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs) {
+      int pit = 0;
+      for (int tile = pair_id; tile < num_tiles && ok; tile += num_pairs, ++pit) {
         const int mt = tile / n_tiles, nt = tile % n_tiles;
         for (int kb = 0; kb < kblocks; ++kb) {
+          if (kb == 1) gtrace(gtr, pit, 5, globaltimer_ns());
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) { ok = false; break; }
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
           const uint32_t fb = lead_full0 + 8u * stage;
@@ -682,9 +698,16 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
         if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        if (gtr) gtrace(gtr, it, 0, globaltimer_ns());
+        unsigned long long waited = 0;
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
+          if (gtr && !mbar_try_wait(full_bar(stage), phase)) {
+            const unsigned long long w0 = globaltimer_ns();
+            if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
+            waited += globaltimer_ns() - w0;
+          } else if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
+          if (gtr && kb == 0) gtrace(gtr, it, 1, globaltimer_ns());
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
           const uint32_t sb = sa + A_BYTES;
 #pragma unroll
@@ -693,6 +716,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           commit_pair(own_empty0 + 8u * stage);
           commit_pair(peer_empty0 + 8u * stage);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (gtr) {
+          gtrace(gtr, it, 2, globaltimer_ns());
+          gtrace(gtr, it, 6, waited);
         }
         if (ok) {
           commit_pair(own_tfull0 + 8u * acc);
@@ -740,6 +767,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
       if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag)) break;
       tc_fence_after();
+      const bool tw = gtr != nullptr && warp == 2 && lane == 0;
+      if (tw) gtrace(gtr, it, 3, globaltimer_ns());
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
       bool aborted = false;
       for (int j = 0; j < (SKIP_EPI ? 0 : ng); ++j) {
@@ -773,6 +802,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       tc_fence_before();
       __syncwarp();
       if (lane == 0) arrive_cluster(lead_tempty0 + 8u * acc);
+      if (tw) gtrace(gtr, it, 4, globaltimer_ns());
       if (aborted) break;
     }
     if (lane == 0) bulk_wait_all();
@@ -916,6 +946,12 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
 }  // namespace tc
 
 // bf16 2-D tensor map with 128-byte swizzle (shared with the attention kernels).
+int set_gemm_trace(void* buf) {
+  unsigned long long* p = (unsigned long long*)buf;
+  CC2_CUDA(cudaMemcpyToSymbol(tc::pair::g_gemm_trace, &p, sizeof(p)));
+  return CC2_OK;
+}
+
 int encode_bf16_map(CUtensorMap* map, const void* ptr, int cols, int rows, int ld, int box_cols, int box_rows) {
   return tc::make_map_box(map, ptr, cols, rows, ld, box_cols, box_rows);
 }

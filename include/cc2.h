@@ -236,6 +236,14 @@ CC2_API int cc2_set_attention_variant(int variant);
  * done (one slot unused).  NULL turns it off. */
 CC2_API int cc2_set_attention_trace(void* device_buffer);
 
+/* Event trace of the 2-SM GEMM: with a device buffer of 32 x 8 uint64
+ * (zeroed by the caller), CTA 0 of every later launch writes, for its first
+ * 32 tiles: %globaltimer stamps (ns) of accumulator free, first stage loaded,
+ * last k-block issued (MMA thread), accumulator full, epilogue done (first
+ * epilogue warp), first load issued (producer), and the nanoseconds the MMA
+ * thread waited for loaded stages in the tile.  NULL turns it off. */
+CC2_API int cc2_set_gemm_trace(void* device_buffer);
+
 /* out[M, N] = epilogue(A[M, K] @ W[N, K]^T); A, W, out, resid of `dtype`,
  * row-major with the given row pitches (elements).  bf16 runs on tcgen05
  * tensor cores (TMEM accumulators, TMA-fed); f32 runs on CUDA cores. */
