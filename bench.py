@@ -113,6 +113,19 @@ class ClockSampler:
                 "power_w_max": max((num(r[3]) or 0.0) for r in self.rows)}
 
 
+def gemm_traffic_per_launch():
+    """DRAM bytes per GEMM launch from the committed ncu summary of the same
+    workload (profiles/gemm_dram_cfg1.md); None when it is absent."""
+    p = Path(__file__).resolve().parent / "profiles" / "gemm_dram_cfg1.md"
+    try:
+        for line in p.read_text().splitlines():
+            if line.startswith("traffic_bytes_per_launch:"):
+                return int(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -385,7 +398,8 @@ def run_b200(args):
             "bound": "tensor", "kernel": "gemm_tc_kernel (tcgen05, all GEMM launches of the step)",
             "achieved": achieved_tf, "peak": tf_sus, "unit": "TFLOP/s", "frac": achieved_tf / tf_sus,
             "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long step)",
-            "traffic": None,
+            "traffic": gemm_traffic_per_launch(),
+            "traffic_source": "profiles/gemm_dram_cfg1.md (ncu dram__bytes_read+write, per GEMM launch of one forward)",
             "launches_per_step": gemm["launches"] / args.steps,
             "avg_launch_us": 1e3 * gemm["ms"] / max(1, gemm["launches"]),
         }
