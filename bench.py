@@ -240,6 +240,14 @@ def other_configs(model_bf16, dev, flush):
                     ("cfg4_b4096_ctx512", config4())):
         out[name + "_forecasts_per_s"] = forecasts_per_s(model_bf16, w.context.to(dev), w.num_output_patches,
                                                          w.group_ids, flush)
+    # configs[1] with the TurboQuant K/V hook on (4 bits, prod keys, mse values)
+    from cutechronos_b200.workloads import series_cfg1
+    model_bf16.enable_turboquant_kv(bits=4, key_mode="prod", value_mode="mse")
+    try:
+        out["cfg1_turboquant_kv4_forecasts_per_s"] = forecasts_per_s(model_bf16, series_cfg1(256, 2048, 1).to(dev),
+                                                                     4, None, flush)
+    finally:
+        model_bf16.disable_turboquant_kv()
     return out
 
 

@@ -71,6 +71,9 @@ extern int g_gemm_variant;
 extern int g_attn_variant;
 int set_attn_trace(void* buf);
 int set_gemm_trace(void* buf);
+int launch_kv_quant(int dtype, void* qkv, int ld, int rows, int q_col, int k_col, int v_col, int heads,
+                    const cc2_kvq* key, const cc2_kvq* value, const float* rope_cs, int rope_period, float* stats,
+                    cudaStream_t st);
 int launch_gemm_f32(const void*, int, const void*, int, void*, int, int, int, int, const cc2_epilogue*,
                     cudaStream_t, float* scratch = nullptr, size_t scratch_floats = 0);
 int launch_attention(int, int, const void*, int, int, int, int, void*, int, const uint8_t*, int, int, int, int,
@@ -221,6 +224,12 @@ struct cc2_model {
   float* rope;
   float* pack_tmp;
   uint32_t* rope_bf;  // [pos][d_kv/2] packed (cos, sin) bf16 pairs for the QKV epilogue
+  struct KvQuant {
+    bool has_k = false, has_v = false;
+    cc2_kvq key{}, value{};
+    float* stats = nullptr;
+  };
+  std::vector<KvQuant> kvq;  // per layer: TurboQuant K/V hook of the time attention
 };
 
 namespace {
@@ -596,10 +605,19 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
     a.ssq_in = ssq(3 * l); a.norm_dim = d; a.eps = eps;
     a.rope_cs = m->rope_bf; a.rope_period = S; a.rope_cols = 2 * d;
     CC2_TRY(gemm(dt, X, d, Lw.wqkv_t, d, w.QKV, 3 * d, M, 3 * d, d, &a, st));
+    // TurboQuant K/V hook: K and V replaced by their quantised reconstructions
+    // after RoPE (applied here first in fp32, where the attention would)
+    bool rope_done = rope_in_gemm;
+    if (l < (int)m->kvq.size() && (m->kvq[l].has_k || m->kvq[l].has_v)) {
+      const cc2_model::KvQuant& q = m->kvq[l];
+      CC2_TRY(launch_kv_quant(dt, w.QKV, 3 * d, M, 0, d, 2 * d, c.num_heads, q.has_k ? &q.key : nullptr,
+                              q.has_v ? &q.value : nullptr, rope_done ? nullptr : m->rope, S, q.stats, st));
+      rope_done = true;
+    }
     {
       ProfScope ps_(CC2_K_ATTN_TIME, 4.0 * B * (double)S * S * d, 0.0, st);
       CC2_TRY(launch_attention(dt, 0, w.QKV, 3 * d, 0, d, 2 * d, Y, d, w.tok, B, S, c.num_heads, c.d_kv,
-                               nullptr, nullptr, 0, 0, rope_in_gemm ? nullptr : m->rope, st));
+                               nullptr, nullptr, 0, 0, rope_done ? nullptr : m->rope, st));
     }
     cc2_epilogue o = epi_m(CC2_EPI_RESID | CC2_EPI_SSQ, M);
     o.resid = X; o.ld_resid = d; o.ssq_out = ssq(3 * l + 1);
@@ -758,6 +776,30 @@ int cc2_set_attention_variant(int variant) {
   const int old = g_attn_variant;
   g_attn_variant = (variant == 1 || variant == 2) ? variant : 0;
   return old;
+}
+
+int cc2_kv_quant(int dtype, void* qkv, int ld, int rows, int q_col, int k_col, int v_col, int heads,
+                 const cc2_kvq* key, const cc2_kvq* value, const float* rope_cs, int rope_period, float* stats,
+                 void* stream) {
+  clear_error();
+  return launch_kv_quant(dtype, qkv, ld, rows, q_col, k_col, v_col, heads, key, value, rope_cs, rope_period, stats,
+                         (cudaStream_t)stream);
+}
+
+int cc2_model_set_kv_quant(cc2_model* m, int layer, const cc2_kvq* key, const cc2_kvq* value, float* stats) {
+  clear_error();
+  CC2_REQUIRE(m != nullptr, "cc2_model_set_kv_quant: null model");
+  CC2_REQUIRE(layer >= 0 && layer < m->cfg.num_layers, "cc2_model_set_kv_quant: layer %d out of range", layer);
+  CC2_REQUIRE(m->cfg.d_kv == 64, "cc2_model_set_kv_quant: the quantiser works on d_kv = 64");
+  if (m->kvq.size() < (size_t)m->cfg.num_layers) m->kvq.resize(m->cfg.num_layers);
+  cc2_model::KvQuant q;
+  q.has_k = key != nullptr;
+  q.has_v = value != nullptr;
+  if (key) q.key = *key;
+  if (value) q.value = *value;
+  q.stats = stats;
+  m->kvq[layer] = q;
+  return CC2_OK;
 }
 
 int cc2_set_gemm_trace(void* device_buffer) {

@@ -239,6 +239,9 @@ class CuteChronos2Model(nn.Module):
         self.register_buffer("quantiles", torch.tensor(config.quantiles, dtype=torch.float32), persistent=False)
         self._engine: _Engine | None = None
         self._engine_key = None
+        self._tubroquant_config: dict | None = None
+        self._tq_state = None  # (engine, per-layer params, stats tensor) of the enabled hook
+        self._tq_last_rows = 0
 
     # -- helpers mirroring the reference ---------------------------------------------
     def _param_dtype(self) -> torch.dtype:
@@ -305,6 +308,11 @@ class CuteChronos2Model(nn.Module):
         self._last_loc = torch.empty(B, dtype=torch.float32, device=dev)
         self._last_scale = torch.empty(B, dtype=torch.float32, device=dev)
         ws, ws_bytes = eng.workspace(B, L, N, max_group)
+        tq = self._turboquant_for(eng, dev)
+        if tq is not None:
+            tq[2].zero_()
+            P = -(-min(L, cfg.context_length) // cfg.input_patch_size)
+            self._tq_last_rows = B * (P + int(cfg.use_reg_token) + N)
         stream = torch.cuda.current_stream(dev).cuda_stream
         with torch.cuda.device(dev):
             st = eng._lib.cc2_forward(
@@ -313,6 +321,84 @@ class CuteChronos2Model(nn.Module):
                 _ptr(self._last_loc), _ptr(self._last_scale), ws, ws_bytes, stream)
         nat.check(st, "cc2_forward")
         return out
+
+    # -- TurboQuant K/V hook (model.py:615-688) ------------------------------------------
+    def enable_turboquant_kv(self, bits: int = 4, *, key_mode: str = "prod", value_mode: str = "mse",
+                             rotation: str = "hadamard", seed: int = 0,
+                             norm_dtype: str = "float16") -> "CuteChronos2Model":
+        """Quantise the time-attention K and V vectors of every layer with
+        TurboQuant-style quantisers (layer i: key seed ``seed + 2i``, value seed
+        ``seed + 2i + 1``); the device kernel runs inside the forward."""
+        from .turboquant import TurboQuantParams
+        # validate now, as the reference's constructor does
+        TurboQuantParams.build(self.config.d_kv, bits, mode=key_mode, rotation=rotation, seed=seed,
+                               norm_dtype=norm_dtype, device="cpu")
+        TurboQuantParams.build(self.config.d_kv, bits, mode=value_mode, rotation=rotation, seed=seed + 1,
+                               norm_dtype=norm_dtype, device="cpu")
+        self._tubroquant_config = {"bits": bits, "key_mode": key_mode, "value_mode": value_mode,
+                                   "rotation": rotation, "seed": seed, "norm_dtype": norm_dtype}
+        self._tq_state = None
+        self._tq_last_rows = 0
+        return self
+
+    def disable_turboquant_kv(self) -> "CuteChronos2Model":
+        """Turn the hook off for every layer."""
+        if self._tq_state is not None and self._engine is self._tq_state[0]:
+            eng = self._engine
+            for l in range(self.config.num_layers):
+                nat.check(eng._lib.cc2_model_set_kv_quant(eng.handle, l, None, None, None), "cc2_model_set_kv_quant")
+        self._tubroquant_config = None
+        self._tq_state = None
+        self._tq_last_rows = 0
+        return self
+
+    def _turboquant_for(self, eng: "_Engine", dev: torch.device):
+        """The hook's device state for this engine (built and registered with the
+        native model on first use after enabling or re-packing)."""
+        if self._tubroquant_config is None:
+            return None
+        if self._tq_state is not None and self._tq_state[0] is eng:
+            return self._tq_state
+        from .turboquant import TurboQuantParams
+        c = self._tubroquant_config
+        layers = []
+        stats = torch.zeros(self.config.num_layers, 4, dtype=torch.float32, device=dev)
+        for l in range(self.config.num_layers):
+            kq = TurboQuantParams.build(self.config.d_kv, c["bits"], mode=c["key_mode"], rotation=c["rotation"],
+                                        seed=c["seed"] + 2 * l, norm_dtype=c["norm_dtype"], device=dev)
+            vq = TurboQuantParams.build(self.config.d_kv, c["bits"], mode=c["value_mode"], rotation=c["rotation"],
+                                        seed=c["seed"] + 2 * l + 1, norm_dtype=c["norm_dtype"], device=dev)
+            kn, vn = kq.native(), vq.native()
+            nat.check(eng._lib.cc2_model_set_kv_quant(eng.handle, l, C.byref(kn), C.byref(vn), stats[l].data_ptr()),
+                      "cc2_model_set_kv_quant")
+            layers.append((kq, vq))
+        self._tq_state = (eng, layers, stats)
+        return self._tq_state
+
+    def get_tubroquant_summary(self) -> dict[str, Any]:
+        """Per-layer statistics of the last forward (model.py:669-688): raw and
+        packed bytes of K and V, compression ratio, mean squared and max
+        absolute error of the reconstructions."""
+        layers: list[dict[str, float]] = []
+        if self._tq_state is not None and self._tq_last_rows > 0:
+            _, params, stats = self._tq_state
+            st = stats.cpu()
+            cfg = self.config
+            vectors = self._tq_last_rows * cfg.num_heads
+            esz = torch.finfo(self._param_dtype()).bits // 8
+            for l, (kq, vq) in enumerate(params):
+                raw = 2.0 * vectors * cfg.d_kv * esz
+                packed = float(vectors * (kq.quantized_bytes_per_vector() + vq.quantized_bytes_per_vector()))
+                n = float(vectors * cfg.d_kv)
+                layers.append({"layer": float(l), "raw_bytes": raw, "quantized_bytes": packed,
+                               "compression_ratio": raw / max(packed, 1.0),
+                               "key_mse": float(st[l, 0]) / n, "value_mse": float(st[l, 2]) / n,
+                               "key_max_abs_error": float(st[l, 1]), "value_max_abs_error": float(st[l, 3])})
+        total_raw = sum(x["raw_bytes"] for x in layers)
+        total_q = sum(x["quantized_bytes"] for x in layers)
+        return {"enabled": self._tubroquant_config is not None, "config": self._tubroquant_config,
+                "layers": layers, "total_raw_bytes": total_raw, "total_quantized_bytes": total_q,
+                "compression_ratio": total_raw / max(total_q, 1.0)}
 
     @torch.inference_mode()
     def predict(self, context: torch.Tensor, context_mask: torch.Tensor | None = None,

@@ -277,6 +277,42 @@ CC2_API int cc2_output_transform(int dtype, const void* preds, int ld_preds, con
                          int use_arcsinh, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* TurboQuant K/V hook of the time attention (model.py:615-667,              */
+/* tubroquant/quantizer.py:41-178).                                           */
+/* ------------------------------------------------------------------------ */
+/* One quantiser of 64-value vectors; every pointer is device memory.        */
+typedef struct {
+  int mode;                 /* 0 = "mse", 1 = "prod" (centroids on bits - 1, plus a 1-bit QJL sketch) */
+  int bits;                 /* bits per coordinate, 0..8 centroid bits */
+  int rotation;             /* 0 = Hadamard (signs, perm, inv_perm), 1 = dense matrix */
+  int norm_dtype;           /* storage of the norms: 0 float16, 1 bfloat16, 2 float32 */
+  const float* signs;       /* (64) +-1 */
+  const int32_t* perm;      /* (64): rotated[i] = fwht(x[perm[i]] * signs[i]) / 8 */
+  const int32_t* inv_perm;  /* (64) */
+  const float* matrix;      /* (64, 64) row-major: rotated = x @ matrix^T */
+  const float* codebook;    /* (2^centroid bits), ascending */
+  const float* boundaries;  /* (2^centroid bits - 1), ascending */
+  const float* proj;        /* (64, 64) Gaussian projection (prod mode) */
+} cc2_kvq;
+
+/* In place on packed token rows (dtype, row pitch ld): RoPE on the Q and K
+ * columns first when rope_cs (float32 [pos][32] (cos, sin) pairs, position =
+ * row % rope_period) is given, then every 64-column K vector of each head
+ * replaced by its quantised reconstruction with `key` and every V vector with
+ * `value` (NULL = leave as is).  stats (dev float32[4] or NULL) accumulates K
+ * squared error, K max |error|, V squared error, V max |error|. */
+CC2_API int cc2_kv_quant(int dtype, void* qkv, int ld, int rows, int q_col, int k_col, int v_col, int heads,
+                         const cc2_kvq* key, const cc2_kvq* value, const float* rope_cs, int rope_period,
+                         float* stats, void* stream);
+
+/* Enable (key and/or value non-NULL; the structs are copied, the tables they
+ * point to stay the caller's) or disable (both NULL) the hook for one layer
+ * of a model; cc2_forward then runs it between that layer's QKV GEMM and its
+ * time attention, accumulating into stats (dev float32[4] or NULL). */
+CC2_API int cc2_model_set_kv_quant(cc2_model* m, int layer, const cc2_kvq* key, const cc2_kvq* value,
+                                   float* stats);
+
+/* ------------------------------------------------------------------------ */
 /* Pipeline steps on the device (pipeline.py:221-322, 24-58).                 */
 /* ------------------------------------------------------------------------ */
 /* Ragged series -> (B, L) batch: row b is values[offsets[b] .. offsets[b+1])

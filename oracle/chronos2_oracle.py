@@ -189,8 +189,10 @@ def unscaled_attention(q, k, v, mask):
     return torch.matmul(w, v)
 
 
-def time_self_attention(cfg, W, p, x, ext_mask, cos, sin):
-    """TimeSelfAttentionFallback.forward, CPU branch (model.py:209-275)."""
+def time_self_attention(cfg, W, p, x, ext_mask, cos, sin, kv_hook=None):
+    """TimeSelfAttentionFallback.forward, CPU branch (model.py:209-275).
+    ``kv_hook(k, v) -> (k, v)`` stands for the key/value quantisers of
+    model.py:243-248 (applied after RoPE)."""
     B, S, _ = x.shape
     H, Dh = cfg.num_heads, cfg.d_kv
     n = rms_norm(x, W[p + "layer_norm_weight"], cfg.layer_norm_epsilon)
@@ -199,6 +201,8 @@ def time_self_attention(cfg, W, p, x, ext_mask, cos, sin):
     v = F.linear(n, W[p + "v.weight"]).view(B, S, H, Dh).transpose(1, 2)
     c, s_ = cos.unsqueeze(1), sin.unsqueeze(1)  # apply_rope_fallback (model.py:112-128)
     q, k = q * c + _rotate_half(q) * s_, k * c + _rotate_half(k) * s_
+    if kv_hook is not None:
+        k, v = kv_hook(k, v)
     a = unscaled_attention(q, k, v, ext_mask).transpose(1, 2).reshape(B, S, H * Dh)
     return x + F.linear(a, W[p + "o.weight"])
 
@@ -230,12 +234,13 @@ def feed_forward(cfg, W, p, x):
 @torch.no_grad()
 def forward(cfg: OracleConfig, W: dict, context: torch.Tensor, context_mask=None,
             num_output_patches: int = 1, group_ids=None, dtype=torch.float32,
-            return_intermediates: bool = False):
+            return_intermediates: bool = False, kv_hooks=None):
     """CuteChronos2Model.forward (cutechronos/model.py:738-831) on the CPU.
 
     ``W`` maps reference parameter names to CPU tensors (any dtype; they are
     cast to ``dtype``).  Returns (B, Q, 16*N) in ``dtype``; with
-    ``return_intermediates`` also a dict of stage outputs."""
+    ``return_intermediates`` also a dict of stage outputs; ``kv_hooks`` (one
+    callable per layer or None) quantise the time attention's K and V."""
     W = {k: v.detach().to("cpu", dtype) for k, v in W.items()}
     context = context.detach().cpu()
     B = context.shape[0]
@@ -267,7 +272,8 @@ def forward(cfg: OracleConfig, W: dict, context: torch.Tensor, context_mask=None
     cos, sin = rope_cos_sin(cfg, S, dtype)
     for i in range(cfg.num_layers):
         p = f"blocks.{i}."
-        x = time_self_attention(cfg, W, p + "time_attn.", x, ext, cos, sin)
+        x = time_self_attention(cfg, W, p + "time_attn.", x, ext, cos, sin,
+                                kv_hooks[i] if kv_hooks is not None else None)
         x = group_self_attention(cfg, W, p + "group_attn.", x, gtm)
         x = feed_forward(cfg, W, p + "feed_forward.", x)
         if return_intermediates:
