@@ -485,7 +485,21 @@ def run_micro(args):
     qkv4 = rnd(B4 * 37, 3 * d, scale=0.5)
     tok4 = torch.ones(B4 * 37, dtype=torch.uint8, device=dev)
     att4 = torch.empty(B4 * 37, d, dtype=torch.bfloat16, device=dev)
+    # memory-bound kernels at a streaming size (HBM-bound; the forward's own
+    # launches are a few MB and launch/latency-bound)
+    Bp, Lp = 16384, 2048
+    Pp = Lp // 16
+    ctxp = torch.randn(Bp, Lp, generator=g, device=dev)
+    predp = rnd(Bp, 4, 336)
+    locp, scp = torch.zeros(Bp, device=dev), torch.ones(Bp, device=dev)
+    wln = rnd(d)
     cases = {
+        "preprocess B=16384 L=2048 bf16": (
+            lambda: kk.fused_preprocess(ctxp, 16, 8192, True, dtype=torch.bfloat16), 0,
+            Bp * (4 * Lp + 2 * 48 * Pp + Pp + 4 * Pp + 8)),
+        "output transform B=16384 N=4 bf16": (
+            lambda: kk.fused_output_transform(predp, locp, scp, 21, 16, True), 0, 2 * 2 * Bp * 4 * 336 + 8 * Bp),
+        "rmsnorm M=34048 d=768 bf16": (lambda: kk.rms_layernorm(x, wln), 0, 2 * 2 * M * d),
         "qkv  N=2304 K=768 rowscale": (lambda: kk.linear(x, wqkv, row_ssq=ssq, norm_dim=d), 2 * M * 3 * d * d),
         "o    N=768  K=768 resid+ssq": (lambda: kk.linear(x, wo, residual=res, ssq_out=so, out=res), 2 * M * d * d),
         "ffn1 N=3072 K=768 rowscale+relu": (lambda: kk.linear(x, wi, row_ssq=ssq, norm_dim=d, relu=True),
@@ -510,7 +524,10 @@ def run_micro(args):
         "cublas 8192^3": (lambda: torch.matmul(big, big), 2 * 8192 ** 3),
     }
     out = {}
-    for name, (fn, flops) in cases.items():
+    hbm, *_ = measured_peaks()
+    for name, spec in cases.items():
+        fn, flops = spec[0], spec[1]
+        nbytes = spec[2] if len(spec) > 2 else 0
         if args.only and args.only not in name:
             continue
         for _ in range(3):
@@ -523,6 +540,11 @@ def run_micro(args):
             b.record()
         torch.cuda.synchronize()
         ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+        if nbytes:
+            gbs = nbytes / (ms / 1e3) / 1e9
+            out[name] = {"us": round(ms * 1e3, 2), "gbs": round(gbs, 1), "hbm_frac": round(gbs / hbm, 3)}
+            log(f"{name:36s} {ms * 1e3:9.1f} us  {gbs:7.1f} GB/s ({gbs / hbm:.2f} of measured HBM)")
+            continue
         out[name] = {"us": round(ms * 1e3, 2), "tflops": round(flops / (ms / 1e3) / 1e12, 1)}
         log(f"{name:36s} {ms * 1e3:9.1f} us  {flops / (ms / 1e3) / 1e12:7.1f} TFLOP/s")
     print(json.dumps({"micro": out, "M": M}), flush=True)

@@ -16,6 +16,11 @@ namespace {
 
 constexpr int kPreThreads = 256;
 
+__device__ __forceinline__ uint32_t pack2bf(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
 __device__ __forceinline__ double block_sum(double v, double* red) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -129,6 +134,243 @@ preprocess_kernel(const float* __restrict__ ctx, const float* __restrict__ cmask
   }
 }
 
+// Vectorised preprocessing: one CTA per series, each thread owns chunks of 8
+// consecutive patch positions (CH per thread, kept in registers across the
+// three passes), 16-byte loads when the series is 16-byte aligned, and the
+// [time_enc | value | mask] chunks written as 16-byte (bf16) / 32-byte (fp32)
+// stores.  Same arithmetic as preprocess_kernel.
+template <typename T, int CH>
+__global__ void __launch_bounds__(kPreThreads)
+preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ cmask, int L, int Leff, int P, int ps,
+                      float te_scale, int use_arcsinh, int use_reg, int N, T* __restrict__ out, int ld,
+                      int pad_cols, uint8_t* __restrict__ tok_mask, float* __restrict__ attn_out,
+                      float* __restrict__ loc_out, float* __restrict__ scale_out, int vec_loads) {
+  __shared__ double red[kPreThreads / 32];
+  const int b = blockIdx.x;
+  const int S = P + use_reg + N;
+  const float* x = ctx + (size_t)b * L + (L - Leff);
+  const float* m = cmask ? cmask + (size_t)b * L + (L - Leff) : nullptr;
+  const int total = P * ps, pad = total - Leff;
+  float v[CH][8], mk[CH][8];
+  double sum = 0.0, cnt = 0.0;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int j0 = 8 * ((int)threadIdx.x + c * (int)blockDim.x);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[c][i] = __int_as_float(0x7fc00000);
+    if (j0 < total) {
+      const int s0 = j0 - pad;
+      if (vec_loads && s0 >= 0) {
+        const float4 a = *reinterpret_cast<const float4*>(x + s0);
+        const float4 e = *reinterpret_cast<const float4*>(x + s0 + 4);
+        v[c][0] = a.x; v[c][1] = a.y; v[c][2] = a.z; v[c][3] = a.w;
+        v[c][4] = e.x; v[c][5] = e.y; v[c][6] = e.z; v[c][7] = e.w;
+      } else if (vec_loads && s0 + 4 >= 0 && s0 < 0) {  // pad is a multiple of 4: upper half present
+        const float4 e = *reinterpret_cast<const float4*>(x + s0 + 4);
+        v[c][4] = e.x; v[c][5] = e.y; v[c][6] = e.z; v[c][7] = e.w;
+      } else if (!vec_loads) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (s0 + i >= 0) v[c][i] = x[s0 + i];
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int src = s0 + i;
+        mk[c][i] = src < 0 ? 0.0f : (m ? m[src] : (isnan(v[c][i]) ? 0.0f : 1.0f));
+        if (!isnan(v[c][i])) {
+          sum += v[c][i];
+          cnt += 1.0;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mk[c][i] = 0.0f;
+    }
+  }
+  sum = block_sum(sum, red);
+  cnt = block_sum(cnt, red);
+  const float lo = cnt > 0.0 ? (float)(sum / cnt) : 0.0f;
+  double ss = 0.0;
+#pragma unroll
+  for (int c = 0; c < CH; ++c)
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (!isnan(v[c][i])) {
+        const float d = v[c][i] - lo;
+        ss += (double)(d * d);
+      }
+  ss = block_sum(ss, red);
+  float sc = cnt > 0.0 ? sqrtf((float)(ss / cnt)) : 1.0f;
+  if (sc == 0.0f) sc = 1e-5f;
+  if (threadIdx.x == 0) {
+    loc_out[b] = lo;
+    scale_out[b] = sc;
+  }
+  const size_t row0 = (size_t)b * S;
+  const int cpp = ps / 8;  // chunks per patch: 1, 2 or 4 adjacent lanes
+#pragma unroll
+  for (int c = 0; c < CH; ++c) {
+    const int k = (int)threadIdx.x + c * (int)blockDim.x;
+    const int j0 = 8 * k;
+    float acc = 0.0f;
+    if (j0 < total) {
+      float te[8], val[8], mt[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int src = j0 + i - pad;
+        float z = __int_as_float(0x7fc00000);
+        if (src >= 0) {
+          z = (v[c][i] - lo) / sc;
+          if (use_arcsinh) z = asinhf(z);
+        }
+        mt[i] = roundT<T>(mk[c][i]);
+        val[i] = mt[i] > 0.0f ? roundT<T>(z) : 0.0f;
+        te[i] = (float)(j0 + i - total) / te_scale;
+        acc += mt[i];
+      }
+      const int p = j0 / ps, c0 = j0 % ps;
+      T* r = out + (row0 + p) * ld + c0;
+      if constexpr (sizeof(T) == 2) {
+        uint4 w;
+        w.x = pack2bf(te[0], te[1]); w.y = pack2bf(te[2], te[3]); w.z = pack2bf(te[4], te[5]); w.w = pack2bf(te[6], te[7]);
+        *reinterpret_cast<uint4*>(r) = w;
+        w.x = pack2bf(val[0], val[1]); w.y = pack2bf(val[2], val[3]); w.z = pack2bf(val[4], val[5]);
+        w.w = pack2bf(val[6], val[7]);
+        *reinterpret_cast<uint4*>(r + ps) = w;
+        w.x = pack2bf(mt[0], mt[1]); w.y = pack2bf(mt[2], mt[3]); w.z = pack2bf(mt[4], mt[5]); w.w = pack2bf(mt[6], mt[7]);
+        *reinterpret_cast<uint4*>(r + 2 * ps) = w;
+      } else {
+        float4* q4 = reinterpret_cast<float4*>(r);
+        q4[0] = make_float4(te[0], te[1], te[2], te[3]);
+        q4[1] = make_float4(te[4], te[5], te[6], te[7]);
+        q4 = reinterpret_cast<float4*>(r + ps);
+        q4[0] = make_float4(val[0], val[1], val[2], val[3]);
+        q4[1] = make_float4(val[4], val[5], val[6], val[7]);
+        q4 = reinterpret_cast<float4*>(r + 2 * ps);
+        q4[0] = make_float4(mt[0], mt[1], mt[2], mt[3]);
+        q4[1] = make_float4(mt[4], mt[5], mt[6], mt[7]);
+      }
+    }
+    // attention mask per patch: sum of the (rounded) patch mask > 0, over the
+    // patch's cpp adjacent lanes
+    for (int o = 1; o < cpp; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (j0 < total && (k % cpp) == 0) {
+      const int p = j0 / ps;
+      const bool on = acc > 0.0f;
+      tok_mask[row0 + p] = on ? 1 : 0;
+      if (attn_out) attn_out[(size_t)b * P + p] = on ? 1.0f : 0.0f;
+    }
+  }
+  // REG row (zeros) and future rows ([future time enc | 0 | 0])
+  const int extra = use_reg + N;
+  for (int idx = threadIdx.x; idx < extra * 3 * ps; idx += blockDim.x) {
+    const int e = idx / (3 * ps), c = idx % (3 * ps);
+    T* r = out + (row0 + P + e) * ld;
+    float fv = 0.0f;
+    const int n = e - use_reg;
+    if (n >= 0 && c < ps) fv = (float)(n * ps + c) / te_scale;
+    r[c] = fromf<T>(fv);
+  }
+  for (int e = threadIdx.x; e < extra; e += blockDim.x) tok_mask[row0 + P + e] = 1;
+  const int pc = pad_cols - 3 * ps;
+  if (pc > 0)
+    for (int idx = threadIdx.x; idx < S * pc; idx += blockDim.x) {
+      const int rr = idx / pc, c = idx % pc;
+      out[(row0 + rr) * ld + 3 * ps + c] = fromf<T>(0.0f);
+    }
+}
+
+// Vectorised output transform: one thread per 8 consecutive outputs of a
+// (series, quantile, patch) row; 16-byte (bf16) / 32-byte (fp32) loads and stores.
+template <typename T>
+__global__ void __launch_bounds__(256)
+output_transform_vec_kernel(const T* __restrict__ preds, int ld, const float* __restrict__ loc,
+                            const float* __restrict__ scale, T* __restrict__ out, int B, int N, int Q, int ps,
+                            int use_arcsinh) {
+  const int spp = ps / 8;  // segments per patch row
+  const long long total = (long long)B * Q * N * spp;
+  for (long long sidx = (long long)blockIdx.x * blockDim.x + threadIdx.x; sidx < total;
+       sidx += (long long)gridDim.x * blockDim.x) {
+    const int s8 = (int)(sidx % spp);
+    long long t = sidx / spp;
+    const int n = (int)(t % N);
+    t /= N;
+    const int q = (int)(t % Q);
+    const int b = (int)(t / Q);
+    const T* src = preds + ((size_t)b * N + n) * ld + q * ps + 8 * s8;
+    T* dst = out + (((size_t)b * Q + q) * N + n) * ps + 8 * s8;
+    const float sc = scale[b], lo = loc[b];
+    float f[8];
+    if constexpr (sizeof(T) == 2) {
+      const uint4 w = *reinterpret_cast<const uint4*>(src);
+      const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        f[2 * i] = __uint_as_float(u[i] << 16);
+        f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+      }
+    } else {
+      const float4 a = reinterpret_cast<const float4*>(src)[0], e = reinterpret_cast<const float4*>(src)[1];
+      f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = e.x; f[5] = e.y; f[6] = e.z; f[7] = e.w;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float vv = f[i];
+      if (use_arcsinh) vv = sinhf(vv);
+      f[i] = __fadd_rn(__fmul_rn(vv, sc), lo);
+    }
+    if constexpr (sizeof(T) == 2) {
+      uint4 w;
+      w.x = pack2bf(f[0], f[1]); w.y = pack2bf(f[2], f[3]); w.z = pack2bf(f[4], f[5]); w.w = pack2bf(f[6], f[7]);
+      *reinterpret_cast<uint4*>(dst) = w;
+    } else {
+      reinterpret_cast<float4*>(dst)[0] = make_float4(f[0], f[1], f[2], f[3]);
+      reinterpret_cast<float4*>(dst)[1] = make_float4(f[4], f[5], f[6], f[7]);
+    }
+  }
+}
+
+// Vectorised RMSNorm rows: one warp per row, each lane holds VPL = dim / 32
+// values loaded 16 bytes at a time.
+template <typename T, int VPL>
+__global__ void __launch_bounds__(256)
+rmsnorm_rows_vec_kernel(const T* __restrict__ x, int ldx, const T* __restrict__ w, T* __restrict__ y, int ldy,
+                        int rows, int dim, int per, int stride, int offset, float eps) {
+  constexpr int V = 16 / sizeof(T);  // elements per 16-byte access
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= rows) return;
+  const size_t src = (size_t)(warp / per) * stride + offset + warp % per;
+  const T* xr = x + src * ldx;
+  float xv[VPL];
+  float ss = 0.0f;
+#pragma unroll
+  for (int g = 0; g < VPL / V; ++g) {
+    const int c = (g * 32 + lane) * V;
+    const uint4 u = *reinterpret_cast<const uint4*>(xr + c);
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int i = 0; i < V; ++i) {
+      xv[g * V + i] = tof<T>(e[i]);
+      ss += xv[g * V + i] * xv[g * V + i];
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / (float)dim + eps);
+  T* yr = y + (size_t)warp * ldy;
+#pragma unroll
+  for (int g = 0; g < VPL / V; ++g) {
+    const int c = (g * 32 + lane) * V;
+    const uint4 wu = *reinterpret_cast<const uint4*>(w + c);
+    const T* we = reinterpret_cast<const T*>(&wu);
+    uint4 o;
+    T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+    for (int i = 0; i < V; ++i) oe[i] = fromf<T>(tof<T>(we[i]) * roundT<T>(xv[g * V + i] * r));
+    *reinterpret_cast<uint4*>(yr + c) = o;
+  }
+}
+
 template <typename T>
 __global__ void output_transform_kernel(const T* __restrict__ preds, int ld, const float* __restrict__ loc,
                                         const float* __restrict__ scale, T* __restrict__ out, int B,
@@ -182,7 +424,22 @@ int launch_preprocess(const float* context, const float* cmask, int B, int L, in
   CC2_REQUIRE(pad_cols >= 3 * ps && ld >= pad_cols, "preprocess: ld/pad_cols too small");
   const int Leff = L < ctx_len ? L : ctx_len;
   const int P = (Leff + ps - 1) / ps;
-  if (dtype == CC2_BF16) {
+  const int total = P * ps;
+  const size_t esz = dtype == CC2_BF16 ? 2 : 4;
+  // vectorised kernel: patch width 8/16/32, 16-byte aligned rows, <= 8192 positions
+  const bool vec = (ps == 8 || ps == 16 || ps == 32) && ((uintptr_t)patched & 15u) == 0 && (ld * esz) % 16 == 0 &&
+                   total <= 4 * 8 * kPreThreads;
+  const int vec_loads = ((uintptr_t)context & 15u) == 0 && L % 4 == 0 && (L - Leff) % 4 == 0 && (total - Leff) % 4 == 0;
+  const int CH = total <= 8 * kPreThreads ? 1 : total <= 16 * kPreThreads ? 2 : 4;
+#define CC2_PRE_VEC(TT, C_)                                                                                   \
+  preprocess_vec_kernel<TT, C_><<<B, kPreThreads, 0, st>>>(context, cmask, L, Leff, P, ps, te_scale, use_arcsinh, \
+                                                          use_reg ? 1 : 0, N, (TT*)patched, ld, pad_cols, tok, attn,  \
+                                                          loc, scale, vec_loads)
+  if (vec && dtype == CC2_BF16) {
+    if (CH == 1) CC2_PRE_VEC(__nv_bfloat16, 1); else if (CH == 2) CC2_PRE_VEC(__nv_bfloat16, 2); else CC2_PRE_VEC(__nv_bfloat16, 4);
+  } else if (vec && dtype == CC2_F32) {
+    if (CH == 1) CC2_PRE_VEC(float, 1); else if (CH == 2) CC2_PRE_VEC(float, 2); else CC2_PRE_VEC(float, 4);
+  } else if (dtype == CC2_BF16) {
     preprocess_kernel<__nv_bfloat16><<<B, kPreThreads, 0, st>>>(
         context, cmask, L, Leff, P, ps, te_scale, use_arcsinh, use_reg ? 1 : 0, N,
         (__nv_bfloat16*)patched, ld, pad_cols, tok, attn, loc, scale);
@@ -205,6 +462,22 @@ int launch_output_transform(int dtype, const void* preds, int ld, const float* l
   CC2_REQUIRE(preds && loc && scale && out, "output_transform: null pointer");
   const size_t total = (size_t)B * Q * N * ps;
   const int threads = 256;
+  const size_t esz = dtype == CC2_BF16 ? 2 : 4;
+  if (ps % 8 == 0 && ((uintptr_t)preds & 15u) == 0 && ((uintptr_t)out & 15u) == 0 && (ld * esz) % 16 == 0 &&
+      (ps * esz) % 16 == 0) {
+    const size_t segs = total / 8;
+    const int vb = (int)std::min<size_t>((segs + threads - 1) / threads, (size_t)num_sms() * 16);
+    if (dtype == CC2_BF16)
+      output_transform_vec_kernel<__nv_bfloat16><<<vb, threads, 0, st>>>(
+          (const __nv_bfloat16*)preds, ld, loc, scale, (__nv_bfloat16*)out, B, N, Q, ps, use_arcsinh);
+    else if (dtype == CC2_F32)
+      output_transform_vec_kernel<float><<<vb, threads, 0, st>>>((const float*)preds, ld, loc, scale, (float*)out, B,
+                                                                 N, Q, ps, use_arcsinh);
+    else
+      CC2_REQUIRE(false, "output_transform: unsupported dtype %d", dtype);
+    CC2_CHECK_LAUNCH();
+    return CC2_OK;
+  }
   const int blocks = (int)std::min<size_t>((total + threads - 1) / threads, (size_t)num_sms() * 16);
   if (dtype == CC2_BF16)
     output_transform_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(
@@ -224,6 +497,26 @@ int launch_rmsnorm_rows(int dtype, const void* x, int ldx, const void* w, void* 
   CC2_REQUIRE(x && w && y, "rmsnorm_rows: null pointer");
   const int threads = 256;
   const int blocks = (rows * 32 + threads - 1) / threads;
+  const int V = dtype == CC2_BF16 ? 8 : 4;
+  const int vpl = dim / 32;
+  const bool vec = dim % (32 * V) == 0 && (vpl == 8 || vpl == 16 || vpl == 24 || vpl == 32) && ldx % V == 0 &&
+                   ldy % V == 0 && ((uintptr_t)x & 15u) == 0 && ((uintptr_t)w & 15u) == 0 && ((uintptr_t)y & 15u) == 0;
+  if (vec) {
+#define CC2_RMS_VEC(TT, VP)                                                                                     \
+  rmsnorm_rows_vec_kernel<TT, VP><<<blocks, threads, 0, st>>>((const TT*)x, ldx, (const TT*)w, (TT*)y, ldy, rows, dim, \
+                                                              per, stride, offset, eps)
+    if (dtype == CC2_BF16) {
+      if (vpl == 8) CC2_RMS_VEC(__nv_bfloat16, 8); else if (vpl == 16) CC2_RMS_VEC(__nv_bfloat16, 16);
+      else if (vpl == 24) CC2_RMS_VEC(__nv_bfloat16, 24); else CC2_RMS_VEC(__nv_bfloat16, 32);
+    } else if (dtype == CC2_F32) {
+      if (vpl == 8) CC2_RMS_VEC(float, 8); else if (vpl == 16) CC2_RMS_VEC(float, 16);
+      else if (vpl == 24) CC2_RMS_VEC(float, 24); else CC2_RMS_VEC(float, 32);
+    } else {
+      CC2_REQUIRE(false, "rmsnorm_rows: unsupported dtype %d", dtype);
+    }
+    CC2_CHECK_LAUNCH();
+    return CC2_OK;
+  }
   if (dtype == CC2_BF16)
     rmsnorm_rows_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(
         (const __nv_bfloat16*)x, ldx, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, ldy, rows, dim,
