@@ -371,6 +371,39 @@ def run_b200(args):
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_value = world * B * args.steps / (float(t.item()) / 1e3)
 
+        # ---- the same two measurements with CUDA-graph replay (compile_mode) ------
+        model.enable_cuda_graphs(True)
+        try:
+            for _ in range(2):
+                step(ctx)
+            torch.cuda.synchronize()
+            gev, gev_e2e = [], []
+            for i in range(args.steps):
+                flush.fill_(i & 0xFF)
+                a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                step(ctx)
+                b_.record()
+                gev.append((a, b_))
+            for i in range(args.steps):
+                flush.fill_(i & 0xFF)
+                a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                y = step(ctx_host.to(dev, non_blocking=True))
+                out_host.copy_(y, non_blocking=True)
+                b_.record()
+                gev_e2e.append((a, b_))
+            torch.cuda.synchronize()
+            t = torch.tensor([sum(a.elapsed_time(b_) for a, b_ in gev), sum(a.elapsed_time(b_) for a, b_ in gev_e2e)],
+                             device=dev)
+            if world > 1:
+                dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            graph_mode = {"forecasts_per_s": world * B * args.steps / (float(t[0]) / 1e3),
+                          "e2e_forecasts_per_s": world * B * args.steps / (float(t[1]) / 1e3),
+                          "path": "CuteChronos2Model.enable_cuda_graphs (compile_mode): one graph replay per step"}
+        finally:
+            model.enable_cuda_graphs(False)
+
         # ---- p50 batch-1 latency (CUDA graph of one B=1 forward) ---------------
         lat_p50 = None
         if rank == 0 and not args.no_latency:
@@ -432,6 +465,7 @@ def run_b200(args):
             "model_flops_frac": value / world * gflop * 1e9 / (tf_sus * 1e12),
             "gflop_per_forecast": gflop,
             "latency_b1_p50_ms": lat_p50,
+            "graph_mode": graph_mode,
             "other_configs": other,
             "pipeline": pipe_rates,
             "kernels": kernels,

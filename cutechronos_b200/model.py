@@ -239,6 +239,8 @@ class CuteChronos2Model(nn.Module):
         self.register_buffer("quantiles", torch.tensor(config.quantiles, dtype=torch.float32), persistent=False)
         self._engine: _Engine | None = None
         self._engine_key = None
+        self._cuda_graphs = False
+        self._graphs: dict = {}
         self._tubroquant_config: dict | None = None
         self._tq_state = None  # (engine, per-layer params, stats tensor) of the enabled hook
         self._tq_last_rows = 0
@@ -304,9 +306,17 @@ class CuteChronos2Model(nn.Module):
             if max_group > 1:
                 gid_host = g
         cfg = self.config
+        if (self._cuda_graphs and gid_host is None and not torch.cuda.is_current_stream_capturing()):
+            return self._forward_graph(eng, dev, ctx, mask, B, L, N)
         out = torch.empty(B, cfg.num_quantiles, N * cfg.output_patch_size, dtype=eng.dtype, device=dev)
         self._last_loc = torch.empty(B, dtype=torch.float32, device=dev)
         self._last_scale = torch.empty(B, dtype=torch.float32, device=dev)
+        self._native_forward(eng, dev, ctx, mask, gid_host, B, L, N, max_group, out, self._last_loc,
+                             self._last_scale)
+        return out
+
+    def _native_forward(self, eng, dev, ctx, mask, gid_host, B, L, N, max_group, out, loc, scale):
+        cfg = self.config
         ws, ws_bytes = eng.workspace(B, L, N, max_group)
         tq = self._turboquant_for(eng, dev)
         if tq is not None:
@@ -317,10 +327,70 @@ class CuteChronos2Model(nn.Module):
         with torch.cuda.device(dev):
             st = eng._lib.cc2_forward(
                 eng.handle, _ptr(ctx), _ptr(mask) if mask is not None else None, B, L, N,
-                gid_host.data_ptr() if gid_host is not None else None, _ptr(out),
-                _ptr(self._last_loc), _ptr(self._last_scale), ws, ws_bytes, stream)
+                gid_host.data_ptr() if gid_host is not None else None, _ptr(out), _ptr(loc), _ptr(scale), ws,
+                ws_bytes, stream)
         nat.check(st, "cc2_forward")
-        return out
+        return ws
+
+    # -- CUDA-graph replay (the reference's compile_mode, model.py:1065-1140) ---------------
+    def enable_cuda_graphs(self, enabled: bool = True) -> "CuteChronos2Model":
+        """Replay one captured CUDA graph per (B, L, N, mask) shape instead of
+        launching the forward's kernels one by one (the role torch.compile's
+        "reduce-overhead" mode plays in the reference).  Series groups (group
+        ids with repeated values) run eagerly.  Each call copies its inputs
+        into the graph's buffers and returns copies of its outputs."""
+        self._cuda_graphs = bool(enabled)
+        self._graphs = {}
+        return self
+
+    def _forward_graph(self, eng, dev, ctx, mask, B, L, N):
+        cfg = self.config
+        ws_now = eng._ws.data_ptr() if eng._ws is not None else None
+        key = (B, L, N, mask is not None, str(dev))
+        ent = self._graphs.get(key)
+        tq_id = id(self._tq_state) if self._tubroquant_config is not None else None
+        if ent is not None and (ent["eng"] is not eng or ent["tq"] != tq_id or ent["ws"] != ws_now):
+            ent = None
+        if ent is None:
+            ent = {"ctx": torch.empty_like(ctx), "mask": torch.empty_like(mask) if mask is not None else None,
+                   "out": torch.empty(B, cfg.num_quantiles, N * cfg.output_patch_size, dtype=eng.dtype, device=dev),
+                   "loc": torch.empty(B, dtype=torch.float32, device=dev),
+                   "scale": torch.empty(B, dtype=torch.float32, device=dev)}
+            ent["ctx"].copy_(ctx)
+            if mask is not None:
+                ent["mask"].copy_(mask)
+            s = torch.cuda.Stream(dev)
+            s.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(s):
+                # an eager run first: sizes the workspace and sets kernel attributes
+                self._native_forward(eng, dev, ent["ctx"], ent["mask"], None, B, L, N, 1, ent["out"], ent["loc"],
+                                     ent["scale"])
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    ws = self._native_forward(eng, dev, ent["ctx"], ent["mask"], None, B, L, N, 1, ent["out"],
+                                              ent["loc"], ent["scale"])
+            torch.cuda.current_stream(dev).wait_stream(s)
+            # graphs of other shapes hold the workspace address they were captured with
+            ws_addr = eng._ws.data_ptr()
+            self._graphs = {k: e for k, e in self._graphs.items() if e["ws"] == ws_addr}
+            ent.update(graph=g, eng=eng, ws=ws_addr,
+                       tq=id(self._tq_state) if self._tubroquant_config is not None else None)
+            self._graphs[key] = ent
+        else:
+            ent["ctx"].copy_(ctx)
+            if mask is not None:
+                ent["mask"].copy_(mask)
+            ent["graph"].replay()
+        self._last_loc = ent["loc"].clone()
+        self._last_scale = ent["scale"].clone()
+        return ent["out"].clone()
+
+    @classmethod
+    def from_pretrained_compiled(cls, model_path: str | Path, compile_mode: str = "reduce-overhead",
+                                 adapter_path: str | Path | None = None) -> "CuteChronos2Model":
+        """from_pretrained with CUDA-graph replay on (model.py:1065-1084);
+        ``compile_mode`` is accepted for the reference's signature."""
+        return cls.from_pretrained(model_path, adapter_path=adapter_path).enable_cuda_graphs(True)
 
     # -- TurboQuant K/V hook (model.py:615-688) ------------------------------------------
     def enable_turboquant_kv(self, bits: int = 4, *, key_mode: str = "prod", value_mode: str = "mse",

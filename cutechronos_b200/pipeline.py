@@ -125,14 +125,17 @@ class CuteChronos2Pipeline:
     @classmethod
     def from_pretrained(cls, model_path: str, *, device: str = "cuda", dtype: torch.dtype = torch.bfloat16,
                         use_cute: bool = True, compile_mode: str | None = None) -> "CuteChronos2Pipeline":
-        """Load a local Chronos-2 checkpoint directory.  ``compile_mode`` is
-        accepted for API compatibility and ignored (the engine has no tracing
-        compiler; use CUDA graphs for launch-bound batch sizes)."""
+        """Load a local Chronos-2 checkpoint directory.  A ``compile_mode``
+        (the reference's torch.compile mode, e.g. "reduce-overhead") turns on
+        CUDA-graph replay of the forward per input shape; there is no tracing
+        compiler."""
         if not use_cute:
             raise NotImplementedError("use_cute=False (upstream Chronos2Pipeline) is not part of this engine")
         if not Path(model_path).is_dir():
             raise FileNotFoundError(f"{model_path} is not a local checkpoint directory")
         model = CuteChronos2Model.from_pretrained(model_path).to(device=device, dtype=dtype).eval()
+        if compile_mode:
+            model.enable_cuda_graphs(True)
         return cls(model, device=device)
 
     # -- helpers (pipeline.py:221-322) ---------------------------------------------------

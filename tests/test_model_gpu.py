@@ -171,3 +171,25 @@ def test_cpu_model_raises():
     m = CuteChronos2Model(small_config())
     with pytest.raises(RuntimeError, match="CUDA"):
         m(torch.randn(1, 32))
+
+
+def test_cuda_graph_replay_equals_eager(small_bf16):
+    """enable_cuda_graphs: one graph per shape, replays equal eager runs,
+    shape changes (workspace regrowth) recapture, outputs are copies."""
+    g = torch.Generator().manual_seed(5)
+    xs = [torch.randn(4, 300, generator=g), torch.randn(4, 300, generator=g), torch.randn(9, 700, generator=g),
+          torch.randn(4, 300, generator=g)]
+    eager = [small_bf16(x.to(DEV), num_output_patches=3).cpu() for x in xs]
+    small_bf16.enable_cuda_graphs(True)
+    try:
+        outs = [small_bf16(x.to(DEV), num_output_patches=3) for x in xs]
+        assert outs[0].data_ptr() != outs[1].data_ptr()
+        for o, e in zip(outs, eager):
+            assert torch.equal(o.cpu(), e)
+        # series groups run eagerly under the same switch
+        gid = torch.tensor([0, 0, 1, 1])
+        assert torch.equal(small_bf16(xs[0].to(DEV), num_output_patches=3, group_ids=gid).cpu(),
+                           small_bf16.__class__.forward(small_bf16, xs[0].to(DEV), num_output_patches=3,
+                                                        group_ids=gid).cpu())
+    finally:
+        small_bf16.enable_cuda_graphs(False)
