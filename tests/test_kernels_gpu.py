@@ -174,7 +174,10 @@ def test_linear_fused_epilogues(M, N, Kd, dtype):
     assert torch.allclose(so.cpu(), kk.row_sumsq_parts(out.cpu()), rtol=1e-4, atol=1e-3)
 
 
-@pytest.mark.parametrize("M,N,Kd", [(129, 768, 768), (34048, 768, 768), (1000, 2304, 768), (777, 336, 3840)])
+# (34048, 768) and (34048, 2304): the 2-SM kernel's last partial wave runs as
+# 256 x 128 half units; (40000, 336): half units past N and a partial group
+@pytest.mark.parametrize("M,N,Kd", [(129, 768, 768), (34048, 768, 768), (1000, 2304, 768), (777, 336, 3840),
+                                    (34048, 2304, 768), (40000, 336, 256)])
 def test_gemm_pair_vs_single_sm_tiles(M, N, Kd):
     # the 2-SM (cta_group::2) and 1-SM tile paths give the same result
     from cutechronos_b200 import _native as nat
