@@ -138,6 +138,8 @@ template <bool ROPE>
 __global__ void __launch_bounds__(128)
 attn_mma_kernel(const bf16* __restrict__ qkv, int ld, int qcol, int kcol, int vcol, bf16* __restrict__ out,
                 int ldo, const uint8_t* __restrict__ tok, const float2* __restrict__ rope, SetInfo si) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ __align__(16) bf16 Qs[QT][LDS];
   __shared__ __align__(16) bf16 Ks[KT][LDS];
   __shared__ __align__(16) bf16 Vs[KT][LDS];
@@ -350,6 +352,8 @@ template <bool ROPE>
 __global__ void __launch_bounds__(kSetMaxWarps * 32, 2)
 attn_set_kernel(const bf16* __restrict__ qkv, int ld, int qcol, int kcol, int vcol, bf16* __restrict__ out,
                 int ldo, const uint8_t* __restrict__ tok, const float2* __restrict__ rope, SetInfo si) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const SetGeom g = set_geom(si, blockIdx.y);
   const int h = blockIdx.x;
@@ -502,6 +506,8 @@ template <typename T, bool ROPE>
 __global__ void __launch_bounds__(128)
 attn_simt_kernel(const T* __restrict__ qkv, int ld, int qcol, int kcol, int vcol, T* __restrict__ out, int ldo,
                  const uint8_t* __restrict__ tok, const float2* __restrict__ rope, SetInfo si) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float Qs[SQ][DH];
   __shared__ float Ks[SK][DH + 1];
   __shared__ float Vs[SK][DH];
@@ -635,6 +641,8 @@ template <typename T>
 __global__ void __launch_bounds__(256)
 attn_group_small_kernel(const T* __restrict__ qkv, int ld, int qcol, int kcol, int vcol, T* __restrict__ out,
                         int ldo, const uint8_t* __restrict__ tok, SetInfo si, int heads) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   const SetGeom g = set_geom(si, blockIdx.x);
   const int n = g.n;
@@ -756,6 +764,7 @@ struct PersistArgs {
 __global__ void __launch_bounds__(kPWarps * 32, 1)
 attn_persist_kernel(const __grid_constant__ CUtensorMap tmQKV, bf16* __restrict__ out, int ldo,
                     const uint8_t* __restrict__ tok, PersistArgs a, int* __restrict__ err) {
+  pdl_launch_dependents();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full_bar[kPBufs];
@@ -815,6 +824,7 @@ attn_persist_kernel(const __grid_constant__ CUtensorMap tmQKV, bf16* __restrict_
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   __syncthreads();
+  pdl_wait();  // the kernel before may still run until here; activations are read from now on
   if (warp < a.nbufs && warp < my_items) issue(warp);
 
   while (true) {
@@ -1016,16 +1026,16 @@ int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int
       int* err = nullptr;
       CC2_CUDA(cudaGetSymbolAddress((void**)&err, g_attn_error));
       const int grid = std::min(num_sets * heads, num_sms());
-      attn_persist_kernel<<<grid, kPWarps * 32, smem_p, st>>>(map, (bf16*)out, ldo, tok, pa, err);
+      CC2_CUDA(launch_k(attn_persist_kernel, grid, kPWarps * 32, smem_p, st, map, (bf16*)out, ldo, tok, pa, err));
     } else if (mode == 1 && max_group <= kSmallGroupMax) {
       const size_t sm = small_group_smem(max_group, heads, sizeof(bf16));
       CC2_TRY(set_small_group_attr<bf16>(sm));
-      attn_group_small_kernel<bf16><<<num_sets, 256, sm, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out,
-                                                               ldo, tok, si, heads);
+      CC2_CUDA(launch_k(attn_group_small_kernel<bf16>, num_sets, 256, sm, st, (const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out,
+                                                               ldo, tok, si, heads));
     } else if (mode == 1 && max_group <= SK) {
       dim3 grid((nmax + SQ - 1) / SQ, heads, num_sets);
-      attn_simt_kernel<bf16, false><<<grid, 128, 0, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out,
-                                                          ldo, tok, cs, si);
+      CC2_CUDA(launch_k(attn_simt_kernel<bf16, false>, grid, 128, 0, st, (const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out,
+                                                          ldo, tok, cs, si));
     } else if (smem <= kSetSmemLimit) {
       static unsigned long long attr_done = 0;  // one bit per device
       int dev = 0;
@@ -1039,33 +1049,33 @@ int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int
       }
       dim3 grid(heads, num_sets);
       if (mode == 0 && cs)
-        attn_set_kernel<true><<<grid, warps * 32, smem, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out,
-                                                              ldo, tok, cs, si);
+        CC2_CUDA(launch_k(attn_set_kernel<true>, grid, warps * 32, smem, st, (const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out,
+                                                              ldo, tok, cs, si));
       else
-        attn_set_kernel<false><<<grid, warps * 32, smem, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol,
-                                                               (bf16*)out, ldo, tok, cs, si);
+        CC2_CUDA(launch_k(attn_set_kernel<false>, grid, warps * 32, smem, st, (const bf16*)qkv, ld, qcol, kcol, vcol,
+                                                               (bf16*)out, ldo, tok, cs, si));
     } else {
       dim3 grid((nmax + QT - 1) / QT, heads, num_sets);
       if (mode == 0 && cs)
-        attn_mma_kernel<true><<<grid, 128, 0, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out, ldo,
-                                                    tok, cs, si);
+        CC2_CUDA(launch_k(attn_mma_kernel<true>, grid, 128, 0, st, (const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out, ldo,
+                                                    tok, cs, si));
       else
-        attn_mma_kernel<false><<<grid, 128, 0, st>>>((const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out, ldo,
-                                                     tok, cs, si);
+        CC2_CUDA(launch_k(attn_mma_kernel<false>, grid, 128, 0, st, (const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out, ldo,
+                                                     tok, cs, si));
     }
   } else if (dtype == CC2_F32 && mode == 1 && max_group <= kSmallGroupMax) {
     const size_t sm = small_group_smem(max_group, heads, sizeof(float));
     CC2_TRY(set_small_group_attr<float>(sm));
-    attn_group_small_kernel<float><<<num_sets, 256, sm, st>>>((const float*)qkv, ld, qcol, kcol, vcol, (float*)out,
-                                                              ldo, tok, si, heads);
+    CC2_CUDA(launch_k(attn_group_small_kernel<float>, num_sets, 256, sm, st, (const float*)qkv, ld, qcol, kcol, vcol, (float*)out,
+                                                              ldo, tok, si, heads));
   } else if (dtype == CC2_F32) {
     dim3 grid((nmax + SQ - 1) / SQ, heads, num_sets);
     if (mode == 0 && cs)
-      attn_simt_kernel<float, true><<<grid, 128, 0, st>>>((const float*)qkv, ld, qcol, kcol, vcol, (float*)out,
-                                                          ldo, tok, cs, si);
+      CC2_CUDA(launch_k(attn_simt_kernel<float, true>, grid, 128, 0, st, (const float*)qkv, ld, qcol, kcol, vcol, (float*)out,
+                                                          ldo, tok, cs, si));
     else
-      attn_simt_kernel<float, false><<<grid, 128, 0, st>>>((const float*)qkv, ld, qcol, kcol, vcol, (float*)out,
-                                                           ldo, tok, cs, si);
+      CC2_CUDA(launch_k(attn_simt_kernel<float, false>, grid, 128, 0, st, (const float*)qkv, ld, qcol, kcol, vcol, (float*)out,
+                                                           ldo, tok, cs, si));
   } else {
     CC2_REQUIRE(false, "attention: unsupported dtype %d", dtype);
   }

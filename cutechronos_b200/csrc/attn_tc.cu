@@ -193,6 +193,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__ CUtensorMap tmQ1,
                const __grid_constant__ CUtensorMap tmKV, bf16* __restrict__ out, const uint8_t* __restrict__ tok,
                Args a, int* __restrict__ err) {
+  pdl_launch_dependents();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   __shared__ __align__(8) uint64_t full_qk[kMaxStages], full_v[kMaxStages], empty_qk[kMaxStages],
@@ -235,6 +236,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // the kernel before may still run until here; activations are read from now on
   const uint32_t tmem = tmem_slot;
 
   if (warp == 0) {
@@ -555,11 +557,11 @@ int launch_attn_tc(const void* qkv, int ld, int qcol, int kcol, int vcol, void* 
   }
   const int grid = std::min(a.items, 2 * num_sms());
   if (a.NK <= 64)
-    attn_tc_kernel<64><<<grid, kThreads, smem, st>>>(mq0, mq1, mkv, (bf16*)out, tok, a, err);
+    CC2_CUDA(launch_k(attn_tc_kernel<64>, grid, kThreads, smem, st, mq0, mq1, mkv, (bf16*)out, tok, a, err));
   else if (a.NK <= 128)
-    attn_tc_kernel<128><<<grid, kThreads, smem, st>>>(mq0, mq1, mkv, (bf16*)out, tok, a, err);
+    CC2_CUDA(launch_k(attn_tc_kernel<128>, grid, kThreads, smem, st, mq0, mq1, mkv, (bf16*)out, tok, a, err));
   else
-    attn_tc_kernel<144><<<grid, kThreads, smem, st>>>(mq0, mq1, mkv, (bf16*)out, tok, a, err);
+    CC2_CUDA(launch_k(attn_tc_kernel<144>, grid, kThreads, smem, st, mq0, mq1, mkv, (bf16*)out, tok, a, err));
   CC2_CHECK_LAUNCH();
   return CC2_OK;
 }

@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/cc2.h"
 
@@ -90,5 +91,38 @@ template <typename T> __device__ __forceinline__ T fromf(float x) { return Elem<
 template <typename T> __device__ __forceinline__ float roundT(float x) { return tof<T>(fromf<T>(x)); }
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// ---- programmatic dependent launch ------------------------------------------
+// Every kernel of the forward is launched with programmatic stream
+// serialization (unless turned off by cc2_set_launch_overlap): it may start
+// while the kernel before it on the stream is still running.  Each kernel
+// therefore (1) signals at its start that the next one may be scheduled and
+// (2) executes pdl_wait() - which returns once the previous kernel has
+// completed and its writes are visible - before it reads or writes any
+// activation memory; only its prologue (barrier set-up, TMEM allocation,
+// descriptor prefetch, weight-only work) overlaps the previous kernel.
+// Outside a programmatic launch both instructions are no-ops.
+extern int g_launch_overlap;
+
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                            Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = g_launch_overlap ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace cc2

@@ -33,6 +33,9 @@
 
 namespace cc2 {
 
+// programmatic dependent launch of the forward's kernels (1 = on)
+int g_launch_overlap = 1;
+
 // ---- status -----------------------------------------------------------------
 static thread_local std::string t_error;
 void set_error(const char* fmt, ...) {
@@ -775,6 +778,12 @@ int cc2_set_gemm_variant(int variant) {
 int cc2_set_attention_variant(int variant) {
   const int old = g_attn_variant;
   g_attn_variant = (variant == 1 || variant == 2) ? variant : 0;
+  return old;
+}
+
+int cc2_set_launch_overlap(int enabled) {
+  const int old = g_launch_overlap;
+  g_launch_overlap = enabled ? 1 : 0;
   return old;
 }
 

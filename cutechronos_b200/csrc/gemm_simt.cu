@@ -31,6 +31,8 @@ template <bool SPLIT>
 __global__ void __launch_bounds__(kThreads)
 gemm_f32_kernel(const float* __restrict__ A, int lda, const float* __restrict__ W, int ldw, float* out, int ldo,
                 int M, int N, int K, cc2_epilogue ep, int kchunk, float* __restrict__ part) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float As[2][TK][TM + 4];
   __shared__ float Ws[2][TK][TN + 4];
   const int tid = threadIdx.x;
@@ -127,6 +129,8 @@ gemm_f32_kernel(const float* __restrict__ A, int lda, const float* __restrict__ 
 __global__ void __launch_bounds__(256)
 splitk_epilogue_kernel(const float* __restrict__ part, int slices, float* out, int ldo, int M, int N,
                        cc2_epilogue ep) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int groups = (N + 63) / 64;
   if (warp >= M * groups) return;
@@ -181,17 +185,17 @@ int launch_gemm_f32(const void* A, int lda, const void* W, int ldw, void* out, i
     const int kchunk = ((K + slices - 1) / slices + TK - 1) / TK * TK;
     slices = (K + kchunk - 1) / kchunk;
     dim3 grid((N + TN - 1) / TN, (M + TM - 1) / TM, slices);
-    gemm_f32_kernel<true><<<grid, kThreads, 0, st>>>((const float*)A, lda, (const float*)W, ldw, nullptr, 0, M, N,
-                                                     K, ep, kchunk, scratch);
+    CC2_CUDA(launch_k(gemm_f32_kernel<true>, grid, kThreads, 0, st, (const float*)A, lda, (const float*)W, ldw, nullptr, 0, M, N,
+                                                     K, ep, kchunk, scratch));
     CC2_CHECK_LAUNCH();
     const int warps = M * ((N + 63) / 64);
-    splitk_epilogue_kernel<<<(warps * 32 + 255) / 256, 256, 0, st>>>(scratch, slices, (float*)out, ldo, M, N, ep);
+    CC2_CUDA(launch_k(splitk_epilogue_kernel, (warps * 32 + 255) / 256, 256, 0, st, scratch, slices, (float*)out, ldo, M, N, ep));
     CC2_CHECK_LAUNCH();
     return CC2_OK;
   }
   dim3 grid((N + TN - 1) / TN, (M + TM - 1) / TM);
-  gemm_f32_kernel<false><<<grid, kThreads, 0, st>>>((const float*)A, lda, (const float*)W, ldw, (float*)out, ldo, M,
-                                                    N, K, ep, K, nullptr);
+  CC2_CUDA(launch_k(gemm_f32_kernel<false>, grid, kThreads, 0, st, (const float*)A, lda, (const float*)W, ldw, (float*)out, ldo, M,
+                                                    N, K, ep, K, nullptr));
   CC2_CHECK_LAUNCH();
   return CC2_OK;
 }

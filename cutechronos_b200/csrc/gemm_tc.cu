@@ -333,6 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, int M, int N,
                int K, Epi ep) {
+  pdl_launch_dependents();
   using C = Cfg<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -376,6 +377,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  pdl_wait();  // the kernel before may still run until here; activations are read from now on
   const uint32_t tmem_base = *tmem_slot;
 
   const int m_tiles = (M + BM - 1) / BM;
@@ -605,6 +607,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                  const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, int M, int N,
                  int K, Epi ep) {
+  pdl_launch_dependents();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* epi_smem = smem + STAGES * STAGE_BYTES;
@@ -652,6 +655,7 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   tc_fence_before();
   cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
+  pdl_wait();  // the kernel before may still run until here; activations are read from now on
   const uint32_t tmem_base = *tmem_slot;
 
   const int m_tiles = (M + 255) / 256;
@@ -877,7 +881,7 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMa
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  gemm_tc_kernel<BN><<<grid, kThreads, C::SMEM, st>>>(ma, mb, mc, mr, M, N, K, ep);
+  CC2_CUDA(launch_k(gemm_tc_kernel<BN>, grid, kThreads, C::SMEM, st, ma, mb, mc, mr, M, N, K, ep));
   CC2_CHECK_LAUNCH();
   return CC2_OK;
 }
@@ -901,13 +905,15 @@ static int launch_pair_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUt
   cfg.blockDim = dim3(pair::THREADS, 1, 1);
   cfg.dynamicSmemBytes = SMEM;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = g_launch_overlap ? 2 : 1;
   CC2_CUDA(cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<F, STAGES, BOXES, SKIP_EPI>, ma, mb, mc, mr, M, N, K,
                               ep));
   return CC2_OK;

@@ -216,6 +216,8 @@ __global__ void __launch_bounds__(kWarps * 32)
 kv_quant_kernel(T* __restrict__ qkv, int ld, int rows, int q_col, int k_col, int v_col, int heads, cc2_kvq kp,
                 cc2_kvq vp, int has_k, int has_v, const float2* __restrict__ rope, int rope_period,
                 float* __restrict__ stats) {
+  pdl_launch_dependents();
+  pdl_wait();
   extern __shared__ __align__(16) float dyn[];
   __shared__ QTab tab[2];
   __shared__ float scratch[kWarps][64];
@@ -334,12 +336,12 @@ int launch_kv_quant(int dtype, void* qkv, int ld, int rows, int q_col, int k_col
   const int grid = (int)std::min<long long>((vecs + kWarps - 1) / kWarps, 4LL * num_sms());
   const float2* cs = (const float2*)rope_cs;
   if (dtype == CC2_BF16)
-    kv_quant_kernel<__nv_bfloat16><<<grid, kWarps * 32, smem, st>>>((__nv_bfloat16*)qkv, ld, rows, q_col, k_col,
+    CC2_CUDA(launch_k(kv_quant_kernel<__nv_bfloat16>, grid, kWarps * 32, smem, st, (__nv_bfloat16*)qkv, ld, rows, q_col, k_col,
                                                                    v_col, heads, kp, vp, key != nullptr,
-                                                                   value != nullptr, cs, rope_period, stats);
+                                                                   value != nullptr, cs, rope_period, stats));
   else if (dtype == CC2_F32)
-    kv_quant_kernel<float><<<grid, kWarps * 32, smem, st>>>((float*)qkv, ld, rows, q_col, k_col, v_col, heads, kp, vp,
-                                                            key != nullptr, value != nullptr, cs, rope_period, stats);
+    CC2_CUDA(launch_k(kv_quant_kernel<float>, grid, kWarps * 32, smem, st, (float*)qkv, ld, rows, q_col, k_col, v_col, heads, kp, vp,
+                                                            key != nullptr, value != nullptr, cs, rope_period, stats));
   else
     CC2_REQUIRE(false, "kv_quant: unsupported dtype %d", dtype);
   CC2_CHECK_LAUNCH();

@@ -42,6 +42,8 @@ preprocess_kernel(const float* __restrict__ ctx, const float* __restrict__ cmask
                   T* __restrict__ out, int ld, int pad_cols, uint8_t* __restrict__ tok_mask,
                   float* __restrict__ attn_out, float* __restrict__ loc_out,
                   float* __restrict__ scale_out) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ double red[kPreThreads / 32];
   __shared__ float s_loc, s_scale;
   const int b = blockIdx.x;
@@ -145,6 +147,8 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
                       float te_scale, int use_arcsinh, int use_reg, int N, T* __restrict__ out, int ld,
                       int pad_cols, uint8_t* __restrict__ tok_mask, float* __restrict__ attn_out,
                       float* __restrict__ loc_out, float* __restrict__ scale_out, int vec_loads) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ double red[kPreThreads / 32];
   const int b = blockIdx.x;
   const int S = P + use_reg + N;
@@ -287,6 +291,8 @@ __global__ void __launch_bounds__(256)
 output_transform_vec_kernel(const T* __restrict__ preds, int ld, const float* __restrict__ loc,
                             const float* __restrict__ scale, T* __restrict__ out, int B, int N, int Q, int ps,
                             int use_arcsinh) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int spp = ps / 8;  // segments per patch row
   const long long total = (long long)B * Q * N * spp;
   for (long long sidx = (long long)blockIdx.x * blockDim.x + threadIdx.x; sidx < total;
@@ -336,6 +342,8 @@ template <typename T, int VPL>
 __global__ void __launch_bounds__(256)
 rmsnorm_rows_vec_kernel(const T* __restrict__ x, int ldx, const T* __restrict__ w, T* __restrict__ y, int ldy,
                         int rows, int dim, int per, int stride, int offset, float eps) {
+  pdl_launch_dependents();
+  pdl_wait();
   constexpr int V = 16 / sizeof(T);  // elements per 16-byte access
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -375,6 +383,8 @@ template <typename T>
 __global__ void output_transform_kernel(const T* __restrict__ preds, int ld, const float* __restrict__ loc,
                                         const float* __restrict__ scale, T* __restrict__ out, int B,
                                         int N, int Q, int ps, int use_arcsinh) {
+  pdl_launch_dependents();
+  pdl_wait();
   const size_t H = (size_t)N * ps;
   const size_t total = (size_t)B * Q * H;
   for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total;
@@ -394,6 +404,8 @@ template <typename T>
 __global__ void rmsnorm_rows_kernel(const T* __restrict__ x, int ldx, const T* __restrict__ w,
                                     T* __restrict__ y, int ldy, int rows, int dim, int per,
                                     int stride, int offset, float eps) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= rows) return;
@@ -432,22 +444,22 @@ int launch_preprocess(const float* context, const float* cmask, int B, int L, in
   const int vec_loads = ((uintptr_t)context & 15u) == 0 && L % 4 == 0 && (L - Leff) % 4 == 0 && (total - Leff) % 4 == 0;
   const int CH = total <= 8 * kPreThreads ? 1 : total <= 16 * kPreThreads ? 2 : 4;
 #define CC2_PRE_VEC(TT, C_)                                                                                   \
-  preprocess_vec_kernel<TT, C_><<<B, kPreThreads, 0, st>>>(context, cmask, L, Leff, P, ps, te_scale, use_arcsinh, \
+  CC2_CUDA(launch_k(preprocess_vec_kernel<TT, C_>, B, kPreThreads, 0, st, context, cmask, L, Leff, P, ps, te_scale, use_arcsinh, \
                                                           use_reg ? 1 : 0, N, (TT*)patched, ld, pad_cols, tok, attn,  \
-                                                          loc, scale, vec_loads)
+                                                          loc, scale, vec_loads))
   if (vec && dtype == CC2_BF16) {
     if (CH == 1) CC2_PRE_VEC(__nv_bfloat16, 1); else if (CH == 2) CC2_PRE_VEC(__nv_bfloat16, 2); else CC2_PRE_VEC(__nv_bfloat16, 4);
   } else if (vec && dtype == CC2_F32) {
     if (CH == 1) CC2_PRE_VEC(float, 1); else if (CH == 2) CC2_PRE_VEC(float, 2); else CC2_PRE_VEC(float, 4);
   } else if (dtype == CC2_BF16) {
-    preprocess_kernel<__nv_bfloat16><<<B, kPreThreads, 0, st>>>(
+    CC2_CUDA(launch_k(preprocess_kernel<__nv_bfloat16>, B, kPreThreads, 0, st, 
         context, cmask, L, Leff, P, ps, te_scale, use_arcsinh, use_reg ? 1 : 0, N,
-        (__nv_bfloat16*)patched, ld, pad_cols, tok, attn, loc, scale);
+        (__nv_bfloat16*)patched, ld, pad_cols, tok, attn, loc, scale));
   } else if (dtype == CC2_F32) {
-    preprocess_kernel<float><<<B, kPreThreads, 0, st>>>(context, cmask, L, Leff, P, ps, te_scale,
+    CC2_CUDA(launch_k(preprocess_kernel<float>, B, kPreThreads, 0, st, context, cmask, L, Leff, P, ps, te_scale,
                                                         use_arcsinh, use_reg ? 1 : 0, N,
                                                         (float*)patched, ld, pad_cols, tok, attn,
-                                                        loc, scale);
+                                                        loc, scale));
   } else {
     CC2_REQUIRE(false, "preprocess: unsupported dtype %d", dtype);
   }
@@ -468,11 +480,11 @@ int launch_output_transform(int dtype, const void* preds, int ld, const float* l
     const size_t segs = total / 8;
     const int vb = (int)std::min<size_t>((segs + threads - 1) / threads, (size_t)num_sms() * 16);
     if (dtype == CC2_BF16)
-      output_transform_vec_kernel<__nv_bfloat16><<<vb, threads, 0, st>>>(
-          (const __nv_bfloat16*)preds, ld, loc, scale, (__nv_bfloat16*)out, B, N, Q, ps, use_arcsinh);
+      CC2_CUDA(launch_k(output_transform_vec_kernel<__nv_bfloat16>, vb, threads, 0, st, 
+          (const __nv_bfloat16*)preds, ld, loc, scale, (__nv_bfloat16*)out, B, N, Q, ps, use_arcsinh));
     else if (dtype == CC2_F32)
-      output_transform_vec_kernel<float><<<vb, threads, 0, st>>>((const float*)preds, ld, loc, scale, (float*)out, B,
-                                                                 N, Q, ps, use_arcsinh);
+      CC2_CUDA(launch_k(output_transform_vec_kernel<float>, vb, threads, 0, st, (const float*)preds, ld, loc, scale, (float*)out, B,
+                                                                 N, Q, ps, use_arcsinh));
     else
       CC2_REQUIRE(false, "output_transform: unsupported dtype %d", dtype);
     CC2_CHECK_LAUNCH();
@@ -480,11 +492,11 @@ int launch_output_transform(int dtype, const void* preds, int ld, const float* l
   }
   const int blocks = (int)std::min<size_t>((total + threads - 1) / threads, (size_t)num_sms() * 16);
   if (dtype == CC2_BF16)
-    output_transform_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(
-        (const __nv_bfloat16*)preds, ld, loc, scale, (__nv_bfloat16*)out, B, N, Q, ps, use_arcsinh);
+    CC2_CUDA(launch_k(output_transform_kernel<__nv_bfloat16>, blocks, threads, 0, st, 
+        (const __nv_bfloat16*)preds, ld, loc, scale, (__nv_bfloat16*)out, B, N, Q, ps, use_arcsinh));
   else if (dtype == CC2_F32)
-    output_transform_kernel<float><<<blocks, threads, 0, st>>>((const float*)preds, ld, loc, scale,
-                                                                (float*)out, B, N, Q, ps, use_arcsinh);
+    CC2_CUDA(launch_k(output_transform_kernel<float>, blocks, threads, 0, st, (const float*)preds, ld, loc, scale,
+                                                                (float*)out, B, N, Q, ps, use_arcsinh));
   else
     CC2_REQUIRE(false, "output_transform: unsupported dtype %d", dtype);
   CC2_CHECK_LAUNCH();
@@ -503,8 +515,8 @@ int launch_rmsnorm_rows(int dtype, const void* x, int ldx, const void* w, void* 
                    ldy % V == 0 && ((uintptr_t)x & 15u) == 0 && ((uintptr_t)w & 15u) == 0 && ((uintptr_t)y & 15u) == 0;
   if (vec) {
 #define CC2_RMS_VEC(TT, VP)                                                                                     \
-  rmsnorm_rows_vec_kernel<TT, VP><<<blocks, threads, 0, st>>>((const TT*)x, ldx, (const TT*)w, (TT*)y, ldy, rows, dim, \
-                                                              per, stride, offset, eps)
+  CC2_CUDA(launch_k(rmsnorm_rows_vec_kernel<TT, VP>, blocks, threads, 0, st, (const TT*)x, ldx, (const TT*)w, (TT*)y, ldy, rows, dim, \
+                                                              per, stride, offset, eps))
     if (dtype == CC2_BF16) {
       if (vpl == 8) CC2_RMS_VEC(__nv_bfloat16, 8); else if (vpl == 16) CC2_RMS_VEC(__nv_bfloat16, 16);
       else if (vpl == 24) CC2_RMS_VEC(__nv_bfloat16, 24); else CC2_RMS_VEC(__nv_bfloat16, 32);
@@ -518,13 +530,13 @@ int launch_rmsnorm_rows(int dtype, const void* x, int ldx, const void* w, void* 
     return CC2_OK;
   }
   if (dtype == CC2_BF16)
-    rmsnorm_rows_kernel<__nv_bfloat16><<<blocks, threads, 0, st>>>(
+    CC2_CUDA(launch_k(rmsnorm_rows_kernel<__nv_bfloat16>, blocks, threads, 0, st, 
         (const __nv_bfloat16*)x, ldx, (const __nv_bfloat16*)w, (__nv_bfloat16*)y, ldy, rows, dim,
-        per, stride, offset, eps);
+        per, stride, offset, eps));
   else if (dtype == CC2_F32)
-    rmsnorm_rows_kernel<float><<<blocks, threads, 0, st>>>((const float*)x, ldx, (const float*)w,
+    CC2_CUDA(launch_k(rmsnorm_rows_kernel<float>, blocks, threads, 0, st, (const float*)x, ldx, (const float*)w,
                                                             (float*)y, ldy, rows, dim, per, stride,
-                                                            offset, eps);
+                                                            offset, eps));
   else
     CC2_REQUIRE(false, "rmsnorm_rows: unsupported dtype %d", dtype);
   CC2_CHECK_LAUNCH();

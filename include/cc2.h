@@ -236,6 +236,13 @@ CC2_API int cc2_set_attention_variant(int variant);
  * done (one slot unused).  NULL turns it off. */
 CC2_API int cc2_set_attention_trace(void* device_buffer);
 
+/* Programmatic dependent launch of the forward's kernels (default 1): each
+ * kernel may start - barrier set-up, TMEM allocation, descriptor prefetch -
+ * while the previous one finishes, and waits for it before touching
+ * activations.  0 launches them strictly one after another.  Process-wide;
+ * returns the previous value. */
+CC2_API int cc2_set_launch_overlap(int enabled);
+
 /* Event trace of the 2-SM GEMM: with a device buffer of 32 x 8 uint64
  * (zeroed by the caller), CTA 0 of every later launch writes, for its first
  * 32 tiles: %globaltimer stamps (ns) of accumulator free, first stage loaded,
