@@ -1,6 +1,6 @@
 """Benchmark: Chronos-2-base encoder forward (bf16, fp32 accumulate) on B200.
 
-Workload: per GPU 256 independent univariate
+Workload (the benchmark's configs[1]): per GPU 256 independent univariate
 series, context 2048 (128 patches), prediction_length 64 (4 future patches),
 synthetic seeded data (random walk + daily/weekly sinusoids + noise, 2% NaN),
 random-init weights (seed 0, N(0, 0.02), RMS weights 1).  One step = one
@@ -115,8 +115,8 @@ class ClockSampler:
 
 def gemm_traffic_per_launch():
     """DRAM bytes per GEMM launch from the committed ncu summary of the same
-    workload (profiles/gemm_dram_cfg1.md); None when it is absent."""
-    p = Path(__file__).resolve().parent / "profiles" / "gemm_dram_cfg1.md"
+    workload (profiles/gemm_dram_cfg1.txt); None when it is absent."""
+    p = Path(__file__).resolve().parent / "profiles" / "gemm_dram_cfg1.txt"
     try:
         for line in p.read_text().splitlines():
             if line.startswith("traffic_bytes_per_launch:"):
@@ -224,7 +224,7 @@ def forecasts_per_s(model, ctx, N, gid, flush, steps=5, warmup=2):
 
 
 def other_configs(model_bf16, dev, flush):
-    """The other BASELINE.json configs on one GPU (their own workloads; not the
+    """The benchmark's other configs on one GPU (their own workloads; not the
     headline line): configs[0] fp32 batch-1 latency (CUDA graph) and
     forecasts/s for configs[2], [3], [4]."""
     from cutechronos_b200.model import CuteChronos2Config, CuteChronos2Model
@@ -440,7 +440,7 @@ def run_b200(args):
             "achieved": achieved_tf, "peak": tf_sus, "unit": "TFLOP/s", "frac": achieved_tf / tf_sus,
             "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long step)",
             "traffic": gemm_traffic_per_launch(),
-            "traffic_source": "profiles/gemm_dram_cfg1.md (ncu dram__bytes_read+write, per GEMM launch of one forward)",
+            "traffic_source": "profiles/gemm_dram_cfg1.txt (ncu dram__bytes_read+write, per GEMM launch of one forward)",
             "launches_per_step": gemm["launches"] / args.steps,
             "avg_launch_us": 1e3 * gemm["ms"] / max(1, gemm["launches"]),
         }

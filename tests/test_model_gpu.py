@@ -1,7 +1,7 @@
 """Whole-forward parity on the GPU: CuteChronos2Model (native engine) against
 fixtures from the reference module and against the CPU oracle.
 
-Tolerances: fp32 mode max-abs 1e-4 in the model's
+Tolerances (the parity bar of this path): fp32 mode max-abs 1e-4 in the model's
 normalised output space (|y - ref| / scale_b, scale_b = the series' instance
 norm scale; for the reference's own test inputs the scale is ~0.1 and the
 bound holds in absolute terms as well); bf16 mode 2e-2 relative:
@@ -193,3 +193,16 @@ def test_cuda_graph_replay_equals_eager(small_bf16):
                                                         group_ids=gid).cpu())
     finally:
         small_bf16.enable_cuda_graphs(False)
+
+
+
+def test_batch1_equals_batched(base_bf16, base_weights):
+    """A single series (batch-1 serving, 133 token rows) gives the same
+    forecast, bit for bit, as inside a batch, and stays within the bf16 bar of
+    the oracle."""
+    w = config1(B=8, L=2048)
+    one = base_bf16(w.context[3:4].to(DEV), num_output_patches=4).cpu()
+    batch = base_bf16(w.context.to(DEV), num_output_patches=4).cpu()[3:4]
+    assert torch.equal(one, batch)
+    ref = orc.forward(orc.OracleConfig(), base_weights, w.context[3:4], None, 4)
+    assert _rel_err(one, ref) <= 2e-2
