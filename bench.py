@@ -551,6 +551,10 @@ def run_micro(args):
                                   4 * B4 * 12 * 37 * 37 * 64),
         "attn time S=37 B=4096 (tcgen05)": (
             variant(2, lambda: kk.attention_rows(qkv4, tok4, B4, 37, 12, False, att4)), 4 * B4 * 12 * 37 * 37 * 64),
+        "attn time S=521 B=32": (lambda: kk.attention_rows(qkvr, tok, 32, 521, 12, False, att),
+                                 4 * 32 * 12 * 521 * 521 * 64),
+        "attn time S=521 B=32 (mma.sync)": (
+            variant(1, lambda: kk.attention_rows(qkvr, tok, 32, 521, 12, False, att)), 4 * 32 * 12 * 521 * 521 * 64),
         "cublas qkv  N=2304 K=768": (lambda: torch.matmul(x, wqkv.T), 2 * M * 3 * d * d),
         "cublas o    N=768  K=768": (lambda: torch.matmul(x, wo.T), 2 * M * d * d),
         "cublas ffn1 N=3072 K=768": (lambda: torch.matmul(x, wi.T), 2 * M * dff * d),

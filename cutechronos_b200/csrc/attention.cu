@@ -40,12 +40,16 @@ namespace cc2 {
 
 int encode_bf16_map(CUtensorMap* map, const void* ptr, int cols, int rows, int ld, int box_cols, int box_rows);
 bool attn_tc_supported(int S, int ld, int ldo, const void* qkv);
+bool attn_tc_long_supported(int S, int ld, int ldo, const void* qkv, const void* out);
+int launch_attn_tc_long(const void* qkv, int ld, int qcol, int kcol, int vcol, void* out, int ldo,
+                        const uint8_t* tok, int num_sets, int S, int heads, int* err, cudaStream_t st);
 int launch_attn_tc(const void* qkv, int ld, int qcol, int kcol, int vcol, void* out, int ldo, const uint8_t* tok,
                    int num_sets, int S, int heads, int* err, cudaStream_t st);
 
 // 0 (default): tcgen05 time attention for sets of 112..144 tokens, where it
-// is faster than the mma.sync kernels; 1: the mma.sync kernels only; 2:
-// tcgen05 for every set it supports (17..144 tokens).  Set through
+// is faster than the mma.sync kernels, and the long-set tcgen05 kernel for
+// 145..640 tokens; 1: the mma.sync kernels only; 2: tcgen05 for every set it
+// supports (17..640 tokens).  Set through
 // cc2_set_attention_variant.
 int g_attn_variant = 0;
 
@@ -1010,6 +1014,11 @@ int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int
       int* err = nullptr;
       CC2_CUDA(cudaGetSymbolAddress((void**)&err, g_attn_error));
       return launch_attn_tc(qkv, ld, qcol, kcol, vcol, out, ldo, tok, num_sets, S, heads, err, st);
+    } else if (mode == 0 && !cs && (g_attn_variant == 0 || g_attn_variant == 2) &&
+               attn_tc_long_supported(S, ld, ldo, qkv, out)) {
+      int* err = nullptr;
+      CC2_CUDA(cudaGetSymbolAddress((void**)&err, g_attn_error));
+      return launch_attn_tc_long(qkv, ld, qcol, kcol, vcol, out, ldo, tok, num_sets, S, heads, err, st);
     } else if (mode == 0 && !cs && pbufs >= 1 && aligned && (S + 15) / 16 >= 8) {
       CUtensorMap map;
       CC2_TRY(encode_bf16_map(&map, qkv, ld, num_sets * S, ld, 64, npad_t / nbox));

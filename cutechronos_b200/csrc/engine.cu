@@ -73,6 +73,7 @@ int launch_gemm_tc(const void*, int, const void*, int, void*, int, int, int, int
 extern int g_gemm_variant;
 extern int g_attn_variant;
 int set_attn_trace(void* buf);
+int set_attn_long_trace(void* buf);
 int set_gemm_trace(void* buf);
 int launch_kv_quant(int dtype, void* qkv, int ld, int rows, int q_col, int k_col, int v_col, int heads,
                     const cc2_kvq* key, const cc2_kvq* value, const float* rope_cs, int rope_period, float* stats,
@@ -818,7 +819,8 @@ int cc2_set_gemm_trace(void* device_buffer) {
 
 int cc2_set_attention_trace(void* device_buffer) {
   clear_error();
-  return set_attn_trace(device_buffer);
+  CC2_TRY(set_attn_trace(device_buffer));
+  return set_attn_long_trace(device_buffer);
 }
 
 int cc2_gemm(int dtype, const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,

@@ -228,12 +228,16 @@ CC2_API int cc2_set_gemm_variant(int variant);
  * for every set of 17..144 tokens.  Process-wide; returns the previous value. */
 CC2_API int cc2_set_attention_variant(int variant);
 
-/* Event trace of the tcgen05 time-attention kernel: with a device buffer of
- * 16 x 12 uint64 (zeroed by the caller), CTA 0 of every later launch writes
- * %globaltimer stamps (ns) of its first 16 query tiles, 12 per tile: load
- * issued, MMA saw the load, S MMAs issued, MMA saw P, O MMAs issued, softmax
- * saw S, P written, softmax saw O, O stored, scores in registers, row max
- * done (one slot unused).  NULL turns it off. */
+/* Event trace of the tcgen05 time-attention kernels: with a device buffer of
+ * 16 x 44 uint64 (zeroed by the caller), CTA 0 of every later launch writes
+ * %globaltimer stamps (ns) of its first 16 query tiles.  Sets of up to 144
+ * tokens, 12 per tile: load issued, MMA saw the load, S MMAs issued, MMA saw
+ * P, O MMAs issued, softmax saw S, P written, softmax saw O, O stored, scores
+ * in registers, row max done (one slot unused).  Longer sets, 44 per tile: per
+ * key block j at 8j + {0 softmax saw S, 1 block max exchanged, 2 P in
+ * registers, 3 softmax saw P free, 4 P written, 5 S MMAs issued, 6 MMA saw P,
+ * 7 O MMAs issued}, then 40 Q load issued, 41 softmax saw O, 42 O stored.
+ * NULL turns it off. */
 CC2_API int cc2_set_attention_trace(void* device_buffer);
 
 /* Programmatic dependent launch of the forward's kernels (default 1): each

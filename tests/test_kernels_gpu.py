@@ -261,12 +261,14 @@ def attn_variant():
     lib.cc2_set_attention_variant(old)
 
 
-# tcgen05 kernel (variant 2: wherever it runs, 17..144 tokens), the default
+# tcgen05 kernels (variant 2: wherever they run, 17..640 tokens), the default
 # choice (0) and the mma.sync kernels (1) on bf16 sets: one or two query
 # tiles, 64/128/144-key widths, one or two buffer stages, many items per CTA,
-# a series whose keys are all masked
+# a series whose keys are all masked; long sets of 2..5 key blocks with a
+# ragged last block (145, 200, 257, 521) or full blocks (256, 640)
 @pytest.mark.parametrize("B,S", [(1, 17), (3, 37), (2, 64), (5, 128), (4, 129), (7, 133), (2, 144), (3, 160),
-                                 (2, 160), (2, 192), (300, 133), (700, 37)])
+                                 (2, 160), (2, 192), (300, 133), (700, 37), (3, 145), (4, 200), (2, 256),
+                                 (3, 257), (5, 521), (3, 640), (30, 521)])
 @pytest.mark.parametrize("variant", [0, 1, 2])
 def test_time_attention_bf16_variants(attn_variant, B, S, variant):
     attn_variant(variant)
@@ -281,6 +283,26 @@ def test_time_attention_bf16_variants(attn_variant, B, S, variant):
     ref = orc.unscaled_attention(q.float(), k.float(), v.float(), mask)
     if B > 2:
         ref[1] = v[1].float().mean(dim=1, keepdim=True).expand(H, S, 64)
+    out = K().unscaled_attention(q.to(DEV), k.to(DEV), v.to(DEV), valid.to(DEV)).cpu().float()
+    assert torch.isfinite(out).all()
+    assert (out - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+
+
+# long sets with large, rising scores: the running max of a row grows by more
+# than 2^8 from one key block to the next, so O is rescaled in TMEM
+@pytest.mark.parametrize("S", [300, 521])
+@pytest.mark.parametrize("variant", [0, 2])
+def test_time_attention_long_rescale(attn_variant, S, variant):
+    attn_variant(variant)
+    g = torch.Generator().manual_seed(S)
+    B, H = 3, 12
+    q, k, v = (torch.randn(B, H, S, 64, generator=g) for _ in range(3))
+    k = k + torch.linspace(0, 3, S)[None, None, :, None] * q.mean(dim=2, keepdim=True).sign()
+    q, k, v = (t.to(torch.bfloat16) for t in (q * 2, k * 2, v))
+    valid = torch.rand(B, S, generator=g) > 0.1
+    valid[:, -1] = True
+    mask = (1.0 - valid.float())[:, None, None, :] * torch.finfo(torch.float32).min
+    ref = orc.unscaled_attention(q.float(), k.float(), v.float(), mask)
     out = K().unscaled_attention(q.to(DEV), k.to(DEV), v.to(DEV), valid.to(DEV)).cpu().float()
     assert torch.isfinite(out).all()
     assert (out - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
