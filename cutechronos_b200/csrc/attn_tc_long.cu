@@ -6,22 +6,28 @@
 //
 // One persistent CTA per SM walks (series, head) items.  Per item the whole
 // K and V (up to 640 rows each, 128-byte swizzled TMA boxes of 128 rows)
-// stay in shared memory; the queries run as tiles of 128 rows.  Per query
-// tile the keys are visited once, in blocks of 128, with an online softmax:
-//   S_j = Q K_j^T -> block row max -> P_j = exp2(S_j - m) (bf16, swizzled
-//   K-major in shared memory) -> O += P_j V_j (V read MN-major from its box)
+// stay in shared memory; the queries run as tiles of 128 rows, two at a time:
+// even tiles belong to pipeline 0, odd tiles to pipeline 1.  Each pipeline
+// has its own Q buffer, its own MMA-issuing warp, four softmax warps (one
+// thread per query row) and TMEM columns for S (128), P (64) and O (64).
+// Per query tile the keys are visited once, in blocks of 128, with an
+// online softmax:
+//   S_j = Q K_j^T -> row max -> P_j = exp2(S_j - m) (bf16, written to TMEM)
+//   -> O += P_j V_j (P the TMEM operand, V read MN-major from its box)
 // The running max m is only moved when a block's max exceeds it by more than
 // 2^8 (then O and the row sum are rescaled in TMEM first); otherwise the
 // exponents are taken against the stale max, which keeps P <= 256 and costs
 // nothing in precision (the same lazy-rescale rule as FlashAttention-4).
-//   warp 0      TMA producer (K, V and the key bias per item; Q per tile)
-//   warp 1      TMEM owner and MMA issuer (one thread); TMEM: S in two
-//               ping-pong buffers of 128 columns, O in 64 columns
-//   warps 2-9   softmax and epilogue: TMEM lane quarter q = warp % 4 (query
-//               rows 32q..), warps 2-5 the first 64 keys of each block and
-//               O columns 0-31, warps 6-9 the other half; the two warps of a
-//               quarter exchange block maxima through shared memory
-// The S MMA of block j + 1 runs while the softmax warps process block j.
+// S_{j+1} is computed while the softmax threads turn S_j into P_j, and the
+// two pipelines drift out of phase, so one pipeline's exponentials overlap
+// the other's loads, maxima and TMEM stores.
+//   warp 0        TMA producer (K, V and the key bias per item; Q per tile)
+//   warp 1        TMEM owner and MMA issuer of both pipelines (one thread
+//                 polling the two pipelines' barriers)
+//   warps 2-3     idle (they complete the first warpgroup, which hands its
+//                 registers to the softmax warpgroups)
+//   warps 4-7     softmax and epilogue of pipeline 0 (TMEM lane quarter
+//                 warp % 4), warps 8-11 of pipeline 1
 // Every wait is bounded (about 2 s): on expiry the CTA sets the attention
 // error word, all roles leave their loops, copies and MMAs in flight are
 // waited for, TMEM is freed and the kernel returns.
@@ -38,32 +44,37 @@ namespace {
 
 using namespace tcx;
 
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;
+// Registers per thread after the split: the producer / MMA warpgroup gives
+// registers to the two softmax warpgroups.  128 x 80 + 256 x 208 = 63488 is
+// within the 384 x 168 = 64512 the block is launched with.
+constexpr int kRegsControl = 80, kRegsSoftmax = 208;
 constexpr int kQT = 128, kKB = 128;
 constexpr int kMaxKeys = 640;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kOCol = 256;
-constexpr uint32_t kBlockBytes = 128 * 128;  // 128 rows x 128 bytes
+constexpr uint32_t kSCol = 0, kPCol = 256, kOCol = 384;  // + 128 G, + 64 G, + 64 G for pipeline G
+constexpr uint32_t kBlockBytes = 128 * 128;            // 128 rows x 128 bytes
 constexpr float kMaskedScore = -1e30f;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;  // move the running max only past 2^8
 
 // Optional event trace (cc2_set_attention_trace): CTA 0 records %globaltimer
-// stamps of its first kTraceUnits query tiles.  Per key block j (events
-// 8j + e): 0 softmax saw S_j, 1 block max exchanged, 2 P_j in registers,
-// 3 softmax saw P free, 4 P_j written; 5 S_j MMAs issued, 6 MMA saw P_j,
-// 7 O MMAs issued.  Per tile: 40 Q load issued, 41 softmax saw O, 42 O stored.
+// stamps of the first 8 query tiles of each pipeline (unit 8 G + tile).  Per
+// key block j (events 8j + e): 0 softmax saw S_j, 1 row max done, 2 P_j in
+// registers, 3 softmax saw P free, 4 P_j written; 5 S_j MMAs issued, 6 MMA
+// saw P_j, 7 O MMAs issued.  Per tile: 40 Q load issued, 41 softmax saw O,
+// 42 O stored.
 constexpr int kTraceUnits = 16, kTraceEvents = 44;
 __device__ unsigned long long* g_attn_long_trace = nullptr;
 
-__device__ __forceinline__ void trace(unsigned long long* tr, uint32_t unit, int ev) {
-  if (tr != nullptr && unit < (uint32_t)kTraceUnits) tr[unit * kTraceEvents + ev] = globaltimer_ns();
+__device__ __forceinline__ void trace(unsigned long long* tr, uint32_t G, uint32_t n, int ev) {
+  if (tr != nullptr && n < 8u) tr[(8u * G + n) * kTraceEvents + ev] = globaltimer_ns();
 }
 
 struct LArgs {
   int S, heads, items, nkb, nqt;
   int qcol, kcol, vcol, ldo;
-  uint32_t k_off, v_off, p_off, kv_bytes;
+  uint32_t k_off, v_off, kv_bytes;
 };
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -72,30 +83,30 @@ attn_tc_long_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
   pdl_launch_dependents();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  __shared__ __align__(8) uint64_t q_full, q_empty, kv_full, kv_empty, s_full[2], s_free[2], p_full, p_free, o_full,
-      mma_done;
+  __shared__ __align__(8) uint64_t q_full[2], q_empty[2], kv_full, kv_empty, s_full[2], s_free[2], p_full[2],
+      p_free[2], o_full[2], mma_done[2];
   __shared__ __align__(16) float kbias[kMaxKeys];
-  __shared__ float red_max[2][2][128], red_sum[2][128];
+  __shared__ uint32_t blk_masked;  // bit j: key block j of the item holds a masked or padding key
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int my_items = a.items > (int)blockIdx.x ? (a.items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
-  const uint32_t sbase = smem_u32(smem);  // Q tile at offset 0
+  const uint32_t sbase = smem_u32(smem);  // Q buffers of the two pipelines at 0 and kBlockBytes
 
   if (tid == 0) {
-    mbar_init(smem_u32(&q_full), 1);
-    mbar_init(smem_u32(&q_empty), 1);
-    mbar_init(smem_u32(&kv_full), 32);
-    mbar_init(smem_u32(&kv_empty), 1);
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(smem_u32(&s_full[b]), 1);
-      mbar_init(smem_u32(&s_free[b]), 8);
+    for (int G = 0; G < 2; ++G) {
+      mbar_init(smem_u32(&q_full[G]), 1);
+      mbar_init(smem_u32(&q_empty[G]), 1);
+      mbar_init(smem_u32(&s_full[G]), 1);
+      mbar_init(smem_u32(&s_free[G]), 4);
+      mbar_init(smem_u32(&p_full[G]), 4);
+      mbar_init(smem_u32(&p_free[G]), 1);
+      mbar_init(smem_u32(&o_full[G]), 1);
+      mbar_init(smem_u32(&mma_done[G]), 1);
     }
-    mbar_init(smem_u32(&p_full), 8);
-    mbar_init(smem_u32(&p_free), 1);
-    mbar_init(smem_u32(&o_full), 1);
-    mbar_init(smem_u32(&mma_done), 1);
+    mbar_init(smem_u32(&kv_full), 32);
+    mbar_init(smem_u32(&kv_empty), 2);
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -114,14 +125,15 @@ attn_tc_long_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
-    int kv_issued = -1, q_issued = -1;  // phases of the last loads (for the exit wait)
-    int t = 0;                          // query tiles issued so far
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+    int kv_issued = -1;
+    uint32_t nq[2] = {0, 0};  // Q tiles loaded per pipeline
     for (int li = 0; li < my_items && !abort_flag; ++li) {
       const int item = (int)blockIdx.x + li * (int)gridDim.x;
       const int b = item / a.heads, h = item % a.heads;
       const int row0 = b * a.S;
-      // K, V and the key bias of the item once the previous item's MMAs are done
-      if (li > 0 && !mbar_wait(smem_u32(&kv_empty), (uint32_t)(li - 1) & 1u, &abort_flag, err)) break;
+      // K, V and the key bias of the item once both pipelines finished the previous item
+      if (li > 0 && !mbar_wait_inl(smem_u32(&kv_empty), (uint32_t)(li - 1) & 1u, &abort_flag, err)) break;
       const uint32_t bkv = smem_u32(&kv_full);
       if (lane == 0) {
         mbar_expect_tx(bkv, a.kv_bytes);
@@ -130,23 +142,29 @@ attn_tc_long_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           tma_load(sbase + a.v_off + (uint32_t)j * kBlockBytes, &tmKV, bkv, a.vcol + h * 64, row0 + j * kKB);
         }
       }
-      for (int k = lane; k < a.nkb * kKB; k += 32)
-        kbias[k] = k < a.S ? (tok[(size_t)b * a.S + k] ? 0.0f : kMaskedScore) : -INFINITY;
+      uint32_t masked = 0;
+      for (int k = lane; k < a.nkb * kKB; k += 32) {
+        const float kb = k < a.S ? (tok[(size_t)b * a.S + k] ? 0.0f : kMaskedScore) : -INFINITY;
+        kbias[k] = kb;
+        if (__any_sync(0xffffffffu, kb != 0.0f)) masked |= 1u << (k / kKB);
+      }
+      if (lane == 0) blk_masked = masked;
       mbar_arrive(bkv);
       kv_issued = li;
       bool ok = true;
-      for (int qt = 0; qt < a.nqt; ++qt, ++t) {
-        if (t > 0 && !mbar_wait(smem_u32(&q_empty), (uint32_t)(t - 1) & 1u, &abort_flag, err)) {
+      for (int qt = 0; qt < a.nqt; ++qt) {
+        const int G = qt & 1;
+        if (nq[G] > 0 && !mbar_wait_inl(smem_u32(&q_empty[G]), (nq[G] - 1) & 1u, &abort_flag, err)) {
           ok = false;
           break;
         }
         if (lane == 0) {
-          const uint32_t bq = smem_u32(&q_full);
+          const uint32_t bq = smem_u32(&q_full[G]);
           mbar_arrive_expect_tx(bq, kBlockBytes);
-          tma_load(sbase, &tmQ, bq, a.qcol + h * 64, row0 + qt * kQT);
-          trace(tr, (uint32_t)t, 40);
+          tma_load(sbase + (uint32_t)G * kBlockBytes, &tmQ, bq, a.qcol + h * 64, row0 + qt * kQT);
+          trace(tr, (uint32_t)G, nq[G], 40);
         }
-        q_issued = t;
+        ++nq[G];
       }
       if (!ok) break;
     }
@@ -156,128 +174,211 @@ attn_tc_long_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
       if (kv_issued >= 0)
         while (!mbar_try(smem_u32(&kv_full), (uint32_t)kv_issued & 1u) && globaltimer_ns() - t0 < kWaitLimitNs) {
         }
-      if (q_issued >= 0)
-        while (!mbar_try(smem_u32(&q_full), (uint32_t)q_issued & 1u) && globaltimer_ns() - t0 < kWaitLimitNs) {
-        }
+      for (int G = 0; G < 2; ++G)
+        if (nq[G] > 0)
+          while (!mbar_try(smem_u32(&q_full[G]), (nq[G] - 1) & 1u) && globaltimer_ns() - t0 < kWaitLimitNs) {
+          }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ---------------- MMA issuer ----------------
+    // ---------------- MMA issuer of both pipelines ----------------
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
+    // Each pipeline is a small state machine; the thread polls both (never
+    // blocking on one) and advances whichever is ready.  Per query tile:
+    // S_0, S_1, PV_0, S_2, PV_1, ..., S_{n-1}, PV_{n-2}, PV_{n-1}.
     if (lane == 0) {
+      enum { kKV, kQ, kS, kPV, kDone };
       const uint32_t id_s = idesc(128, kKB, false), id_o = idesc(128, 64, true);
-      const uint64_t dq = sw128_desc(sbase), dk0 = sw128_desc(sbase + a.k_off), dv0 = sw128_desc(sbase + a.v_off);
-      const uint64_t dp = sw128_desc(sbase + a.p_off);
-      uint32_t g = 0, c = 0, t = 0;  // S blocks, P blocks, query tiles so far
-      bool ok = true, any = false;
-      // S_j = Q K_j^T into buffer g & 1 (after the softmax released it)
-      auto issue_s = [&](int j) -> bool {
-        const uint32_t b = g & 1u;
-        if (g >= 2 && !mbar_wait(smem_u32(&s_free[b]), ((g >> 1) - 1) & 1u, &abort_flag, err)) return false;
-        tc_fence_after();
-        const uint64_t dk = dk0 + (uint64_t)(j * (kBlockBytes >> 4));
+      const uint64_t dk0 = sw128_desc(sbase + a.k_off), dv0 = sw128_desc(sbase + a.v_off);
+      int st[2] = {my_items > 0 ? kKV : kDone, my_items > 0 ? kKV : kDone};
+      int li[2] = {0, 0}, qt[2] = {0, 1}, jb[2] = {0, 0};
+      uint32_t ns[2] = {0, 0}, np[2] = {0, 0}, nt[2] = {0, 0};
+      bool any = false;
+      unsigned long long last = globaltimer_ns();
+      uint32_t spins = 0;
+      while (st[0] != kDone || st[1] != kDone) {
+        bool progress = false;
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) mma_bf16(tmem + b * 128u, dq + 2u * ks, dk + 2u * ks, id_s, ks > 0);
-        mma_commit(smem_u32(&s_full[b]));
-        trace(tr, t, 8 * j + 5);
-        ++g;
-        any = true;
-        return true;
-      };
-      for (int li = 0; li < my_items && ok; ++li) {
-        if (!mbar_wait(smem_u32(&kv_full), (uint32_t)li & 1u, &abort_flag, err)) break;
-        for (int qt = 0; qt < a.nqt && ok; ++qt, ++t) {
-          if (!mbar_wait(smem_u32(&q_full), t & 1u, &abort_flag, err)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          ok = issue_s(0);
-          for (int j = 0; j < a.nkb && ok; ++j) {
-            if (j + 1 < a.nkb) ok = issue_s(j + 1);
-            if (!ok) break;
-            if (j == a.nkb - 1) mma_commit(smem_u32(&q_empty));  // the tile's last S MMA is issued
-            if (!mbar_wait(smem_u32(&p_full), c & 1u, &abort_flag, err)) {
-              ok = false;
+        for (uint32_t G = 0; G < 2; ++G) {
+          const uint32_t t_s = tmem + kSCol + 128u * G, t_p = tmem + kPCol + 64u * G, t_o = tmem + kOCol + 64u * G;
+          switch (st[G]) {
+            case kKV:
+              if (!mbar_test(smem_u32(&kv_full), (uint32_t)li[G] & 1u)) break;
+              progress = true;
+              qt[G] = (int)G;
+              if (qt[G] < a.nqt) {
+                st[G] = kQ;
+              } else {
+                mma_commit(smem_u32(&kv_empty));
+                st[G] = ++li[G] < my_items ? kKV : kDone;
+              }
+              break;
+            case kQ:
+              if (!mbar_test(smem_u32(&q_full[G]), nt[G] & 1u)) break;
+              progress = true;
+              tc_fence_after();
+              st[G] = kS;
+              jb[G] = 0;
+              break;
+            case kS: {
+              if (ns[G] > 0 && !mbar_test(smem_u32(&s_free[G]), (ns[G] - 1) & 1u)) break;
+              progress = true;
+              tc_fence_after();
+              const int j = jb[G];
+              const uint64_t dq = sw128_desc(sbase + G * kBlockBytes);
+              const uint64_t dk = dk0 + (uint64_t)(j * (kBlockBytes >> 4));
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks) mma_bf16(t_s, dq + 2u * ks, dk + 2u * ks, id_s, ks > 0);
+              mma_commit(smem_u32(&s_full[G]));
+              trace(tr, G, nt[G], 8 * j + 5);
+              ++ns[G];
+              any = true;
+              if (j == a.nkb - 1) mma_commit(smem_u32(&q_empty[G]));  // the tile's last S MMA is issued
+              if (j == 0 && a.nkb > 1) {
+                jb[G] = 1;  // S_1 before PV_0
+              } else {
+                st[G] = kPV;
+                jb[G] = j == 0 ? 0 : j - 1;
+              }
               break;
             }
-            trace(tr, t, 8 * j + 6);
-            tc_fence_after();
-            const uint64_t dv = dv0 + (uint64_t)(j * (kBlockBytes >> 4));
-            for (int ks = 0; ks < kKB / 16; ++ks)
-              mma_bf16(tmem + kOCol, dp + (uint64_t)((ks >> 2) * (kBlockBytes >> 4) + 2 * (ks & 3)), dv + 128u * ks,
-                       id_o, (j > 0 || ks > 0) ? 1u : 0u);
-            mma_commit(smem_u32(&p_free));
-            trace(tr, t, 8 * j + 7);
-            ++c;
+            case kPV: {
+              if (!mbar_test(smem_u32(&p_full[G]), np[G] & 1u)) break;
+              progress = true;
+              const int j = jb[G];
+              trace(tr, G, nt[G], 8 * j + 6);
+              tc_fence_after();
+              const uint64_t dv = dv0 + (uint64_t)(j * (kBlockBytes >> 4));
+#pragma unroll
+              for (int ks = 0; ks < kKB / 16; ++ks)
+                mma_bf16_ts(t_o, t_p + 8u * ks, dv + 128u * ks, id_o, (j > 0 || ks > 0) ? 1u : 0u);
+              mma_commit(smem_u32(&p_free[G]));
+              trace(tr, G, nt[G], 8 * j + 7);
+              ++np[G];
+              if (j + 2 < a.nkb) {
+                st[G] = kS;
+                jb[G] = j + 2;
+              } else if (j + 1 < a.nkb) {
+                jb[G] = j + 1;  // the last PV follows the last S directly
+              } else {
+                mma_commit(smem_u32(&o_full[G]));
+                ++nt[G];
+                qt[G] += 2;
+                if (qt[G] < a.nqt) {
+                  st[G] = kQ;
+                } else {
+                  mma_commit(smem_u32(&kv_empty));
+                  st[G] = ++li[G] < my_items ? kKV : kDone;
+                }
+              }
+              break;
+            }
+            default:
+              break;
           }
-          if (ok) mma_commit(smem_u32(&o_full));
         }
-        if (ok) mma_commit(smem_u32(&kv_empty));
+        if (progress) {
+          spins = 0;
+          continue;
+        }
+        __nanosleep(32);  // leave the issue slots to the softmax warps of this SM quarter
+        if ((++spins & 63u) == 0) {
+          if (abort_flag) break;
+          const unsigned long long now = globaltimer_ns();
+          if (spins == 64) last = now;  // first idle check of this wait
+          if (now - last > kWaitLimitNs) {
+            abort_flag = 1;
+            atomicOr(err, 1);
+            break;
+          }
+        }
       }
       // every MMA issued above has completed before TMEM is released
       if (any) {
-        mma_commit(smem_u32(&mma_done));
+        mma_commit(smem_u32(&mma_done[0]));
         const unsigned long long t0 = globaltimer_ns();
-        while (!mbar_try(smem_u32(&mma_done), 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+        while (!mbar_try(smem_u32(&mma_done[0]), 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
         }
       }
     }
     __syncwarp();
+  } else if (warp < 4) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
   } else {
-    // ---------------- softmax + epilogue (warps 2-9) ----------------
-    const int q = warp & 3, hf = (warp - 2) >> 2;
+    // ---------------- softmax + epilogue of pipeline G (warps 4-7: 0, 8-11: 1) ----------------
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
+    const uint32_t G = warp >= 8 ? 1u : 0u;
+    const int q = warp & 3;
     const int r = 32 * q + lane;
     const uint32_t t_lane = tmem + ((uint32_t)(32 * q) << 16);
-    const uint32_t prow = sbase + a.p_off + (uint32_t)hf * kBlockBytes + (uint32_t)r * 128u;
-    const uint32_t sw = (uint32_t)(r & 7);
-    const uint32_t pair_bar = 1u + (uint32_t)q;  // named barrier of the two warps on these lanes
-    uint32_t g = 0, c = 0, t = 0;
+    const uint32_t t_s = t_lane + kSCol + 128u * G, t_p = t_lane + kPCol + 64u * G, t_o = t_lane + kOCol + 64u * G;
+    const bool tw = (warp == 4 || warp == 8) && lane == 0;
+    uint32_t ns = 0, np = 0, nt = 0;
     bool ok = true;
     for (int li = 0; li < my_items && ok; ++li) {
-      if (!mbar_wait(smem_u32(&kv_full), (uint32_t)li & 1u, &abort_flag, err)) break;  // key bias
+      if (!mbar_wait_inl(smem_u32(&kv_full), (uint32_t)li & 1u, &abort_flag, err)) break;  // key bias
       const int item = (int)blockIdx.x + li * (int)gridDim.x;
       const int b = item / a.heads, h = item % a.heads;
-      for (int qt = 0; qt < a.nqt && ok; ++qt, ++t) {
+      const uint32_t masked = blk_masked;
+      for (int qt = (int)G; qt < a.nqt && ok; qt += 2, ++nt) {
         const int row = qt * kQT + r;
         const bool valid = row < a.S;
         const bool warp_rows = qt * kQT + 32 * q < a.S;  // warp-uniform
         float m = -INFINITY, l = 0.0f;
-        const bool tw = warp == 2 && lane == 0;
         for (int j = 0; j < a.nkb; ++j) {
-          const uint32_t sb = g & 1u;
-          if (!mbar_wait(smem_u32(&s_full[sb]), (g >> 1) & 1u, &abort_flag, err)) {
+          if (!mbar_wait_inl(smem_u32(&s_full[G]), ns & 1u, &abort_flag, err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          if (tw) trace(tr, t, 8 * j);
+          if (tw) trace(tr, G, nt, 8 * j);
+          uint32_t v[128];
+          if (warp_rows) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tmem_ld32(t_s + 32u * c, v + 32 * c);
+            tmem_ld_wait();
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&s_free[G]));  // S_j is in registers
+          ++ns;
           float scale = 1.0f;
           bool rescale = false;
-          uint32_t pk[32];
           if (warp_rows) {
-            uint32_t v[64];
-            tmem_ld32(t_lane + sb * 128u + 64u * hf, v);
-            tmem_ld32(t_lane + sb * 128u + 64u * hf + 32u, v + 32);
-            tmem_ld_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&s_free[sb]));  // S_j is in registers
-            const float* kb = kbias + j * kKB + 64 * hf;
-            float bm = -INFINITY;
+            // x = S log2(e) + key bias; blocks without masked keys skip the bias and
+            // fold the scale into the exponent's FMA
+            const bool clean = !((masked >> j) & 1u);
+            float bm;
+            if (clean) {
+              float bm0 = -INFINITY, bm1 = -INFINITY;
 #pragma unroll
-            for (int i = 0; i < 64; i += 4) {
-              const float4 b4 = *reinterpret_cast<const float4*>(kb + i);
-              v[i] = __float_as_uint(fmaf(__uint_as_float(v[i]), kLog2e, b4.x));
-              v[i + 1] = __float_as_uint(fmaf(__uint_as_float(v[i + 1]), kLog2e, b4.y));
-              v[i + 2] = __float_as_uint(fmaf(__uint_as_float(v[i + 2]), kLog2e, b4.z));
-              v[i + 3] = __float_as_uint(fmaf(__uint_as_float(v[i + 3]), kLog2e, b4.w));
-              bm = fmaxf(bm, fmaxf(fmaxf(__uint_as_float(v[i]), __uint_as_float(v[i + 1])),
-                                   fmaxf(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]))));
+              for (int i = 0; i < 128; i += 4) {
+                bm0 = max3(bm0, __uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+                bm1 = max3(bm1, __uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
+              }
+              bm = fmaxf(bm0, bm1) * kLog2e;
+            } else {
+              const float* kb = kbias + j * kKB;
+              float bm0 = -INFINITY, bm1 = -INFINITY;
+#pragma unroll
+              for (int i = 0; i < 128; i += 4) {
+                float4 b4;
+                asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                             : "=f"(b4.x), "=f"(b4.y), "=f"(b4.z), "=f"(b4.w)
+                             : "r"(smem_u32(kb + i)));
+                const float x0 = fmaf(__uint_as_float(v[i]), kLog2e, b4.x);
+                const float x1 = fmaf(__uint_as_float(v[i + 1]), kLog2e, b4.y);
+                const float x2 = fmaf(__uint_as_float(v[i + 2]), kLog2e, b4.z);
+                const float x3 = fmaf(__uint_as_float(v[i + 3]), kLog2e, b4.w);
+                v[i] = __float_as_uint(x0);
+                v[i + 1] = __float_as_uint(x1);
+                v[i + 2] = __float_as_uint(x2);
+                v[i + 3] = __float_as_uint(x3);
+                bm0 = max3(bm0, x0, x1);
+                bm1 = max3(bm1, x2, x3);
+              }
+              bm = fmaxf(bm0, bm1);
             }
-            red_max[j & 1][hf][r] = bm;
-            named_sync(pair_bar, 64);
-            bm = fmaxf(bm, red_max[j & 1][hf ^ 1][r]);
-            if (tw) trace(tr, t, 8 * j + 1);
             if (j == 0) {
               m = bm;
             } else if (bm > m + kRescaleLog2) {
@@ -286,77 +387,86 @@ attn_tc_long_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
               m = bm;
               rescale = true;
             }
-            // P_j while the previous O MMA still runs
-#pragma unroll
-            for (int i = 0; i < 64; i += 2) {
-              const float p0 = ex2(__uint_as_float(v[i]) - m), p1 = ex2(__uint_as_float(v[i + 1]) - m);
-              l += p0 + p1;
-              pk[i >> 1] = pack_bf16(p0, p1);
-            }
-            if (tw) trace(tr, t, 8 * j + 2);
-          } else {
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(&s_free[sb]));
+            if (tw) trace(tr, G, nt, 8 * j + 1);
           }
-          ++g;
           // the previous O MMA has finished reading P and writing O
-          if (c > 0 && !mbar_wait(smem_u32(&p_free), (c - 1) & 1u, &abort_flag, err)) {
+          if (np > 0 && !mbar_wait_inl(smem_u32(&p_free[G]), (np - 1) & 1u, &abort_flag, err)) {
             ok = false;
             break;
           }
-          if (tw) trace(tr, t, 8 * j + 3);
+          tc_fence_after();
+          if (tw) trace(tr, G, nt, 8 * j + 3);
+          if (warp_rows) {
+            // P_j = exp2(x - m), stored to TMEM 32 keys at a time; exponent
+            // fma(x, 1, -m) = x - m exactly on masked blocks
+            const bool clean = !((masked >> j) & 1u);
+            const float sc = clean ? kLog2e : 1.0f, nm = -m;
+            float l0 = 0.0f, l1 = 0.0f;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              uint32_t pk[16];
+#pragma unroll
+              for (int i = 0; i < 32; i += 4) {
+                const float p0 = ex2(fmaf(__uint_as_float(v[32 * c + i]), sc, nm));
+                const float p1 = ex2(fmaf(__uint_as_float(v[32 * c + i + 1]), sc, nm));
+                const float p2 = ex2(fmaf(__uint_as_float(v[32 * c + i + 2]), sc, nm));
+                const float p3 = ex2(fmaf(__uint_as_float(v[32 * c + i + 3]), sc, nm));
+                l0 += p0 + p1;
+                l1 += p2 + p3;
+                pk[i >> 1] = pack_bf16(p0, p1);
+                pk[(i >> 1) + 1] = pack_bf16(p2, p3);
+              }
+              tmem_st16(t_p + 16u * c, pk);
+            }
+            l += l0 + l1;
+            if (tw) trace(tr, G, nt, 8 * j + 2);
+          }
           if (__any_sync(0xffffffffu, rescale)) {
-            tc_fence_after();
-            uint32_t o[32];
-            tmem_ld32(t_lane + kOCol + 32u * hf, o);
-            tmem_ld_wait();
+#pragma unroll 1
+            for (int c = 0; c < 2; ++c) {
+              uint32_t o[32];
+              tmem_ld32(t_o + 32u * c, o);
+              tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * scale);
-            tmem_st32(t_lane + kOCol + 32u * hf, o);
-            tmem_st_wait();
+              for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * scale);
+              tmem_st32(t_o + 32u * c, o);
+            }
           }
-          if (warp_rows && valid) {
-#pragma unroll
-            for (int ch = 0; ch < 8; ++ch)
-              asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(prow + (((uint32_t)ch ^ sw) << 4)),
-                           "r"(pk[4 * ch]), "r"(pk[4 * ch + 1]), "r"(pk[4 * ch + 2]), "r"(pk[4 * ch + 3])
-                           : "memory");
-          }
-          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          tmem_st_wait();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(smem_u32(&p_full));
-          if (tw) trace(tr, t, 8 * j + 4);
-          ++c;
+          if (lane == 0) mbar_arrive(smem_u32(&p_full[G]));
+          if (tw) trace(tr, G, nt, 8 * j + 4);
+          ++np;
         }
         if (!ok) break;
-        if (!mbar_wait(smem_u32(&o_full), t & 1u, &abort_flag, err)) {
+        if (!mbar_wait_inl(smem_u32(&o_full[G]), nt & 1u, &abort_flag, err)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        if (tw) trace(tr, t, 41);
+        if (tw) trace(tr, G, nt, 41);
         if (warp_rows) {
-          red_sum[hf][r] = l;
-          named_sync(pair_bar, 64);
-          const float inv = 1.0f / (l + red_sum[hf ^ 1][r]);
-          uint32_t o[32];
-          tmem_ld32(t_lane + kOCol + 32u * hf, o);
-          tmem_ld_wait();
-          if (valid) {
-            uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)b * a.S + row) * a.ldo + h * 64 + 32 * hf);
+          const float inv = 1.0f / l;
+          uint4* dst = reinterpret_cast<uint4*>(out + ((size_t)b * a.S + row) * a.ldo + h * 64);
 #pragma unroll
-            for (int gq = 0; gq < 4; ++gq) {
-              uint4 w4;
-              w4.x = pack_bf16(__uint_as_float(o[8 * gq + 0]) * inv, __uint_as_float(o[8 * gq + 1]) * inv);
-              w4.y = pack_bf16(__uint_as_float(o[8 * gq + 2]) * inv, __uint_as_float(o[8 * gq + 3]) * inv);
-              w4.z = pack_bf16(__uint_as_float(o[8 * gq + 4]) * inv, __uint_as_float(o[8 * gq + 5]) * inv);
-              w4.w = pack_bf16(__uint_as_float(o[8 * gq + 6]) * inv, __uint_as_float(o[8 * gq + 7]) * inv);
-              dst[gq] = w4;
+          for (int c = 0; c < 2; ++c) {
+            uint32_t o[32];
+            tmem_ld32(t_o + 32u * c, o);
+            tmem_ld_wait();
+            if (valid) {
+#pragma unroll
+              for (int gq = 0; gq < 4; ++gq) {
+                uint4 w4;
+                w4.x = pack_bf16(__uint_as_float(o[8 * gq + 0]) * inv, __uint_as_float(o[8 * gq + 1]) * inv);
+                w4.y = pack_bf16(__uint_as_float(o[8 * gq + 2]) * inv, __uint_as_float(o[8 * gq + 3]) * inv);
+                w4.z = pack_bf16(__uint_as_float(o[8 * gq + 4]) * inv, __uint_as_float(o[8 * gq + 5]) * inv);
+                w4.w = pack_bf16(__uint_as_float(o[8 * gq + 6]) * inv, __uint_as_float(o[8 * gq + 7]) * inv);
+                dst[4 * c + gq] = w4;
+              }
             }
           }
-          named_sync(pair_bar, 64);  // red_sum is rewritten by the next tile
-          if (tw) trace(tr, t, 42);
+          if (tw) trace(tr, G, nt, 42);
         }
         tc_fence_before();
       }
@@ -377,11 +487,10 @@ size_t plan_long(int S, int heads, int num_sets, LArgs& a) {
   a.items = num_sets * heads;
   a.nkb = (S + kKB - 1) / kKB;
   a.nqt = (S + kQT - 1) / kQT;
-  a.k_off = kBlockBytes;  // after the Q tile
+  a.k_off = 2 * kBlockBytes;  // after the two Q buffers
   a.v_off = a.k_off + (uint32_t)a.nkb * kBlockBytes;
-  a.p_off = a.v_off + (uint32_t)a.nkb * kBlockBytes;
   a.kv_bytes = 2u * (uint32_t)a.nkb * kBlockBytes;
-  return 1024 + (size_t)a.p_off + 2 * kBlockBytes;
+  return 1024 + (size_t)a.v_off + (size_t)a.nkb * kBlockBytes;
 }
 
 }  // namespace

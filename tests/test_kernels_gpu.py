@@ -308,6 +308,27 @@ def test_time_attention_long_rescale(attn_variant, S, variant):
     assert (out - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
 
 
+# key blocks without masked keys take a separate path (no bias, scale folded
+# into the exponent): fully valid series, left padding that covers the first
+# one or two blocks (as a shorter series in a batch has), and large scores
+@pytest.mark.parametrize("S", [256, 521, 640])
+@pytest.mark.parametrize("scale", [0.5, 2.0])
+def test_time_attention_long_clean_blocks(attn_variant, S, scale):
+    attn_variant(0)
+    g = torch.Generator().manual_seed(S + int(scale * 10))
+    B, H = 4, 12
+    q, k, v = ((torch.randn(B, H, S, 64, generator=g) * s).to(torch.bfloat16) for s in (scale, scale, 1.0))
+    valid = torch.ones(B, S, dtype=torch.bool)
+    valid[1, :150] = False
+    valid[2, :40] = False
+    valid[3, torch.rand(S, generator=g) < 0.05] = False
+    mask = (1.0 - valid.float())[:, None, None, :] * torch.finfo(torch.float32).min
+    ref = orc.unscaled_attention(q.float(), k.float(), v.float(), mask)
+    out = K().unscaled_attention(q.to(DEV), k.to(DEV), v.to(DEV), valid.to(DEV)).cpu().float()
+    assert torch.isfinite(out).all()
+    assert (out - ref).abs().max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+
+
 def test_attention_uniform_known_answer():
     # identical keys -> uniform weights -> output = mean of V (reference test_attention.py:199-213)
     B, H, S = 2, 12, 70
