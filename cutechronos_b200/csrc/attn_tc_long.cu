@@ -19,12 +19,12 @@
 // exponents are taken against the stale max, which keeps P <= 256 and costs
 // nothing in precision (the same lazy-rescale rule as FlashAttention-4).
 // S_{j+1} is computed while the softmax threads turn S_j into P_j, and the
-// two pipelines drift out of phase, so one pipeline's exponentials overlap
-// the other's loads, maxima and TMEM stores.
+// tensor core alternates between the two pipelines' MMAs.  A share of the
+// exponentials runs as a polynomial on the FMA pipe next to the MUFU unit.
 //   warp 0        TMA producer (K, V and the key bias per item; Q per tile)
-//   warp 1        TMEM owner and MMA issuer of both pipelines (one thread
-//                 polling the two pipelines' barriers)
-//   warps 2-3     idle (they complete the first warpgroup, which hands its
+//   warps 1, 2    MMA issuers of pipelines 0 and 1 (one thread each);
+//                 warp 1 owns the 512 TMEM columns
+//   warp 3        idle (it completes the first warpgroup, which hands its
 //                 registers to the softmax warpgroups)
 //   warps 4-7     softmax and epilogue of pipeline 0 (TMEM lane quarter
 //                 warp % 4), warps 8-11 of pipeline 1
@@ -46,9 +46,9 @@ using namespace tcx;
 
 constexpr int kThreads = 384;
 // Registers per thread after the split: the producer / MMA warpgroup gives
-// registers to the two softmax warpgroups.  128 x 80 + 256 x 208 = 63488 is
-// within the 384 x 168 = 64512 the block is launched with.
-constexpr int kRegsControl = 80, kRegsSoftmax = 208;
+// registers to the two softmax warpgroups.  128 x 72 + 256 x 216 = 64512 is
+// exactly the 384 x 168 = 64512 the block is launched with.
+constexpr int kRegsControl = 72, kRegsSoftmax = 216;
 constexpr int kQT = 128, kKB = 128;
 constexpr int kMaxKeys = 640;
 constexpr uint32_t kTmemCols = 512;
@@ -57,6 +57,9 @@ constexpr uint32_t kBlockBytes = 128 * 128;            // 128 rows x 128 bytes
 constexpr float kMaskedScore = -1e30f;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kRescaleLog2 = 8.0f;  // move the running max only past 2^8
+// Pairs (of each 16) whose exponentials run on the FMA pipe instead of the
+// MUFU unit (6 of 16): the MUFU unit alone would bound the softmax.
+constexpr uint32_t kPolyPairs = (1u << 2) | (1u << 5) | (1u << 7) | (1u << 10) | (1u << 13) | (1u << 15);
 
 // Optional event trace (cc2_set_attention_trace): CTA 0 records %globaltimer
 // stamps of the first 8 query tiles of each pipeline (unit 8 G + tile).  Per
@@ -180,124 +183,67 @@ attn_tc_long_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           }
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ---------------- MMA issuer of both pipelines ----------------
+  } else if (warp == 1 || warp == 2) {
+    // ---------------- MMA issuer of pipeline G ----------------
+    // Per query tile: S_0, S_1, PV_0, S_2, PV_1, ..., S_{n-1}, PV_{n-2}, PV_{n-1}.
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
-    // Each pipeline is a small state machine; the thread polls both (never
-    // blocking on one) and advances whichever is ready.  Per query tile:
-    // S_0, S_1, PV_0, S_2, PV_1, ..., S_{n-1}, PV_{n-2}, PV_{n-1}.
+    const uint32_t G = (uint32_t)warp - 1u;
     if (lane == 0) {
-      enum { kKV, kQ, kS, kPV, kDone };
       const uint32_t id_s = idesc(128, kKB, false), id_o = idesc(128, 64, true);
-      const uint64_t dk0 = sw128_desc(sbase + a.k_off), dv0 = sw128_desc(sbase + a.v_off);
-      int st[2] = {my_items > 0 ? kKV : kDone, my_items > 0 ? kKV : kDone};
-      int li[2] = {0, 0}, qt[2] = {0, 1}, jb[2] = {0, 0};
-      uint32_t ns[2] = {0, 0}, np[2] = {0, 0}, nt[2] = {0, 0};
-      bool any = false;
-      unsigned long long last = globaltimer_ns();
-      uint32_t spins = 0;
-      while (st[0] != kDone || st[1] != kDone) {
-        bool progress = false;
+      const uint64_t dq = sw128_desc(sbase + G * kBlockBytes), dk0 = sw128_desc(sbase + a.k_off),
+                     dv0 = sw128_desc(sbase + a.v_off);
+      const uint32_t t_s = tmem + kSCol + 128u * G, t_p = tmem + kPCol + 64u * G, t_o = tmem + kOCol + 64u * G;
+      uint32_t ns = 0, np = 0, nt = 0;  // S blocks, P blocks, query tiles so far
+      bool ok = true, any = false;
+      // S_j = Q K_j^T, after the softmax threads read the previous S
+      auto issue_s = [&](int j) -> bool {
+        if (ns > 0 && !mbar_wait_inl(smem_u32(&s_free[G]), (ns - 1) & 1u, &abort_flag, err)) return false;
+        tc_fence_after();
+        const uint64_t dk = dk0 + (uint64_t)(j * (kBlockBytes >> 4));
 #pragma unroll
-        for (uint32_t G = 0; G < 2; ++G) {
-          const uint32_t t_s = tmem + kSCol + 128u * G, t_p = tmem + kPCol + 64u * G, t_o = tmem + kOCol + 64u * G;
-          switch (st[G]) {
-            case kKV:
-              if (!mbar_test(smem_u32(&kv_full), (uint32_t)li[G] & 1u)) break;
-              progress = true;
-              qt[G] = (int)G;
-              if (qt[G] < a.nqt) {
-                st[G] = kQ;
-              } else {
-                mma_commit(smem_u32(&kv_empty));
-                st[G] = ++li[G] < my_items ? kKV : kDone;
-              }
-              break;
-            case kQ:
-              if (!mbar_test(smem_u32(&q_full[G]), nt[G] & 1u)) break;
-              progress = true;
-              tc_fence_after();
-              st[G] = kS;
-              jb[G] = 0;
-              break;
-            case kS: {
-              if (ns[G] > 0 && !mbar_test(smem_u32(&s_free[G]), (ns[G] - 1) & 1u)) break;
-              progress = true;
-              tc_fence_after();
-              const int j = jb[G];
-              const uint64_t dq = sw128_desc(sbase + G * kBlockBytes);
-              const uint64_t dk = dk0 + (uint64_t)(j * (kBlockBytes >> 4));
-#pragma unroll
-              for (int ks = 0; ks < 4; ++ks) mma_bf16(t_s, dq + 2u * ks, dk + 2u * ks, id_s, ks > 0);
-              mma_commit(smem_u32(&s_full[G]));
-              trace(tr, G, nt[G], 8 * j + 5);
-              ++ns[G];
-              any = true;
-              if (j == a.nkb - 1) mma_commit(smem_u32(&q_empty[G]));  // the tile's last S MMA is issued
-              if (j == 0 && a.nkb > 1) {
-                jb[G] = 1;  // S_1 before PV_0
-              } else {
-                st[G] = kPV;
-                jb[G] = j == 0 ? 0 : j - 1;
-              }
-              break;
-            }
-            case kPV: {
-              if (!mbar_test(smem_u32(&p_full[G]), np[G] & 1u)) break;
-              progress = true;
-              const int j = jb[G];
-              trace(tr, G, nt[G], 8 * j + 6);
-              tc_fence_after();
-              const uint64_t dv = dv0 + (uint64_t)(j * (kBlockBytes >> 4));
-#pragma unroll
-              for (int ks = 0; ks < kKB / 16; ++ks)
-                mma_bf16_ts(t_o, t_p + 8u * ks, dv + 128u * ks, id_o, (j > 0 || ks > 0) ? 1u : 0u);
-              mma_commit(smem_u32(&p_free[G]));
-              trace(tr, G, nt[G], 8 * j + 7);
-              ++np[G];
-              if (j + 2 < a.nkb) {
-                st[G] = kS;
-                jb[G] = j + 2;
-              } else if (j + 1 < a.nkb) {
-                jb[G] = j + 1;  // the last PV follows the last S directly
-              } else {
-                mma_commit(smem_u32(&o_full[G]));
-                ++nt[G];
-                qt[G] += 2;
-                if (qt[G] < a.nqt) {
-                  st[G] = kQ;
-                } else {
-                  mma_commit(smem_u32(&kv_empty));
-                  st[G] = ++li[G] < my_items ? kKV : kDone;
-                }
-              }
-              break;
-            }
-            default:
-              break;
-          }
-        }
-        if (progress) {
-          spins = 0;
-          continue;
-        }
-        __nanosleep(32);  // leave the issue slots to the softmax warps of this SM quarter
-        if ((++spins & 63u) == 0) {
-          if (abort_flag) break;
-          const unsigned long long now = globaltimer_ns();
-          if (spins == 64) last = now;  // first idle check of this wait
-          if (now - last > kWaitLimitNs) {
-            abort_flag = 1;
-            atomicOr(err, 1);
+        for (int ks = 0; ks < 4; ++ks) mma_bf16(t_s, dq + 2u * ks, dk + 2u * ks, id_s, ks > 0);
+        mma_commit(smem_u32(&s_full[G]));
+        trace(tr, G, nt, 8 * j + 5);
+        ++ns;
+        any = true;
+        return true;
+      };
+      for (int li = 0; li < my_items && ok; ++li) {
+        if (!mbar_wait_inl(smem_u32(&kv_full), (uint32_t)li & 1u, &abort_flag, err)) break;
+        for (int qt = (int)G; qt < a.nqt && ok; qt += 2, ++nt) {
+          if (!mbar_wait_inl(smem_u32(&q_full[G]), nt & 1u, &abort_flag, err)) {
+            ok = false;
             break;
           }
+          tc_fence_after();
+          ok = issue_s(0);
+          for (int j = 0; j < a.nkb && ok; ++j) {
+            if (j + 1 < a.nkb) ok = issue_s(j + 1);
+            if (!ok) break;
+            if (j == a.nkb - 1) mma_commit(smem_u32(&q_empty[G]));  // the tile's last S MMA is issued
+            if (!mbar_wait_inl(smem_u32(&p_full[G]), np & 1u, &abort_flag, err)) {
+              ok = false;
+              break;
+            }
+            trace(tr, G, nt, 8 * j + 6);
+            tc_fence_after();
+            const uint64_t dv = dv0 + (uint64_t)(j * (kBlockBytes >> 4));
+#pragma unroll
+            for (int ks = 0; ks < kKB / 16; ++ks)
+              mma_bf16_ts(t_o, t_p + 8u * ks, dv + 128u * ks, id_o, (j > 0 || ks > 0) ? 1u : 0u);
+            mma_commit(smem_u32(&p_free[G]));
+            trace(tr, G, nt, 8 * j + 7);
+            ++np;
+          }
+          if (ok) mma_commit(smem_u32(&o_full[G]));
         }
+        if (ok) mma_commit(smem_u32(&kv_empty));  // this pipeline is done with the item's K and V
       }
       // every MMA issued above has completed before TMEM is released
       if (any) {
-        mma_commit(smem_u32(&mma_done[0]));
+        mma_commit(smem_u32(&mma_done[G]));
         const unsigned long long t0 = globaltimer_ns();
-        while (!mbar_try(smem_u32(&mma_done[0]), 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
+        while (!mbar_try(smem_u32(&mma_done[G]), 0) && globaltimer_ns() - t0 < kWaitLimitNs) {
         }
       }
     }
@@ -400,24 +346,33 @@ attn_tc_long_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
             // P_j = exp2(x - m), stored to TMEM 32 keys at a time; exponent
             // fma(x, 1, -m) = x - m exactly on masked blocks
             const bool clean = !((masked >> j) & 1u);
-            const float sc = clean ? kLog2e : 1.0f, nm = -m;
-            float l0 = 0.0f, l1 = 0.0f;
+            const float sc = clean ? kLog2e : 1.0f;
+            const uint64_t sc2 = f2_pack(sc, sc), nm2 = f2_pack(-m, -m);
+            uint64_t l2 = f2_pack(0.0f, 0.0f);
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
               uint32_t pk[16];
 #pragma unroll
-              for (int i = 0; i < 32; i += 4) {
-                const float p0 = ex2(fmaf(__uint_as_float(v[32 * c + i]), sc, nm));
-                const float p1 = ex2(fmaf(__uint_as_float(v[32 * c + i + 1]), sc, nm));
-                const float p2 = ex2(fmaf(__uint_as_float(v[32 * c + i + 2]), sc, nm));
-                const float p3 = ex2(fmaf(__uint_as_float(v[32 * c + i + 3]), sc, nm));
-                l0 += p0 + p1;
-                l1 += p2 + p3;
-                pk[i >> 1] = pack_bf16(p0, p1);
-                pk[(i >> 1) + 1] = pack_bf16(p2, p3);
+              for (int k = 0; k < 16; ++k) {
+                const uint64_t x2 =
+                    f2_fma(f2_pack(__uint_as_float(v[32 * c + 2 * k]), __uint_as_float(v[32 * c + 2 * k + 1])), sc2, nm2);
+                uint64_t p2;
+                if ((kPolyPairs >> k) & 1u) {
+                  p2 = f2_exp2_poly(x2);
+                } else {
+                  float x0, x1;
+                  f2_unpack(x2, x0, x1);
+                  p2 = f2_pack(ex2(x0), ex2(x1));
+                }
+                l2 = f2_add(l2, p2);
+                float p0, p1;
+                f2_unpack(p2, p0, p1);
+                pk[k] = pack_bf16(p0, p1);
               }
               tmem_st16(t_p + 16u * c, pk);
             }
+            float l0, l1;
+            f2_unpack(l2, l0, l1);
             l += l0 + l1;
             if (tw) trace(tr, G, nt, 8 * j + 2);
           }

@@ -170,6 +170,49 @@ __device__ __forceinline__ float max3(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
+// Packed pairs of fp32 (Blackwell f32x2 arithmetic: one instruction for two lanes).
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t r, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+// 2^x for a pair, on the FMA pipe instead of the MUFU unit: x clamped to
+// [-125, ...], split as n + f with n = round(x) (adding 1.5 * 2^23 leaves n in
+// the low mantissa bits) and f in [-1/2, 1/2]; 2^f from a degree-3 polynomial
+// (coefficients fitted here for minimal relative error on [-1/2, 1/2], at most
+// 7.5e-5), then n added to the exponent field.  For arguments <= 0 (softmax
+// numerators; -inf gives 2^-125 instead of 0).
+__device__ __forceinline__ uint64_t f2_exp2_poly(uint64_t x) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  float x0, x1;
+  f2_unpack(x, x0, x1);
+  x = f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t j = f2_add(x, f2_pack(kMagic, kMagic));
+  const uint64_t n = f2_add(j, f2_pack(-kMagic, -kMagic));
+  const uint64_t f = f2_fma(n, f2_pack(-1.0f, -1.0f), x);
+  uint64_t p = f2_fma(f2_pack(0.05517134442925453f, 0.05517134442925453f), f,
+                      f2_pack(0.24261033535003662f, 0.24261033535003662f));
+  p = f2_fma(p, f, f2_pack(0.6932609677314758f, 0.6932609677314758f));
+  p = f2_fma(p, f, f2_pack(0.9999281167984009f, 0.9999281167984009f));
+  float p0, p1, j0, j1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(j, j0, j1);
+  return f2_pack(__int_as_float(__float_as_int(p0) + (__float_as_int(j0) << 23)),
+                 __int_as_float(__float_as_int(p1) + (__float_as_int(j1) << 23)));
+}
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
