@@ -102,7 +102,14 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 // activation memory; only its prologue (barrier set-up, TMEM allocation,
 // descriptor prefetch, weight-only work) overlaps the previous kernel.
 // Outside a programmatic launch both instructions are no-ops.
+// The fp32 forward runs without it: its CUDA-core kernels span several waves,
+// and there the early launches cost more than they hide (configs[0] batch-1
+// latency 1.39 ms without, 2.02 ms with); the bf16 forward's kernels are
+// persistent and gain (batch-1 1.49 -> 1.30 ms).  t_launch_overlap is cleared
+// by the forward of an fp32 model for its duration.
 extern int g_launch_overlap;
+extern thread_local int t_launch_overlap;
+inline bool launch_overlap() { return g_launch_overlap != 0 && t_launch_overlap != 0; }
 
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -121,7 +128,7 @@ inline cudaError_t launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, siz
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = g_launch_overlap ? 1 : 0;
+  cfg.numAttrs = launch_overlap() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

@@ -35,6 +35,16 @@ namespace cc2 {
 
 // programmatic dependent launch of the forward's kernels (1 = on)
 int g_launch_overlap = 1;
+thread_local int t_launch_overlap = 1;
+
+namespace {
+// Sets t_launch_overlap for the duration of one forward.
+struct LaunchOverlapScope {
+  int saved;
+  explicit LaunchOverlapScope(int on) : saved(t_launch_overlap) { t_launch_overlap = on; }
+  ~LaunchOverlapScope() { t_launch_overlap = saved; }
+};
+}  // namespace
 
 // ---- status -----------------------------------------------------------------
 static thread_local std::string t_error;
@@ -536,6 +546,7 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
   CC2_REQUIRE(((uintptr_t)workspace & 255u) == 0, "workspace must be 256-byte aligned");
   const cc2_config& c = m->cfg;
   cudaStream_t st = (cudaStream_t)stream;
+  const LaunchOverlapScope overlap(m->dtype == CC2_BF16 ? 1 : 0);
   const size_t need = plan_ws(*m, B, L, N, nullptr, nullptr);
   if (ws_bytes < need) {
     set_error("workspace too small: %zu < %zu", ws_bytes, need);

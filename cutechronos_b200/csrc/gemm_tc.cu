@@ -913,7 +913,7 @@ static int launch_pair_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUt
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = g_launch_overlap ? 2 : 1;
+  cfg.numAttrs = launch_overlap() ? 2 : 1;
   CC2_CUDA(cudaLaunchKernelEx(&cfg, pair::gemm_pair_kernel<F, STAGES, BOXES, SKIP_EPI>, ma, mb, mc, mr, M, N, K,
                               ep));
   return CC2_OK;
