@@ -527,6 +527,7 @@ def run_micro(args):
     predp = rnd(Bp, 4, 336)
     locp, scp = torch.zeros(Bp, device=dev), torch.ones(Bp, device=dev)
     wln = rnd(d)
+    x4 = rnd(4 * M, d)
     cases = {
         "preprocess B=16384 L=2048 bf16": (
             lambda: kk.fused_preprocess(ctxp, 16, 8192, True, dtype=torch.bfloat16), 0,
@@ -534,6 +535,7 @@ def run_micro(args):
         "output transform B=16384 N=4 bf16": (
             lambda: kk.fused_output_transform(predp, locp, scp, 21, 16, True), 0, 2 * 2 * Bp * 4 * 336 + 8 * Bp),
         "rmsnorm M=34048 d=768 bf16": (lambda: kk.rms_layernorm(x, wln), 0, 2 * 2 * M * d),
+        "rmsnorm M=136192 d=768 bf16": (lambda: kk.rms_layernorm(x4, wln), 0, 2 * 2 * 4 * M * d),
         "qkv  N=2304 K=768 rowscale": (lambda: kk.linear(x, wqkv, row_ssq=ssq, norm_dim=d), 2 * M * 3 * d * d),
         "o    N=768  K=768 resid+ssq": (lambda: kk.linear(x, wo, residual=res, ssq_out=so, out=res), 2 * M * d * d),
         "ffn1 N=3072 K=768 rowscale+relu": (lambda: kk.linear(x, wi, row_ssq=ssq, norm_dim=d, relu=True),
