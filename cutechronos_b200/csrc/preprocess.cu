@@ -23,6 +23,29 @@ __device__ __forceinline__ uint32_t pack2bf(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Two sums in one pass over the block (one pair of barriers); red holds
+// 2 * warps doubles.
+__device__ __forceinline__ void block_sum2(double& a, double& b, double* red) {
+  for (int o = 16; o > 0; o >>= 1) {
+    a += __shfl_xor_sync(0xffffffffu, a, o);
+    b += __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = (int)(blockDim.x >> 5);
+  __syncthreads();
+  if (l == 0) {
+    red[w] = a;
+    red[nw + w] = b;
+  }
+  __syncthreads();
+  double ta = 0.0, tb = 0.0;
+  for (int i = 0; i < nw; ++i) {
+    ta += red[i];
+    tb += red[nw + i];
+  }
+  a = ta;
+  b = tb;
+}
+
 __device__ __forceinline__ double block_sum(double v, double* red) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -33,6 +56,10 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
   for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
   return t;
 }
+
+// A NaN in a caller's context mask counts as 0 (the reference patches the mask
+// and applies nan_to_num).
+__device__ __forceinline__ float nan_to_zero(float v) { return isnan(v) ? 0.0f : v; }
 
 // asinh for the vectorised preprocessing, from its definition
 // ln(|x| + sqrt(x^2 + 1)) with the hardware log2 and square root: absolute
@@ -104,7 +131,7 @@ preprocess_kernel(const float* __restrict__ ctx, const float* __restrict__ cmask
     float mk = 0.0f;
     if (src >= 0) {
       v = x[src];
-      mk = m ? m[src] : (isnan(v) ? 0.0f : 1.0f);
+      mk = m ? nan_to_zero(m[src]) : (isnan(v) ? 0.0f : 1.0f);
       float z = (v - lo) / sc;
       if (use_arcsinh) z = asinhf(z);
       v = z;
@@ -123,7 +150,7 @@ preprocess_kernel(const float* __restrict__ ctx, const float* __restrict__ cmask
     for (int c = 0; c < ps; ++c) {
       const int src = p * ps + c - pad;
       if (src >= 0) {
-        float mk = m ? m[src] : (isnan(x[src]) ? 0.0f : 1.0f);
+        float mk = m ? nan_to_zero(m[src]) : (isnan(x[src]) ? 0.0f : 1.0f);
         acc += roundT<T>(mk);
       }
     }
@@ -158,14 +185,14 @@ preprocess_kernel(const float* __restrict__ ctx, const float* __restrict__ cmask
 // [time_enc | value | mask] chunks written as 16-byte (bf16) / 32-byte (fp32)
 // stores.  Same arithmetic as preprocess_kernel.
 template <typename T, int CH>
-__global__ void __launch_bounds__(kPreThreads)
+__global__ void __launch_bounds__(kPreThreads, CH == 1 ? 5 : 1)
 preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ cmask, int L, int Leff, int P, int ps,
                       float te_scale, float te_inv, int use_arcsinh, int use_reg, int N, T* __restrict__ out, int ld,
                       int pad_cols, uint8_t* __restrict__ tok_mask, float* __restrict__ attn_out,
                       float* __restrict__ loc_out, float* __restrict__ scale_out, int vec_loads) {
   pdl_launch_dependents();
   pdl_wait();
-  __shared__ double red[kPreThreads / 32];
+  __shared__ double red[2 * (kPreThreads / 32)];
   const int b = blockIdx.x;
   const int S = P + use_reg + N;
   const float* x = ctx + (size_t)b * L + (L - Leff);
@@ -196,7 +223,7 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int src = s0 + i;
-        mk[c][i] = src < 0 ? 0.0f : (m ? m[src] : (isnan(v[c][i]) ? 0.0f : 1.0f));
+        mk[c][i] = src < 0 ? 0.0f : (m ? nan_to_zero(m[src]) : (isnan(v[c][i]) ? 0.0f : 1.0f));
         if (!isnan(v[c][i])) {
           sum += v[c][i];
           cnt += 1.0;
@@ -207,8 +234,7 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
       for (int i = 0; i < 8; ++i) mk[c][i] = 0.0f;
     }
   }
-  sum = block_sum(sum, red);
-  cnt = block_sum(cnt, red);
+  block_sum2(sum, cnt, red);
   const float lo = cnt > 0.0 ? (float)(sum / cnt) : 0.0f;
   double ss = 0.0;
 #pragma unroll
@@ -250,7 +276,7 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
           z = (v[c][i] - lo) * rsc;
           if (use_arcsinh) z = asinh_fast(z);
         }
-        mt[i] = mk[c][i];  // 0 or 1: exact in every dtype
+        mt[i] = roundT<T>(mk[c][i]);  // the mask in the model dtype (fractional masks pass through)
         // bf16: rounded once when packed below
         val[i] = mt[i] > 0.0f ? (sizeof(T) == 2 ? z : roundT<T>(z)) : 0.0f;
         te[i] = te_inv != 0.0f ? (tbase + (float)i) * te_inv : (float)(j0 + i - total) / te_scale;
@@ -265,11 +291,7 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
         w.x = pack2bf(val[0], val[1]); w.y = pack2bf(val[2], val[3]); w.z = pack2bf(val[4], val[5]);
         w.w = pack2bf(val[6], val[7]);
         *reinterpret_cast<uint4*>(r + ps) = w;
-        // mask 0 / 1 as bf16 bit patterns (1.0 = 0x3f80)
-        auto mbits = [](float lo2, float hi2) -> uint32_t {
-          return (lo2 > 0.0f ? 0x3f80u : 0u) | (hi2 > 0.0f ? 0x3f800000u : 0u);
-        };
-        w.x = mbits(mt[0], mt[1]); w.y = mbits(mt[2], mt[3]); w.z = mbits(mt[4], mt[5]); w.w = mbits(mt[6], mt[7]);
+        w.x = pack2bf(mt[0], mt[1]); w.y = pack2bf(mt[2], mt[3]); w.z = pack2bf(mt[4], mt[5]); w.w = pack2bf(mt[6], mt[7]);
         *reinterpret_cast<uint4*>(r + 2 * ps) = w;
       } else {
         float4* q4 = reinterpret_cast<float4*>(r);

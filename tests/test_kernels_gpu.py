@@ -80,6 +80,34 @@ def test_preprocess_bf16_and_explicit_mask(golden_small):
     assert d.max().item() <= 2 ** -7 * max(1.0, pc[..., 16:32].float().abs().max().item())
 
 
+# a caller's mask with fractional values and NaNs: the patched mask carries the
+# values in the model dtype, NaN counts as 0 (model.py:481-499)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("L", [2048, 512])
+def test_preprocess_fractional_mask(dtype, L):
+    g = torch.Generator().manual_seed(L)
+    ctx = torch.cumsum(torch.randn(3, L, generator=g), -1) + 50
+    ctx[0, :100] = float("nan")
+    mask = torch.rand(3, L, generator=g)
+    mask[mask < 0.2] = 0.0
+    mask[1, 5:40] = float("nan")
+    mask[2, ::7] = 1.0 / 3.0
+    cfg = oracle_config(context_length=8192, time_encoding_scale=8192)
+    pc, attn, loc, scale = orc.prepare_patched_context(cfg, ctx, mask, dtype)
+    gpc, gattn, gloc, gscale = K().fused_preprocess(ctx.to(DEV), 16, 8192, True, context_mask=mask.to(DEV),
+                                                    dtype=dtype)
+    gpc = gpc.cpu()
+    assert torch.equal(gattn.cpu().bool(), attn)
+    assert torch.equal(gpc[..., :16], pc[..., :16])
+    assert torch.equal(gpc[..., 32:], pc[..., 32:])
+    # a NaN value under a positive mask stays NaN, as in the reference
+    a, r = gpc[..., 16:32].float(), pc[..., 16:32].float()
+    assert torch.equal(torch.isnan(a), torch.isnan(r))
+    a, r = torch.nan_to_num(a), torch.nan_to_num(r)
+    tol = 2e-6 if dtype == torch.float32 else 2 ** -7 * max(1.0, r.abs().max().item())
+    assert (a - r).abs().max().item() <= tol
+
+
 def test_preprocess_patch_size_1():
     ctx = _ctx(2, 40, 0.2, 8)
     cfg = orc.OracleConfig(context_length=512, input_patch_size=1, output_patch_size=1)
