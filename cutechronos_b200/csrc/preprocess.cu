@@ -184,25 +184,33 @@ preprocess_kernel(const float* __restrict__ ctx, const float* __restrict__ cmask
 // three passes), 16-byte loads when the series is 16-byte aligned, and the
 // [time_enc | value | mask] chunks written as 16-byte (bf16) / 32-byte (fp32)
 // stores.  Same arithmetic as preprocess_kernel.
+// Vectorised preprocessing: one CTA per series of up to 4 x 8 x kPreThreads
+// positions.  Each thread holds CH chunks of 8 consecutive positions in
+// registers across the mean, variance and patching passes; 16-byte loads and
+// stores.  (A warp per series, with up to 64 positions per lane, ran slower:
+// fewer series fit on an SM and each warp's chain of work grew.)
 template <typename T, int CH>
 __global__ void __launch_bounds__(kPreThreads, CH == 1 ? 5 : 1)
-preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ cmask, int L, int Leff, int P, int ps,
-                      float te_scale, float te_inv, int use_arcsinh, int use_reg, int N, T* __restrict__ out, int ld,
-                      int pad_cols, uint8_t* __restrict__ tok_mask, float* __restrict__ attn_out,
-                      float* __restrict__ loc_out, float* __restrict__ scale_out, int vec_loads) {
+preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ cmask, int B, int L, int Leff, int P,
+                      int ps, float te_scale, float te_inv, int use_arcsinh, int use_reg, int N,
+                      T* __restrict__ out, int ld, int pad_cols, uint8_t* __restrict__ tok_mask,
+                      float* __restrict__ attn_out, float* __restrict__ loc_out, float* __restrict__ scale_out,
+                      int vec_loads) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ double red[2 * (kPreThreads / 32)];
-  const int b = blockIdx.x;
+  const int b = (int)blockIdx.x;
+  const int tid = (int)threadIdx.x;
+  const int G = (int)blockDim.x;
   const int S = P + use_reg + N;
   const float* x = ctx + (size_t)b * L + (L - Leff);
   const float* m = cmask ? cmask + (size_t)b * L + (L - Leff) : nullptr;
   const int total = P * ps, pad = total - Leff;
-  float v[CH][8], mk[CH][8];
+  float v[CH][8];
   double sum = 0.0, cnt = 0.0;
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
-    const int j0 = 8 * ((int)threadIdx.x + c * (int)blockDim.x);
+    const int j0 = 8 * (tid + c * G);
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[c][i] = __int_as_float(0x7fc00000);
     if (j0 < total) {
@@ -220,20 +228,16 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
         for (int i = 0; i < 8; ++i)
           if (s0 + i >= 0) v[c][i] = x[s0 + i];
       }
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int src = s0 + i;
-        mk[c][i] = src < 0 ? 0.0f : (m ? nan_to_zero(m[src]) : (isnan(v[c][i]) ? 0.0f : 1.0f));
-        if (!isnan(v[c][i])) {
-          sum += v[c][i];
-          cnt += 1.0;
-        }
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mk[c][i] = 0.0f;
     }
   }
+#pragma unroll
+  for (int c = 0; c < CH; ++c)
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (!isnan(v[c][i])) {
+        sum += v[c][i];
+        cnt += 1.0;
+      }
   block_sum2(sum, cnt, red);
   const float lo = cnt > 0.0 ? (float)(sum / cnt) : 0.0f;
   double ss = 0.0;
@@ -248,7 +252,7 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
   ss = block_sum(ss, red);
   float sc = cnt > 0.0 ? sqrtf((float)(ss / cnt)) : 1.0f;
   if (sc == 0.0f) sc = 1e-5f;
-  if (threadIdx.x == 0) {
+  if (tid == 0) {
     loc_out[b] = lo;
     scale_out[b] = sc;
   }
@@ -259,7 +263,7 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
   const int cpp = ps / 8;  // chunks per patch: 1, 2 or 4 adjacent lanes
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
-    const int k = (int)threadIdx.x + c * (int)blockDim.x;
+    const int k = tid + c * G;
     const int j0 = 8 * k;
     float acc = 0.0f;
     if (j0 < total) {
@@ -272,11 +276,13 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
       for (int i = 0; i < 8; ++i) {
         const int src = j0 + i - pad;
         float z = __int_as_float(0x7fc00000);
+        float mk = 0.0f;
         if (src >= 0) {
           z = (v[c][i] - lo) * rsc;
           if (use_arcsinh) z = asinh_fast(z);
+          mk = m ? nan_to_zero(m[src]) : (isnan(v[c][i]) ? 0.0f : 1.0f);
         }
-        mt[i] = roundT<T>(mk[c][i]);  // the mask in the model dtype (fractional masks pass through)
+        mt[i] = roundT<T>(mk);  // the mask in the model dtype (fractional masks pass through)
         // bf16: rounded once when packed below
         val[i] = mt[i] > 0.0f ? (sizeof(T) == 2 ? z : roundT<T>(z)) : 0.0f;
         te[i] = te_inv != 0.0f ? (tbase + (float)i) * te_inv : (float)(j0 + i - total) / te_scale;
@@ -317,7 +323,7 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
   }
   // REG row (zeros) and future rows ([future time enc | 0 | 0])
   const int extra = use_reg + N;
-  for (int idx = threadIdx.x; idx < extra * 3 * ps; idx += blockDim.x) {
+  for (int idx = tid; idx < extra * 3 * ps; idx += G) {
     const int e = idx / (3 * ps), c = idx % (3 * ps);
     T* r = out + (row0 + P + e) * ld;
     float fv = 0.0f;
@@ -325,10 +331,10 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
     if (n >= 0 && c < ps) fv = (float)(n * ps + c) / te_scale;
     r[c] = fromf<T>(fv);
   }
-  for (int e = threadIdx.x; e < extra; e += blockDim.x) tok_mask[row0 + P + e] = 1;
+  for (int e = tid; e < extra; e += G) tok_mask[row0 + P + e] = 1;
   const int pc = pad_cols - 3 * ps;
   if (pc > 0)
-    for (int idx = threadIdx.x; idx < S * pc; idx += blockDim.x) {
+    for (int idx = tid; idx < S * pc; idx += G) {
       const int rr = idx / pc, c = idx % pc;
       out[(row0 + rr) * ld + 3 * ps + c] = fromf<T>(0.0f);
     }
@@ -514,14 +520,21 @@ int launch_preprocess(const float* context, const float* cmask, int B, int L, in
   int te_exp = 0;
   const float te_frac = std::frexp(te_scale, &te_exp);
   const float te_inv = te_frac == 0.5f && te_exp > -120 && te_exp < 120 ? std::ldexp(1.0f, 1 - te_exp) : 0.0f;
-#define CC2_PRE_VEC(TT, C_)                                                                                   \
-  CC2_CUDA(launch_k(preprocess_vec_kernel<TT, C_>, B, kPreThreads, 0, st, context, cmask, L, Leff, P, ps, te_scale, te_inv, use_arcsinh, \
-                                                          use_reg ? 1 : 0, N, (TT*)patched, ld, pad_cols, tok, attn,  \
-                                                          loc, scale, vec_loads))
+#define CC2_PRE_VEC(TT, C_)                                                                                       \
+  CC2_CUDA(launch_k(preprocess_vec_kernel<TT, C_>, B, kPreThreads, 0, st, context, cmask, B, L, Leff, P, ps,       \
+                    te_scale, te_inv, use_arcsinh, use_reg ? 1 : 0, N, (TT*)patched, ld, pad_cols, tok, attn, loc, \
+                    scale, vec_loads))
+#define CC2_PRE_VEC_ALL(TT)       \
+  if (CH == 1)                    \
+    CC2_PRE_VEC(TT, 1);           \
+  else if (CH == 2)               \
+    CC2_PRE_VEC(TT, 2);           \
+  else                            \
+    CC2_PRE_VEC(TT, 4);
   if (vec && dtype == CC2_BF16) {
-    if (CH == 1) CC2_PRE_VEC(__nv_bfloat16, 1); else if (CH == 2) CC2_PRE_VEC(__nv_bfloat16, 2); else CC2_PRE_VEC(__nv_bfloat16, 4);
+    CC2_PRE_VEC_ALL(__nv_bfloat16)
   } else if (vec && dtype == CC2_F32) {
-    if (CH == 1) CC2_PRE_VEC(float, 1); else if (CH == 2) CC2_PRE_VEC(float, 2); else CC2_PRE_VEC(float, 4);
+    CC2_PRE_VEC_ALL(float)
   } else if (dtype == CC2_BF16) {
     CC2_CUDA(launch_k(preprocess_kernel<__nv_bfloat16>, B, kPreThreads, 0, st, 
         context, cmask, L, Leff, P, ps, te_scale, use_arcsinh, use_reg ? 1 : 0, N,
