@@ -11,6 +11,8 @@ gathered to every rank with NCCL all_gather inside the step.
 Metric: forecasts/s (whole job).  Timing: CUDA events on the launching stream
 per step; L2 is flushed (256 MB write) before every timed step, outside the
 event pair; barrier + synchronize around the timed loop; max over ranks.
+Per-kernel durations (roofline, kernel shares, launch count) come from a
+second, instrumented pass over the same steps, outside the timed region.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
 
@@ -328,7 +330,6 @@ def run_b200(args):
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
-        nat.check(lib.cc2_profile_begin(cap), "cc2_profile_begin")
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
         for i in range(args.steps):
             flush.fill_(i & 0xFF)
@@ -340,6 +341,14 @@ def run_b200(args):
             dist.barrier()
         clocks.stop()
         step_ms = [a.elapsed_time(b) for a, b in evs]
+        # the same steps once more with a CUDA-event pair around every launch
+        # (per-kernel durations for the roofline and the kernel shares); kept out
+        # of the timed region above, whose launches run back to back
+        nat.check(lib.cc2_profile_begin(cap), "cc2_profile_begin")
+        for i in range(args.steps):
+            flush.fill_(i & 0xFF)
+            step(ctx)
+        torch.cuda.synchronize()
         kinds = (C.c_int * cap)()
         ms = (C.c_float * cap)()
         fl = (C.c_double * cap)()
