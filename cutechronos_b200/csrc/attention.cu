@@ -48,8 +48,9 @@ int launch_attn_tc(const void* qkv, int ld, int qcol, int kcol, int vcol, void* 
 
 // 0 (default): tcgen05 time attention for sets of 112..144 tokens, where it
 // is faster than the mma.sync kernels, and the long-set tcgen05 kernel for
-// 145..640 tokens; 1: the mma.sync kernels only; 2: tcgen05 for every set it
-// supports (17..640 tokens).  Set through
+// 145..640 tokens; 1: the mma.sync kernels only for time attention and the
+// scalar kernel for small groups; 2: tcgen05 for every set it supports
+// (17..640 tokens).  Set through
 // cc2_set_attention_variant.
 int g_attn_variant = 0;
 
@@ -969,6 +970,143 @@ attn_persist_kernel(const __grid_constant__ CUtensorMap tmQKV, bf16* __restrict_
   }
 }
 
+// ---------------------------------------------------------------------------
+// group attention for groups of <= 16 series on the tensor cores (bf16)
+// ---------------------------------------------------------------------------
+// One CTA per (time step, group), one warp per head.  The group's Q, K and V
+// rows (all heads) are staged in shared memory with cp.async; rows past the
+// group's size read a zero row.  Per head: S = Q K^T as mma.sync m16n8k16
+// (M = 16 query rows, N = 8 or 16 keys, K = 64), the softmax on the
+// accumulator fragments (quad shuffles), P re-packed from the accumulators
+// as the A fragment, split into two bf16 parts (hi + lo) so that it keeps
+// about 16 significant bits, and O = P V (K = 16 keys, N = 64 in blocks of
+// 8, V read with ldmatrix.trans).  Masking as attn_group_small_kernel: a masked key
+// scores -1e30, keys past the group -inf.  The scalar kernel unpacked each
+// bf16 Q/K/V element once per use (the ALU bound it ran at).
+constexpr int kGroupMmaMaxN = 16, kGroupMmaMaxHeads = 16;
+
+__global__ void __launch_bounds__(32 * kGroupMmaMaxHeads)
+attn_group_mma_kernel(const bf16* __restrict__ qkv, int ld, int qcol, int kcol, int vcol, bf16* __restrict__ out,
+                      int ldo, const uint8_t* __restrict__ tok, SetInfo si, int heads) {
+  pdl_launch_dependents();
+  pdl_wait();
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const SetGeom g = set_geom(si, blockIdx.x);
+  const int n = g.n;
+  if (n <= 0) return;
+  const int HD = heads * DH;
+  const int pitch = HD * 2 + 16;  // bytes per staged row: +16 keeps ldmatrix rows on distinct banks
+  const uint32_t sb = (uint32_t)__cvta_generic_to_shared(smem_raw);
+  const uint32_t zero_row = sb + 3u * (uint32_t)n * (uint32_t)pitch;
+  float* kb = reinterpret_cast<float*>(smem_raw + (size_t)(3 * n + 1) * pitch);
+  const int tid = threadIdx.x;
+  const int cpr = HD / 8;  // 16-byte chunks per row and matrix
+  for (int idx = tid; idx < 3 * n * cpr; idx += blockDim.x) {
+    const int mtx = idx / (n * cpr), rem = idx - mtx * n * cpr;
+    const int i = rem / cpr, c = rem - i * cpr;
+    const int col = (mtx == 0 ? qcol : mtx == 1 ? kcol : vcol) + 8 * c;
+    const bf16* src = qkv + (size_t)g.row(i, si.S) * ld + col;
+    const uint32_t dst = sb + (uint32_t)((mtx * n + i) * pitch + 16 * c);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+  }
+  for (int c = tid; c < cpr; c += blockDim.x)
+    asm volatile("st.shared.v4.b32 [%0], {%1,%1,%1,%1};" ::"r"(zero_row + 16u * c), "r"(0u) : "memory");
+  if (tid < kGroupMmaMaxN)
+    kb[tid] = tid < n ? (tok[g.row(tid, si.S)] ? 0.0f : kMaskedScore) : -INFINITY;
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncthreads();
+
+  const int h = tid >> 5, lane = tid & 31;
+  if (h >= heads) return;
+  const int gq = lane >> 2, tq = lane & 3;  // fragment row group and column pair
+  const uint32_t qbase = sb, kbase = sb + (uint32_t)(n * pitch), vbase = sb + (uint32_t)(2 * n * pitch);
+  auto row_addr = [&](uint32_t base, int r) -> uint32_t {
+    return r < n ? base + (uint32_t)(r * pitch) : zero_row;
+  };
+  const bool two = n > 8;  // a second block of 8 keys
+  // ---- S = Q K^T ----
+  float s[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+  {
+    const int ar = lane & 15, ac = (lane >> 4) * 8;                  // A: rows 0-15, column halves
+    const int bk = (lane & 7) + ((lane >> 4) << 3), bc = ((lane >> 3) & 1) * 8;  // B: key rows, dim halves
+    const uint32_t a_row = row_addr(qbase, ar), b_row = row_addr(kbase, bk);
+#pragma unroll
+    for (int ks = 0; ks < DH / 16; ++ks) {
+      const int d0 = h * DH + 16 * ks;
+      uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
+      ldsm_x4(a_row + 2u * (uint32_t)(d0 + ac), a0, a1, a2, a3);
+      ldsm_x4(b_row + 2u * (uint32_t)(d0 + bc), b0, b1, b2, b3);
+      mma16816(s[0], a0, a1, a2, a3, b0, b1);
+      if (two) mma16816(s[1], a0, a1, a2, a3, b2, b3);
+    }
+  }
+  // ---- softmax over the keys of rows gq and gq + 8 ----
+  float mx0 = -INFINITY, mx1 = -INFINITY;
+#pragma unroll
+  for (int nb = 0; nb < 2; ++nb) {
+    const float k0 = kb[8 * nb + 2 * tq], k1 = kb[8 * nb + 2 * tq + 1];
+    s[nb][0] = fmaf(s[nb][0], kLog2e, k0);
+    s[nb][1] = fmaf(s[nb][1], kLog2e, k1);
+    s[nb][2] = fmaf(s[nb][2], kLog2e, k0);
+    s[nb][3] = fmaf(s[nb][3], kLog2e, k1);
+    mx0 = fmaxf(mx0, fmaxf(s[nb][0], s[nb][1]));
+    mx1 = fmaxf(mx1, fmaxf(s[nb][2], s[nb][3]));
+  }
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
+  mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
+  mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
+  // P as the sum of two bf16 fragments (P = hi + lo, about 16 significant
+  // bits) so that P V keeps the precision of the fp32 weights
+  float l0 = 0.f, l1 = 0.f;
+  uint32_t pa[4], pl[4];
+  auto split = [](float x, float y, uint32_t& hi, uint32_t& lo) {
+    hi = pack2(x, y);
+    const __nv_bfloat162 h = *reinterpret_cast<const __nv_bfloat162*>(&hi);
+    lo = pack2(x - __bfloat162float(h.x), y - __bfloat162float(h.y));
+  };
+#pragma unroll
+  for (int nb = 0; nb < 2; ++nb) {
+    const float p0 = exp2f(s[nb][0] - mx0), p1 = exp2f(s[nb][1] - mx0);
+    const float p2 = exp2f(s[nb][2] - mx1), p3 = exp2f(s[nb][3] - mx1);
+    l0 += p0 + p1;
+    l1 += p2 + p3;
+    split(p0, p1, pa[2 * nb], pl[2 * nb]);          // row gq,     keys 8 nb + 2 tq ..
+    split(p2, p3, pa[2 * nb + 1], pl[2 * nb + 1]);  // row gq + 8
+  }
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+  const float inv0 = 1.0f / l0, inv1 = 1.0f / l1;
+  // ---- O = P V, 8 dims at a time ----
+  const int vk = (lane & 7) + (((lane >> 3) & 1) << 3), vc = (lane >> 4) * 8;  // key rows, dim-block pair
+  const uint32_t v_row = row_addr(vbase, vk);
+  const int r0 = gq, r1 = gq + 8;
+  bf16* o0 = r0 < n ? out + (size_t)g.row(r0, si.S) * ldo + h * DH : nullptr;
+  bf16* o1 = r1 < n ? out + (size_t)g.row(r1, si.S) * ldo + h * DH : nullptr;
+#pragma unroll
+  for (int dn = 0; dn < DH / 8; dn += 2) {
+    uint32_t b0, b1, b2, b3;
+    ldsm_x4_t(v_row + 2u * (uint32_t)(h * DH + 8 * dn + vc), b0, b1, b2, b3);
+    float o[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    mma16816(o[0], pl[0], pl[1], pl[2], pl[3], b0, b1);
+    mma16816(o[1], pl[0], pl[1], pl[2], pl[3], b2, b3);
+    mma16816(o[0], pa[0], pa[1], pa[2], pa[3], b0, b1);
+    mma16816(o[1], pa[0], pa[1], pa[2], pa[3], b2, b3);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int c = 8 * (dn + e) + 2 * tq;
+      if (o0) *reinterpret_cast<uint32_t*>(o0 + c) = pack2(o[e][0] * inv0, o[e][1] * inv0);
+      if (o1) *reinterpret_cast<uint32_t*>(o1 + c) = pack2(o[e][2] * inv1, o[e][3] * inv1);
+    }
+  }
+}
+
+inline size_t group_mma_smem(int n, int heads) {
+  return (size_t)(3 * n + 1) * (heads * DH * 2 + 16) + kGroupMmaMaxN * sizeof(float);
+}
+
 inline size_t small_group_smem(int n, int heads, size_t esz) {
   return 3 * (size_t)n * (heads * DH * esz + 16) + ((size_t)heads * n * n + n) * sizeof(float);
 }
@@ -1036,6 +1174,19 @@ int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int
       CC2_CUDA(cudaGetSymbolAddress((void**)&err, g_attn_error));
       const int grid = std::min(num_sets * heads, num_sms());
       CC2_CUDA(launch_k(attn_persist_kernel, grid, kPWarps * 32, smem_p, st, map, (bf16*)out, ldo, tok, pa, err));
+    } else if (mode == 1 && max_group <= kGroupMmaMaxN && heads <= kGroupMmaMaxHeads && g_attn_variant != 1 &&
+               ((uintptr_t)qkv & 15u) == 0 && ((uintptr_t)out & 3u) == 0) {
+      const size_t sm = group_mma_smem(max_group, heads);
+      static unsigned long long attr_g = 0;  // one bit per device
+      int dev = 0;
+      CC2_CUDA(cudaGetDevice(&dev));
+      if (dev >= 64 || !((attr_g >> dev) & 1ull)) {
+        CC2_CUDA(cudaFuncSetAttribute(attn_group_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)group_mma_smem(kGroupMmaMaxN, kGroupMmaMaxHeads)));
+        if (dev < 64) attr_g |= 1ull << dev;
+      }
+      CC2_CUDA(launch_k(attn_group_mma_kernel, num_sets, 32 * heads, sm, st, (const bf16*)qkv, ld, qcol, kcol, vcol,
+                        (bf16*)out, ldo, tok, si, heads));
     } else if (mode == 1 && max_group <= kSmallGroupMax) {
       const size_t sm = small_group_smem(max_group, heads, sizeof(bf16));
       CC2_TRY(set_small_group_attr<bf16>(sm));

@@ -368,7 +368,8 @@ def test_attention_uniform_known_answer():
 
 
 @pytest.mark.parametrize("gids,S", [([0, 0, 1, 1, 1, 2, 3, 3], 19), ([5] * 40 + [1] * 3, 9), (list(range(6)), 7),
-                                    ([0] * 100, 5)])
+                                    ([0] * 100, 5), ([0] * 8 + [1] * 9 + [2] * 16 + [3], 7),
+                                    ([i // 8 for i in range(64)], 133)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_group_attention(gids, S, dtype):
     B, H = len(gids), 12
