@@ -1001,13 +1001,13 @@ attn_group_mma_kernel(const bf16* __restrict__ qkv, int ld, int qcol, int kcol, 
   float* kb = reinterpret_cast<float*>(smem_raw + (size_t)(3 * n + 1) * pitch);
   const int tid = threadIdx.x;
   const int cpr = HD / 8;  // 16-byte chunks per row and matrix
-  for (int idx = tid; idx < 3 * n * cpr; idx += blockDim.x) {
-    const int mtx = idx / (n * cpr), rem = idx - mtx * n * cpr;
-    const int i = rem / cpr, c = rem - i * cpr;
-    const int col = (mtx == 0 ? qcol : mtx == 1 ? kcol : vcol) + 8 * c;
-    const bf16* src = qkv + (size_t)g.row(i, si.S) * ld + col;
-    const uint32_t dst = sb + (uint32_t)((mtx * n + i) * pitch + 16 * c);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+  // a warp per (matrix, row), its lanes along the row
+  for (int wr = tid >> 5; wr < 3 * n; wr += (int)(blockDim.x >> 5)) {
+    const int mtx = wr >= 2 * n ? 2 : wr >= n ? 1 : 0, i = wr - mtx * n;
+    const bf16* src = qkv + (size_t)g.row(i, si.S) * ld + (mtx == 0 ? qcol : mtx == 1 ? kcol : vcol);
+    const uint32_t dst = sb + (uint32_t)(wr * pitch);
+    for (int c = tid & 31; c < cpr; c += 32)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst + 16u * c), "l"(src + 8 * c) : "memory");
   }
   for (int c = tid; c < cpr; c += blockDim.x)
     asm volatile("st.shared.v4.b32 [%0], {%1,%1,%1,%1};" ::"r"(zero_row + 16u * c), "r"(0u) : "memory");
