@@ -353,8 +353,10 @@ __device__ __forceinline__ void rope_qk_swz(uint8_t* Qt, uint8_t* Kt, int n, con
   }
 }
 
-template <bool ROPE>
-__global__ void __launch_bounds__(kSetMaxWarps * 32, 2)
+// KTT: keys per inner tile (64; 48 for sets of at most 48 tokens, which then
+// take one tile and fewer registers, so more CTAs share an SM)
+template <bool ROPE, int KTT>
+__global__ void __launch_bounds__(KTT == 64 ? kSetMaxWarps * 32 : 128, KTT == 64 ? 2 : 5)
 attn_set_kernel(const bf16* __restrict__ qkv, int ld, int qcol, int kcol, int vcol, bf16* __restrict__ out,
                 int ldo, const uint8_t* __restrict__ tok, const float2* __restrict__ rope, SetInfo si) {
   pdl_launch_dependents();
@@ -408,11 +410,11 @@ attn_set_kernel(const bf16* __restrict__ qkv, int ld, int qcol, int kcol, int vc
     for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
     float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
 
-    for (int k0 = 0; k0 < n; k0 += KT) {
+    for (int k0 = 0; k0 < n; k0 += KTT) {
       const int kvalid = n - k0;
-      float s[8][4];
+      float s[KTT / 8][4];
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int nt = 0; nt < KTT / 8; ++nt) {
         s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
         if (nt * 8 < kvalid) {
           const int kr = k0 + nt * 8 + (lane & 7);
@@ -427,7 +429,7 @@ attn_set_kernel(const bf16* __restrict__ qkv, int ld, int qcol, int kcol, int vc
       }
       float mx0 = -INFINITY, mx1 = -INFINITY;
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int nt = 0; nt < KTT / 8; ++nt) {
         const int c = nt * 8 + 2 * (lane & 3);
         const float b0 = c < kvalid ? kbias[k0 + c] : -INFINITY;
         const float b1 = c + 1 < kvalid ? kbias[k0 + c + 1] : -INFINITY;
@@ -449,14 +451,14 @@ attn_set_kernel(const bf16* __restrict__ qkv, int ld, int qcol, int kcol, int vc
 #pragma unroll
       for (int dt = 0; dt < 8; ++dt) { o[dt][0] *= c0; o[dt][1] *= c0; o[dt][2] *= c1; o[dt][3] *= c1; }
 #pragma unroll
-      for (int nt = 0; nt < 8; ++nt) {
+      for (int nt = 0; nt < KTT / 8; ++nt) {
         s[nt][0] = exp2f(s[nt][0] - mn0); s[nt][1] = exp2f(s[nt][1] - mn0);
         s[nt][2] = exp2f(s[nt][2] - mn1); s[nt][3] = exp2f(s[nt][3] - mn1);
         l0 += s[nt][0] + s[nt][1];
         l1 += s[nt][2] + s[nt][3];
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < KTT / 16; ++j) {
         if (j * 16 < kvalid) {
           const uint32_t a0 = pack2(s[2 * j][0], s[2 * j][1]);
           const uint32_t a1 = pack2(s[2 * j][2], s[2 * j][3]);
@@ -1201,19 +1203,28 @@ int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int
       int dev = 0;
       CC2_CUDA(cudaGetDevice(&dev));
       if (dev >= 64 || !((attr_done >> dev) & 1ull)) {
-        CC2_CUDA(cudaFuncSetAttribute(attn_set_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        CC2_CUDA(cudaFuncSetAttribute(attn_set_kernel<true, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)kSetSmemLimit));
-        CC2_CUDA(cudaFuncSetAttribute(attn_set_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        CC2_CUDA(cudaFuncSetAttribute(attn_set_kernel<false, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       (int)kSetSmemLimit));
         if (dev < 64) attr_done |= 1ull << dev;
       }
       dim3 grid(heads, num_sets);
-      if (mode == 0 && cs)
-        CC2_CUDA(launch_k(attn_set_kernel<true>, grid, warps * 32, smem, st, (const bf16*)qkv, ld, qcol, kcol, vcol, (bf16*)out,
-                                                              ldo, tok, cs, si));
-      else
-        CC2_CUDA(launch_k(attn_set_kernel<false>, grid, warps * 32, smem, st, (const bf16*)qkv, ld, qcol, kcol, vcol,
-                                                               (bf16*)out, ldo, tok, cs, si));
+      const bool rope_k = mode == 0 && cs;
+      if (nmax <= 48 && warps * 32 <= 128) {  // one 48-key tile; smem < 48 KB needs no attribute
+        if (rope_k)
+          CC2_CUDA(launch_k(attn_set_kernel<true, 48>, grid, warps * 32, smem, st, (const bf16*)qkv, ld, qcol, kcol,
+                            vcol, (bf16*)out, ldo, tok, cs, si));
+        else
+          CC2_CUDA(launch_k(attn_set_kernel<false, 48>, grid, warps * 32, smem, st, (const bf16*)qkv, ld, qcol, kcol,
+                            vcol, (bf16*)out, ldo, tok, cs, si));
+      } else if (rope_k) {
+        CC2_CUDA(launch_k(attn_set_kernel<true, 64>, grid, warps * 32, smem, st, (const bf16*)qkv, ld, qcol, kcol, vcol,
+                          (bf16*)out, ldo, tok, cs, si));
+      } else {
+        CC2_CUDA(launch_k(attn_set_kernel<false, 64>, grid, warps * 32, smem, st, (const bf16*)qkv, ld, qcol, kcol,
+                          vcol, (bf16*)out, ldo, tok, cs, si));
+      }
     } else {
       dim3 grid((nmax + QT - 1) / QT, heads, num_sets);
       if (mode == 0 && cs)
