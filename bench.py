@@ -439,7 +439,9 @@ def run_b200(args):
     result = None
     if rank == 0:
         cpu_v, cpu_threads = None, 0
-        if not args.no_cpu:
+        # the CPU baseline runs at N = 1 only (under torchrun the other ranks'
+        # processes share the host cores)
+        if not args.no_cpu and world == 1:
             ref = CpuReference()
             ref.forecasts_per_s(1, L, N)
             cpu_v, cpu_threads = ref.forecasts_per_s(8, L, N), ref.threads
@@ -480,8 +482,9 @@ def run_b200(args):
             "kernels": kernels,
             "clocks": clk,
             "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads, "kind": "port",
-                             "sample": "8 series of configs[1] (ctx 2048, N=4), fp32 CPU oracle restatement "
-                                       "of CuteChronos2Model.forward, one forward"},
+                             "sample": ("8 series of configs[1] (ctx 2048, N=4), fp32 CPU oracle restatement "
+                                        "of CuteChronos2Model.forward, one forward") if world == 1 else
+                             "not measured at N > 1 (taken on rank 0 of the N = 1 run)"},
         }
         print(json.dumps(result), flush=True)
     if world > 1:
