@@ -83,6 +83,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__
   // every read of the item that used it before
   __shared__ __align__(16) float kbias[3][kMaxNK];
   __shared__ float red_max[2][128], red_sum[2][128];
+  // key bias buffer li % 3 filled (32 producer lanes arrive; phase li / 3).  Its
+  // parity cannot alias: the producer refills a buffer only after the S MMA of
+  // a later item, which needs this item's P.  (full_qk, which the producer may
+  // complete twice while the softmax warps finish an item, would alias.)
+  __shared__ __align__(8) uint64_t kb_full[3];
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
 
@@ -103,6 +108,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__
     mbar_init(smem_u32(&p_full), 8);
     mbar_init(smem_u32(&o_full), 1);
     mbar_init(smem_u32(&mma_done), 1);
+    for (int i = 0; i < 3; ++i) mbar_init(smem_u32(&kb_full[i]), 32);
     abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -144,6 +150,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__
       float* kb = kbias[li % 3];
       for (int k = lane; k < NKM; k += 32)
         kb[k] = k < a.S ? (tok[(size_t)b * a.S + k] ? 0.0f : kMaskedScore) : -INFINITY;
+      mbar_arrive(smem_u32(&kb_full[li % 3]));
       mbar_arrive(bqk);
       qk_phase[st] = n;
       if (n > 0 && !mbar_wait(smem_u32(&empty_v[st]), (uint32_t)(n - 1) & 1u, &abort_flag, err)) break;
@@ -231,91 +238,95 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__
     const uint32_t t_o = tmem + ((uint32_t)(32 * q) << 16) + kOCol + 32u * hf;
     const uint32_t prow = pbase + (uint32_t)r * 128u;
     const uint32_t sw = (uint32_t)(r & 7);
-    const uint32_t pair_bar = 1u + (uint32_t)q;  // named barrier of the two warps on these lanes
+    // Named barrier of the two warps on these lanes.  Both pass the same two
+    // barriers per tile whether or not they hold rows of it; a failed bounded
+    // wait is carried to the next barrier, whose AND tells both to stop, so
+    // neither can be left waiting for the other.
+    const uint32_t pair_bar = 1u + (uint32_t)q;
     uint32_t u = 0;
-    for (int li = 0; li < my_items; ++li) {
-      const int st = li % a.stages, n = li / a.stages;
-      if (!mbar_wait(smem_u32(&full_qk[st]), (uint32_t)n & 1u, &abort_flag, err)) break;  // key bias
+    bool ok = true;
+    for (int li = 0; li < my_items && ok; ++li) {
+      ok = mbar_wait(smem_u32(&kb_full[li % 3]), (uint32_t)(li / 3) & 1u, &abort_flag, err);  // key bias
       const int item = (int)blockIdx.x + li * (int)gridDim.x;
       const int b = item / a.heads, h = item % a.heads;
       const float* kb = kbias[li % 3] + c0;
-      bool ok = true;
       for (int t = 0; t < a.T; ++t, ++u) {
         // lane r holds query row t * 128 + r - lane0 (tile 1 starts at lane 64)
         const int lane0 = t == 0 ? 0 : 64;
-        const int row = t * 128 + r - lane0;
         const int rows_t = t == 0 ? min(a.S, 128) : a.S - 128;
         const bool warp_rows = 32 * q + 31 >= lane0 && 32 * q < lane0 + rows_t;  // warp-uniform
         const bool valid = r >= lane0 && r < lane0 + rows_t;
-        if (!mbar_wait(smem_u32(&s_full), u & 1u, &abort_flag, err)) {
-          ok = false;
-          break;
-        }
+        if (ok) ok = mbar_wait(smem_u32(&s_full), u & 1u, &abort_flag, err);
         tc_fence_after();
         const bool tw = tr != nullptr && warp == 2 && lane == 0;
         if (tw) trace(tr, u, 5);
         float l = 0.0f;
         if (warp_rows) {
           float v[HW];
-#pragma unroll
-          for (int c = 0; c + 32 <= HW; c += 32) tmem_ld32(t_s + (uint32_t)c, reinterpret_cast<uint32_t*>(v + c));
-          if (HW % 32 == 8) tmem_ld8(t_s + (uint32_t)(HW - 8), reinterpret_cast<uint32_t*>(v + HW - 8));
-          tmem_ld_wait();
-          if (tw) trace(tr, u, 9);
-          // score * log2(e) + bias: 0 for a key, -1e30 for a masked key (the
-          // sum stays -1e30 in fp32), -inf past the set
           float mx = -INFINITY;
+          {  // (after a failed wait the scores are garbage and unused)
 #pragma unroll
-          for (int j = 0; j < HW; j += 4) {
-            const float4 b4 = *reinterpret_cast<const float4*>(kb + j);
-            v[j] = fmaf(v[j], kLog2e, b4.x);
-            v[j + 1] = fmaf(v[j + 1], kLog2e, b4.y);
-            v[j + 2] = fmaf(v[j + 2], kLog2e, b4.z);
-            v[j + 3] = fmaf(v[j + 3], kLog2e, b4.w);
-            mx = fmaxf(fmaxf(mx, fmaxf(v[j], v[j + 1])), fmaxf(v[j + 2], v[j + 3]));
+            for (int c = 0; c + 32 <= HW; c += 32) tmem_ld32(t_s + (uint32_t)c, reinterpret_cast<uint32_t*>(v + c));
+            if (HW % 32 == 8) tmem_ld8(t_s + (uint32_t)(HW - 8), reinterpret_cast<uint32_t*>(v + HW - 8));
+            tmem_ld_wait();
+            if (tw) trace(tr, u, 9);
+            // score * log2(e) + bias: 0 for a key, -1e30 for a masked key (the
+            // sum stays -1e30 in fp32), -inf past the set
+#pragma unroll
+            for (int j = 0; j < HW; j += 4) {
+              const float4 b4 = *reinterpret_cast<const float4*>(kb + j);
+              v[j] = fmaf(v[j], kLog2e, b4.x);
+              v[j + 1] = fmaf(v[j + 1], kLog2e, b4.y);
+              v[j + 2] = fmaf(v[j + 2], kLog2e, b4.z);
+              v[j + 3] = fmaf(v[j + 3], kLog2e, b4.w);
+              mx = fmaxf(fmaxf(mx, fmaxf(v[j], v[j + 1])), fmaxf(v[j + 2], v[j + 3]));
+            }
           }
           red_max[hf][r] = mx;
-          named_sync(pair_bar, 64);
-          mx = fmaxf(mx, red_max[hf ^ 1][r]);
-          if (tw) trace(tr, u, 10);
+          ok = barrier_and(pair_bar, 64, ok);
+          if (ok) {
+            mx = fmaxf(mx, red_max[hf ^ 1][r]);
+            if (tw) trace(tr, u, 10);
 #pragma unroll
-          for (int j = 0; j < HW; j += 8) {
-            uint32_t pk[4];
-            float ls = 0.0f;
+            for (int j = 0; j < HW; j += 8) {
+              uint32_t pk[4];
+              float ls = 0.0f;
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const float p0 = ex2(v[j + 2 * i] - mx), p1 = ex2(v[j + 2 * i + 1] - mx);
-              ls += p0 + p1;
-              pk[i] = pack_bf16(p0, p1);
+              for (int i = 0; i < 4; ++i) {
+                const float p0 = ex2(v[j + 2 * i] - mx), p1 = ex2(v[j + 2 * i + 1] - mx);
+                ls += p0 + p1;
+                pk[i] = pack_bf16(p0, p1);
+              }
+              l += ls;
+              if (valid) {
+                const int k = c0 + j;
+                const uint32_t addr = prow + (uint32_t)(k >> 6) * kPBlock + ((((uint32_t)(k & 63) >> 3) ^ sw) << 4);
+                asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(pk[0]), "r"(pk[1]),
+                             "r"(pk[2]), "r"(pk[3])
+                             : "memory");
+              }
             }
-            l += ls;
-            if (valid) {
-              const int k = c0 + j;
-              const uint32_t addr = prow + (uint32_t)(k >> 6) * kPBlock + ((((uint32_t)(k & 63) >> 3) ^ sw) << 4);
-              asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(pk[0]), "r"(pk[1]), "r"(pk[2]),
-                           "r"(pk[3])
-                           : "memory");
-            }
+            red_sum[hf][r] = l;
           }
-          red_sum[hf][r] = l;
+        } else {
+          ok = barrier_and(pair_bar, 64, ok);
         }
+        if (!ok) break;
         tc_fence_before();
         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&p_full));
         if (tw) trace(tr, u, 6);
-        if (!mbar_wait(smem_u32(&o_full), u & 1u, &abort_flag, err)) {
-          ok = false;
-          break;
-        }
+        ok = mbar_wait(smem_u32(&o_full), u & 1u, &abort_flag, err);
         tc_fence_after();
         if (tw) trace(tr, u, 7);
         if (warp_rows) {
           uint32_t o[32];
           tmem_ld32(t_o, o);
-          named_sync(pair_bar, 64);  // the other half's row sum is in red_sum
+          ok = barrier_and(pair_bar, 64, ok);  // and the other half's row sum is in red_sum
+          tmem_ld_wait();                      // nothing may be outstanding at an exit
+          if (!ok) break;
           const float inv = 1.0f / (l + red_sum[hf ^ 1][r]);
-          tmem_ld_wait();
           // normalised bf16 row (32 columns = 4 chunks of 16 bytes) into this
           // warp's own part of P (dead since the O MMAs completed) ...
 #pragma unroll
@@ -347,11 +358,13 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__
             }
           }
           __syncwarp();
+        } else {
+          ok = barrier_and(pair_bar, 64, ok);
+          if (!ok) break;
         }
         tc_fence_before();
         if (tw) trace(tr, u, 8);
       }
-      if (!ok) break;
     }
   }
 
