@@ -92,6 +92,9 @@ attn_tc_long_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
   __shared__ uint32_t blk_masked;  // bit j: key block j of the item holds a masked or padding key
   __shared__ uint32_t tmem_slot;
   __shared__ volatile int abort_flag;
+  // pipeline 0 has written its first P: pipeline 1 starts then, half a block
+  // behind, so that the two pipelines' exponentials do not coincide
+  __shared__ volatile int p0_started;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int my_items = a.items > (int)blockIdx.x ? (a.items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
@@ -111,6 +114,7 @@ attn_tc_long_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
     mbar_init(smem_u32(&kv_full), 32);
     mbar_init(smem_u32(&kv_empty), 2);
     abort_flag = 0;
+    p0_started = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   if (warp == 1) {
@@ -189,6 +193,10 @@ attn_tc_long_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsControl));
     const uint32_t G = (uint32_t)warp - 1u;
     if (lane == 0) {
+      if (G == 1) {  // bounded: on expiry pipeline 1 simply starts
+        const unsigned long long t0 = globaltimer_ns();
+        while (!p0_started && !abort_flag && globaltimer_ns() - t0 < kWaitLimitNs) __nanosleep(64);
+      }
       const uint32_t id_s = idesc(128, kKB, false), id_o = idesc(128, 64, true);
       const uint64_t dq = sw128_desc(sbase + G * kBlockBytes), dk0 = sw128_desc(sbase + a.k_off),
                      dv0 = sw128_desc(sbase + a.v_off);
@@ -391,6 +399,7 @@ attn_tc_long_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_consta
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_u32(&p_full[G]));
+          if (G == 0 && lane == 0 && np == 0) p0_started = 1;
           if (tw) trace(tr, G, nt, 8 * j + 4);
           ++np;
         }
