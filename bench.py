@@ -58,7 +58,11 @@ def log(*a):
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms in a thread."""
+    """SM clock, power and throttle reasons of this rank's GPU during the timed
+    region: NVML every ~10 ms in a thread (the device found by the UUID torch
+    reports, so a remapped CUDA_VISIBLE_DEVICES cannot pick another GPU), plus
+    one sample at start and one at stop; nvidia-smi -lms 200 when NVML is
+    unavailable."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -69,8 +73,42 @@ class ClockSampler:
         self.rows = []
         self.proc = None
         self.thread = None
+        self.nvml = None
+        self.handle = None
+        self.stop_flag = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(gpu_index).uuid)
+            self.handle = pynvml.nvmlDeviceGetHandleByUUID("GPU-" + uuid if not uuid.startswith("GPU-") else uuid)
+            self.nvml = pynvml
+        except Exception:
+            self.nvml = None
+
+    def _sample_nvml(self):
+        n = self.nvml
+        try:
+            sm = n.nvmlDeviceGetClockInfo(self.handle, n.NVML_CLOCK_SM)
+            mx = n.nvmlDeviceGetMaxClockInfo(self.handle, n.NVML_CLOCK_SM)
+            pw = n.nvmlDeviceGetPowerUsage(self.handle) / 1000.0
+            rs = n.nvmlDeviceGetCurrentClocksEventReasons(self.handle)
+        except Exception:
+            return
+        flag = lambda bit: "Active" if rs & bit else "Not Active"  # noqa: E731
+        self.rows.append([str(self.gpu), str(sm), str(mx), f"{pw:.2f}", hex(rs),
+                          flag(n.nvmlClocksEventReasonHwSlowdown), flag(n.nvmlClocksEventReasonHwThermalSlowdown),
+                          flag(n.nvmlClocksEventReasonSwThermalSlowdown), flag(n.nvmlClocksEventReasonSwPowerCap)])
+
+    def _loop_nvml(self):
+        while not self.stop_flag.wait(0.01):
+            self._sample_nvml()
 
     def start(self):
+        if self.nvml is not None:
+            self._sample_nvml()
+            self.thread = threading.Thread(target=self._loop_nvml, daemon=True)
+            self.thread.start()
+            return
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
@@ -88,6 +126,12 @@ class ClockSampler:
                 self.rows.append(parts)
 
     def stop(self):
+        if self.nvml is not None:
+            self.stop_flag.set()
+            if self.thread is not None:
+                self.thread.join(timeout=2)
+            self._sample_nvml()
+            return
         if self.proc is not None:
             self.proc.terminate()
             try:
