@@ -602,7 +602,15 @@ def run_micro(args):
                                     ngr.value, mgr.value, None, torch.cuda.current_stream().cuda_stream),
                   "cc2_attention")
 
+    # TurboQuant K/V hook on one layer's QKV rows: K prod 4 bits, V mse 4 bits, Hadamard
+    from cutechronos_b200 import turboquant as tqm
+    kq_p = tqm.TurboQuantParams.build(64, 4, mode="prod", seed=11, device=dev)
+    vq_p = tqm.TurboQuantParams.build(64, 4, mode="mse", seed=12, device=dev)
+    qkv_tq = rnd(M, 3 * d, scale=0.5)
+
     cases = {
+        "kv_quant prod4/mse4 M=34048": (
+            lambda: tqm.kv_quant(qkv_tq, M, 12, kq_p, vq_p, q_col=0, k_col=d, v_col=2 * d), 0, M * 2 * d * 2 * 2),
         "group attn 64x8 S=133 bf16": (group_attn, 0, Bg * Sg * d * 2 * 4),
         "preprocess B=16384 L=2048 bf16": (
             lambda: kk.fused_preprocess(ctxp, 16, 8192, True, dtype=torch.bfloat16), 0,

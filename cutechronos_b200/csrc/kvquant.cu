@@ -65,21 +65,52 @@ __device__ __forceinline__ void fwht(float& lo, float& hi, int lane) {
   hi = __fsub_rn(a, b);
 }
 
-// y = M-product of the vector v (lo, hi): y[e] = sum_d v[d] * A[d][e] with A
-// given transposed ([d][e]); the vector is broadcast through `scratch`.
-__device__ __forceinline__ void matvec(float& lo, float& hi, const float* AT, float* scratch, int lane) {
-  scratch[lane] = lo;
-  scratch[lane + 32] = hi;
-  __syncwarp();
-  float a = 0.0f, b = 0.0f;
-  for (int d = 0; d < 64; ++d) {
-    const float v = scratch[d];
-    a = fmaf(v, AT[d * 64 + lane], a);
-    b = fmaf(v, AT[d * 64 + lane + 32], b);
+// y = M-product of each of NV vectors (lo, hi): y[e] = sum_d v[d] * A[d][e]
+// with A given transposed ([d][e]); the vectors are broadcast through
+// `scratch` ([NV][64]) and every row of A read once serves all NV vectors.
+template <int NV>
+__device__ __forceinline__ void matvec(float (&lo)[NV], float (&hi)[NV], const float* AT, float (*scratch)[64],
+                                       int lane) {
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    scratch[i][lane] = lo[i];
+    scratch[i][lane + 32] = hi[i];
   }
   __syncwarp();
-  lo = a;
-  hi = b;
+  // lane owns output columns 2*lane and 2*lane+1 (one 8-byte table load per d);
+  // the inputs are read four d at a time; each column still sums d = 0..63 in order
+  float a[NV], b[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) a[i] = b[i] = 0.0f;
+  const float2* at2 = reinterpret_cast<const float2*>(AT) + lane;
+#pragma unroll 2
+  for (int d = 0; d < 64; d += 4) {
+    float2 t[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) t[j] = at2[(d + j) * 32];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float4 v = *reinterpret_cast<const float4*>(&scratch[i][d]);
+      a[i] = fmaf(v.x, t[0].x, a[i]);
+      b[i] = fmaf(v.x, t[0].y, b[i]);
+      a[i] = fmaf(v.y, t[1].x, a[i]);
+      b[i] = fmaf(v.y, t[1].y, b[i]);
+      a[i] = fmaf(v.z, t[2].x, a[i]);
+      b[i] = fmaf(v.z, t[2].y, b[i]);
+      a[i] = fmaf(v.w, t[3].x, a[i]);
+      b[i] = fmaf(v.w, t[3].y, b[i]);
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < NV; ++i) *reinterpret_cast<float2*>(&scratch[i][2 * lane]) = make_float2(a[i], b[i]);
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    lo[i] = scratch[i][lane];
+    hi[i] = scratch[i][lane + 32];
+  }
+  __syncwarp();
 }
 
 __device__ __forceinline__ float norm_storage(float v, int kind) {
@@ -97,65 +128,116 @@ __device__ __forceinline__ int bucket(const float* b, int nb, float y) {
   return lo;
 }
 
-// Quantise one 64-value vector in registers (lo, hi); returns the squared
-// error and max |error| contributions of this lane.
-__device__ void quantise(float& lo, float& hi, const cc2_kvq& p, const QTab& t, float* scratch, int lane,
-                         float& sse, float& mx) {
+// Quantise NV 64-value vectors in registers (lo, hi); returns the squared
+// error and max |error| contributions of this lane.  Every vector goes through
+// the same arithmetic as alone; NV only interleaves them.
+template <int NV>
+__device__ void quantise(float (&lo)[NV], float (&hi)[NV], const cc2_kvq& p, const QTab& t, float (*scratch)[64],
+                         int lane, float& sse, float& mx) {
   const int mse_bits = p.mode == 0 ? p.bits : max(p.bits - 1, 0);
-  const float x0 = lo, x1 = hi;
-  const float norm = sqrtf(warp_sum(x0 * x0 + x1 * x1));
-  const float safe = fmaxf(norm, 1e-12f);
-  const float u0 = norm > 0.0f ? x0 / safe : 0.0f, u1 = norm > 0.0f ? x1 / safe : 0.0f;
-  float m0 = 0.0f, m1 = 0.0f;  // unit-vector reconstruction from the centroids
+  float x0[NV], x1[NV], norm[NV], u0[NV], u1[NV], m0[NV], m1[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    x0[i] = lo[i];
+    x1[i] = hi[i];
+    norm[i] = sqrtf(warp_sum(x0[i] * x0[i] + x1[i] * x1[i]));
+    const float safe = fmaxf(norm[i], 1e-12f);
+    u0[i] = norm[i] > 0.0f ? x0[i] / safe : 0.0f;
+    u1[i] = norm[i] > 0.0f ? x1[i] / safe : 0.0f;
+    m0[i] = m1[i] = 0.0f;  // unit-vector reconstruction from the centroids
+  }
   if (mse_bits > 0) {
-    float y0, y1;
+    float y0[NV], y1[NV];
     if (p.rotation == 0) {
-      y0 = gather(u0, u1, t.perm[lane]) * t.signs[lane];
-      y1 = gather(u0, u1, t.perm[lane + 32]) * t.signs[lane + 32];
-      fwht(y0, y1, lane);
-      y0 *= 0.125f;
-      y1 *= 0.125f;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        y0[i] = gather(u0[i], u1[i], t.perm[lane]) * t.signs[lane];
+        y1[i] = gather(u0[i], u1[i], t.perm[lane + 32]) * t.signs[lane + 32];
+        fwht(y0[i], y1[i], lane);
+        y0[i] *= 0.125f;
+        y1[i] *= 0.125f;
+      }
     } else {
-      y0 = u0;
-      y1 = u1;
-      matvec(y0, y1, t.matT, scratch, lane);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        y0[i] = u0[i];
+        y1[i] = u1[i];
+      }
+      matvec<NV>(y0, y1, t.matT, scratch, lane);
     }
     const int nb = (1 << mse_bits) - 1;
-    float c0 = t.codebook[bucket(t.bounds, nb, y0)], c1 = t.codebook[bucket(t.bounds, nb, y1)];
+    float c0[NV], c1[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      c0[i] = t.codebook[bucket(t.bounds, nb, y0[i])];
+      c1[i] = t.codebook[bucket(t.bounds, nb, y1[i])];
+    }
     if (p.rotation == 0) {
-      fwht(c0, c1, lane);
-      c0 = (c0 * 0.125f) * t.signs[lane];
-      c1 = (c1 * 0.125f) * t.signs[lane + 32];
-      m0 = gather(c0, c1, t.inv_perm[lane]);
-      m1 = gather(c0, c1, t.inv_perm[lane + 32]);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        fwht(c0[i], c1[i], lane);
+        c0[i] = (c0[i] * 0.125f) * t.signs[lane];
+        c1[i] = (c1[i] * 0.125f) * t.signs[lane + 32];
+        m0[i] = gather(c0[i], c1[i], t.inv_perm[lane]);
+        m1[i] = gather(c0[i], c1[i], t.inv_perm[lane + 32]);
+      }
     } else {
-      m0 = c0;
-      m1 = c1;
-      matvec(m0, m1, t.mat, scratch, lane);  // inverse: x[d] = sum_e y[e] mat[e][d]
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        m0[i] = c0[i];
+        m1[i] = c1[i];
+      }
+      matvec<NV>(m0, m1, t.mat, scratch, lane);  // inverse: x[d] = sum_e y[e] mat[e][d]
     }
   }
-  float r0 = m0, r1 = m1;
+  float r0[NV], r1[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    r0[i] = m0[i];
+    r1[i] = m1[i];
+  }
   if (p.mode == 1) {
-    const float e0 = u0 - m0, e1 = u1 - m1;
-    const float rn = norm_storage(sqrtf(warp_sum(e0 * e0 + e1 * e1)), p.norm_dtype);
-    float s0 = 1.0f, s1 = 1.0f;
-    if (p.bits > 0) {
-      float q0 = e0, q1 = e1;
-      matvec(q0, q1, t.projT, scratch, lane);  // sr[e] = sum_d residual[d] proj[e][d]
-      s0 = q0 >= 0.0f ? 1.0f : -1.0f;
-      s1 = q1 >= 0.0f ? 1.0f : -1.0f;
+    float e0[NV], e1[NV], rn[NV], s0[NV], s1[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      e0[i] = u0[i] - m0[i];
+      e1[i] = u1[i] - m1[i];
+      rn[i] = norm_storage(sqrtf(warp_sum(e0[i] * e0[i] + e1[i] * e1[i])), p.norm_dtype);
+      s0[i] = s1[i] = 1.0f;
     }
-    matvec(s0, s1, t.proj, scratch, lane);  // direction[d] = sum_e sign[e] proj[e][d]
-    const float coeff = (float)(1.2533141373155003 / 64.0) * rn;  // sqrt(pi / 2) / dim
-    r0 = m0 + coeff * s0;
-    r1 = m1 + coeff * s1;
+    if (p.bits > 0) {
+      float q0[NV], q1[NV];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        q0[i] = e0[i];
+        q1[i] = e1[i];
+      }
+      matvec<NV>(q0, q1, t.projT, scratch, lane);  // sr[e] = sum_d residual[d] proj[e][d]
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        s0[i] = q0[i] >= 0.0f ? 1.0f : -1.0f;
+        s1[i] = q1[i] >= 0.0f ? 1.0f : -1.0f;
+      }
+    }
+    matvec<NV>(s0, s1, t.proj, scratch, lane);  // direction[d] = sum_e sign[e] proj[e][d]
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float coeff = (float)(1.2533141373155003 / 64.0) * rn[i];  // sqrt(pi / 2) / dim
+      r0[i] = m0[i] + coeff * s0[i];
+      r1[i] = m1[i] + coeff * s1[i];
+    }
   }
-  const float ns = norm_storage(norm, p.norm_dtype);
-  lo = r0 * ns;
-  hi = r1 * ns;
-  const float d0 = lo - x0, d1 = hi - x1;
-  sse = d0 * d0 + d1 * d1;
-  mx = fmaxf(fabsf(d0), fabsf(d1));
+  sse = 0.0f;
+  mx = 0.0f;
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float ns = norm_storage(norm[i], p.norm_dtype);
+    lo[i] = r0[i] * ns;
+    hi[i] = r1[i] * ns;
+    const float d0 = lo[i] - x0[i], d1 = hi[i] - x1[i];
+    sse += d0 * d0 + d1 * d1;
+    mx = fmaxf(mx, fmaxf(fabsf(d0), fabsf(d1)));
+  }
 }
 
 // floats of shared memory a quantiser's dense tables take (matrix and its
@@ -211,7 +293,8 @@ __device__ void load_tab(QTab& t, const cc2_kvq& p, float* dense, int tid, int n
   }
 }
 
-template <typename T>
+// NV: vectors per warp (consecutive heads of one token row)
+template <typename T, int NV>
 __global__ void __launch_bounds__(kWarps * 32)
 kv_quant_kernel(T* __restrict__ qkv, int ld, int rows, int q_col, int k_col, int v_col, int heads, cc2_kvq kp,
                 cc2_kvq vp, int has_k, int has_v, const float2* __restrict__ rope, int rope_period,
@@ -220,49 +303,71 @@ kv_quant_kernel(T* __restrict__ qkv, int ld, int rows, int q_col, int k_col, int
   pdl_wait();
   extern __shared__ __align__(16) float dyn[];
   __shared__ QTab tab[2];
-  __shared__ float scratch[kWarps][64];
+  __shared__ __align__(16) float scratch[kWarps][NV][64];
   __shared__ float part[kWarps][4];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (has_k) load_tab(tab[0], kp, dyn, tid, blockDim.x);
   if (has_v) load_tab(tab[1], vp, dyn + (has_k ? dense_floats(kp) : 0), tid, blockDim.x);
   __syncthreads();
   float ksse = 0.0f, kmx = 0.0f, vsse = 0.0f, vmx = 0.0f;
-  const long long total = (long long)rows * heads;
+  const int groups = heads / NV;
+  const long long total = (long long)rows * groups;
   for (long long v = (long long)blockIdx.x * kWarps + warp; v < total; v += (long long)gridDim.x * kWarps) {
-    const int row = (int)(v / heads), h = (int)(v % heads);
-    T* base = qkv + (size_t)row * ld + h * 64 + lane;
-    T* kq = base + k_col;
-    float k0 = Elem<T>::to_f(kq[0]), k1 = Elem<T>::to_f(kq[32]);
+    const int row = (int)(v / groups), h0 = (int)(v % groups) * NV;
+    T* base = qkv + (size_t)row * ld + h0 * 64 + lane;
+    float k0[NV], k1[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      T* kq = base + k_col + i * 64;
+      k0[i] = Elem<T>::to_f(kq[0]);
+      k1[i] = Elem<T>::to_f(kq[32]);
+    }
     if (rope != nullptr) {  // rotate-half RoPE at position row % rope_period
       const float2 cs = rope[(size_t)(row % rope_period) * 32 + lane];
-      T* qq = base + q_col;
-      const float q0 = Elem<T>::to_f(qq[0]), q1 = Elem<T>::to_f(qq[32]);
-      qq[0] = Elem<T>::from_f(q0 * cs.x - q1 * cs.y);
-      qq[32] = Elem<T>::from_f(q1 * cs.x + q0 * cs.y);
-      const float r0 = k0 * cs.x - k1 * cs.y, r1 = k1 * cs.x + k0 * cs.y;
-      // the quantiser sees K as the attention would (rounded to the storage type)
-      k0 = Elem<T>::to_f(Elem<T>::from_f(r0));
-      k1 = Elem<T>::to_f(Elem<T>::from_f(r1));
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        T* qq = base + q_col + i * 64;
+        const float q0 = Elem<T>::to_f(qq[0]), q1 = Elem<T>::to_f(qq[32]);
+        qq[0] = Elem<T>::from_f(q0 * cs.x - q1 * cs.y);
+        qq[32] = Elem<T>::from_f(q1 * cs.x + q0 * cs.y);
+        const float r0 = k0[i] * cs.x - k1[i] * cs.y, r1 = k1[i] * cs.x + k0[i] * cs.y;
+        // the quantiser sees K as the attention would (rounded to the storage type)
+        k0[i] = Elem<T>::to_f(Elem<T>::from_f(r0));
+        k1[i] = Elem<T>::to_f(Elem<T>::from_f(r1));
+      }
     }
     if (has_k) {
       float s, m;
-      quantise(k0, k1, kp, tab[0], scratch[warp], lane, s, m);
+      quantise<NV>(k0, k1, kp, tab[0], scratch[warp], lane, s, m);
       ksse += s;
       kmx = fmaxf(kmx, m);
     }
     if (has_k || rope != nullptr) {
-      kq[0] = Elem<T>::from_f(k0);
-      kq[32] = Elem<T>::from_f(k1);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        T* kq = base + k_col + i * 64;
+        kq[0] = Elem<T>::from_f(k0[i]);
+        kq[32] = Elem<T>::from_f(k1[i]);
+      }
     }
     if (has_v) {
-      T* vq = base + v_col;
-      float v0 = Elem<T>::to_f(vq[0]), v1 = Elem<T>::to_f(vq[32]);
+      float v0[NV], v1[NV];
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        T* vq = base + v_col + i * 64;
+        v0[i] = Elem<T>::to_f(vq[0]);
+        v1[i] = Elem<T>::to_f(vq[32]);
+      }
       float s, m;
-      quantise(v0, v1, vp, tab[1], scratch[warp], lane, s, m);
+      quantise<NV>(v0, v1, vp, tab[1], scratch[warp], lane, s, m);
       vsse += s;
       vmx = fmaxf(vmx, m);
-      vq[0] = Elem<T>::from_f(v0);
-      vq[32] = Elem<T>::from_f(v1);
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        T* vq = base + v_col + i * 64;
+        vq[0] = Elem<T>::from_f(v0[i]);
+        vq[32] = Elem<T>::from_f(v1[i]);
+      }
     }
   }
   if (stats == nullptr) return;
@@ -328,22 +433,27 @@ int launch_kv_quant(int dtype, void* qkv, int ld, int rows, int q_col, int k_col
   CC2_CUDA(cudaGetDevice(&dev));
   if (dev >= 64 || !((attr_done >> dev) & 1ull)) {
     const int most = 8 * 4096 * (int)sizeof(float);  // both quantisers dense and prod
-    CC2_CUDA(cudaFuncSetAttribute(kv_quant_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
-    CC2_CUDA(cudaFuncSetAttribute(kv_quant_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
+    CC2_CUDA(cudaFuncSetAttribute(kv_quant_kernel<__nv_bfloat16, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
+    CC2_CUDA(cudaFuncSetAttribute(kv_quant_kernel<__nv_bfloat16, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
+    CC2_CUDA(cudaFuncSetAttribute(kv_quant_kernel<float, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
+    CC2_CUDA(cudaFuncSetAttribute(kv_quant_kernel<float, 4>, cudaFuncAttributeMaxDynamicSharedMemorySize, most));
     if (dev < 64) attr_done |= 1ull << dev;
   }
-  const long long vecs = (long long)rows * heads;
-  const int grid = (int)std::min<long long>((vecs + kWarps - 1) / kWarps, 4LL * num_sms());
+  const int nv = heads % 4 == 0 ? 4 : 1;  // four heads of a row per warp when the head count allows
+  const long long units = (long long)rows * (heads / nv);
+  const int grid = (int)std::min<long long>((units + kWarps - 1) / kWarps, 4LL * num_sms());
   const float2* cs = (const float2*)rope_cs;
-  if (dtype == CC2_BF16)
-    CC2_CUDA(launch_k(kv_quant_kernel<__nv_bfloat16>, grid, kWarps * 32, smem, st, (__nv_bfloat16*)qkv, ld, rows, q_col, k_col,
-                                                                   v_col, heads, kp, vp, key != nullptr,
-                                                                   value != nullptr, cs, rope_period, stats));
-  else if (dtype == CC2_F32)
-    CC2_CUDA(launch_k(kv_quant_kernel<float>, grid, kWarps * 32, smem, st, (float*)qkv, ld, rows, q_col, k_col, v_col, heads, kp, vp,
-                                                            key != nullptr, value != nullptr, cs, rope_period, stats));
-  else
+#define CC2_KVQ(TT, NV_)                                                                                     \
+  CC2_CUDA(launch_k(kv_quant_kernel<TT, NV_>, grid, kWarps * 32, smem, st, (TT*)qkv, ld, rows, q_col, k_col,  \
+                    v_col, heads, kp, vp, key != nullptr, value != nullptr, cs, rope_period, stats))
+  if (dtype == CC2_BF16) {
+    if (nv == 4) CC2_KVQ(__nv_bfloat16, 4); else CC2_KVQ(__nv_bfloat16, 1);
+  } else if (dtype == CC2_F32) {
+    if (nv == 4) CC2_KVQ(float, 4); else CC2_KVQ(float, 1);
+  } else {
     CC2_REQUIRE(false, "kv_quant: unsupported dtype %d", dtype);
+  }
+#undef CC2_KVQ
   CC2_CHECK_LAUNCH();
   return CC2_OK;
 }

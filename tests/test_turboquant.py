@@ -109,11 +109,12 @@ def _close_fraction(out, ref, scale):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("heads", [12, 3])  # 4 heads per warp / one vector per warp
 @pytest.mark.parametrize("ci", range(len(CASES)))
-def test_kernel_matches_oracle(gold, ci):
+def test_kernel_matches_oracle(gold, ci, heads):
     case = CASES[ci]
     g = torch.Generator().manual_seed(ci)
-    rows, heads = 40, 12
+    rows = 40
     qkv = (torch.randn(rows, 3 * heads * 64, generator=g) * 1.5).to(torch.bfloat16)
     qkv[3, heads * 64: heads * 64 + 64] = 0  # a zero K vector
     kp = _params(case, "cuda")
