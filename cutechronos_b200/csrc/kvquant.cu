@@ -295,7 +295,7 @@ __device__ void load_tab(QTab& t, const cc2_kvq& p, float* dense, int tid, int n
 
 // NV: vectors per warp (consecutive heads of one token row)
 template <typename T, int NV>
-__global__ void __launch_bounds__(kWarps * 32)
+__global__ void __launch_bounds__(kWarps * 32, 4)  // 4 CTAs (32 warps) per SM: the kernel is latency-bound
 kv_quant_kernel(T* __restrict__ qkv, int ld, int rows, int q_col, int k_col, int v_col, int heads, cc2_kvq kp,
                 cc2_kvq vp, int has_k, int has_v, const float2* __restrict__ rope, int rope_period,
                 float* __restrict__ stats) {
