@@ -12,7 +12,7 @@ from pathlib import Path
 LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libcc2_b200.so"
 
 CC2_F32, CC2_BF16 = 0, 1
-EPI_ROWSCALE, EPI_BIAS, EPI_RELU, EPI_RESID, EPI_SSQ, EPI_SPECIAL, EPI_ROPE = 1, 2, 4, 8, 16, 32, 64
+EPI_ROWSCALE, EPI_BIAS, EPI_RELU, EPI_RESID, EPI_SSQ, EPI_SPECIAL, EPI_ROPE, EPI_LO = 1, 2, 4, 8, 16, 32, 64, 128
 
 EXPORTED = (
     "cc2_last_error", "cc2_version", "cc2_device_status", "cc2_model_pack_bytes", "cc2_model_create",
@@ -21,9 +21,11 @@ EXPORTED = (
     "cc2_profile_begin", "cc2_profile_read", "cc2_set_gemm_variant", "cc2_forward_noalloc",
     "cc2_stack_series", "cc2_select_quantiles", "cc2_set_attention_variant",
     "cc2_set_attention_trace", "cc2_set_gemm_trace", "cc2_kv_quant", "cc2_model_set_kv_quant",
-    "cc2_set_launch_overlap",
+    "cc2_set_launch_overlap", "cc2_test_starve_gemm",
 )
-KIND_NAMES = {1: "preprocess", 2: "gemm_tc", 3: "attn_time", 4: "attn_group", 5: "rmsnorm", 6: "output_transform"}
+KIND_NAMES = {1: "preprocess", 2: "gemm_tc", 3: "attn_time", 4: "attn_group", 5: "rmsnorm", 6: "output_transform",
+              7: "gemm_qkv", 8: "gemm_o", 9: "gemm_group", 10: "gemm_ffn_up", 11: "gemm_ffn_down", 12: "gemm_io"}
+GEMM_KINDS = (2, 7, 8, 9, 10, 11, 12)
 
 
 class Config(C.Structure):
@@ -60,6 +62,7 @@ class Epilogue(C.Structure):
         ("bias", _VP), ("resid", _VP), ("ld_resid", C.c_int), ("ssq_out", _VP), ("ssq_ld", C.c_int),
         ("special", _VP), ("special_period", C.c_int), ("special_offset", C.c_int),
         ("rope_cs", _VP), ("rope_period", C.c_int), ("rope_cols", C.c_int),
+        ("lo_out", _VP), ("resid_lo", _VP), ("ld_lo", C.c_int),
     ]
 
 
@@ -104,6 +107,7 @@ def load(path: Path | str | None = None) -> C.CDLL:
     lib.cc2_kv_quant.argtypes = [i, v, i, i, i, i, i, i, v, v, v, i, v, v]
     lib.cc2_model_set_kv_quant.argtypes = [v, i, v, v, v]
     lib.cc2_set_launch_overlap.argtypes = [i]
+    lib.cc2_test_starve_gemm.argtypes = [i]
     lib.cc2_forward_noalloc.argtypes = [v, v, v, i, i, i, v, v, v, v, v]
     lib.cc2_profile_read.argtypes = [v, v, v, v, i, C.POINTER(i)]
     lib.cc2_stack_series.argtypes = [v, v, i, i, v, v]

@@ -531,6 +531,12 @@ void predict(Session& s, const float* context, int context_length, int H, float*
              "cudaMemcpyAsync(D2H)");
   cuda_check(cudaStreamSynchronize(s.stream), "cudaStreamSynchronize");
   const auto t1 = std::chrono::steady_clock::now();
+  // a kernel whose bounded wait ran out returns early with incomplete outputs
+  const int dev_status = cc2_device_status(1);
+  if (dev_status < 0) cc2_check(dev_status, "cc2_device_status");
+  if (dev_status != 0)
+    throw BridgeError(fmt("a kernel of the forward gave up waiting (device status %d); no forecast returned",
+                          dev_status));
 
   // the 0.5 quantile: the trained level, else linear between its neighbours (pipeline.py:24-58)
   const std::vector<float>& tq = s.quantiles;

@@ -85,6 +85,8 @@ extern int g_attn_variant;
 int set_attn_trace(void* buf);
 int set_attn_long_trace(void* buf);
 int set_gemm_trace(void* buf);
+int set_gemm_starve(int on);
+size_t gemm_f32_splitk_floats();
 int launch_kv_quant(int dtype, void* qkv, int ld, int rows, int q_col, int k_col, int v_col, int heads,
                     const cc2_kvq* key, const cc2_kvq* value, const float* rope_cs, int rope_period, float* stats,
                     cudaStream_t st);
@@ -319,6 +321,7 @@ size_t plan_pack(const cc2_config& c, int dtype, cc2_model* m, char* base) {
 
 struct Workspace {
   char* E; char* X; char* QKV; char* ATT; float* ssq; uint8_t* tok; float* loc; float* scale;
+  char* XLO; char* ALO;  // bf16: low halves of the residual stream X and of its alternate buffer ATT
   int32_t* members; int32_t* offsets; char* O; char* PRED;
   float* splitk; size_t splitk_floats;  // fp32 mode: K-slice partial sums of the small-M GEMMs
 };
@@ -338,8 +341,10 @@ size_t plan_ws(const cc2_model& m, int B, int L, int N, Workspace* w, char* base
   size_t oSSQ = p.take(4 * M * groups * 2), oTOK = p.take(M);
   size_t oLOC = p.take(4 * B), oSC = p.take(4 * B), oMEM = p.take(4 * B), oOFF = p.take(4 * (B + 1));
   size_t oO = p.take(e * (size_t)B * N * m.kout), oPRED = p.take(e * (size_t)B * N * m.qps);
-  const size_t splitk_floats = m.dtype == CC2_F32 ? ((size_t)8 << 20) : 0;
+  const size_t splitk_floats = m.dtype == CC2_F32 ? gemm_f32_splitk_floats() : 0;
   size_t oSPLIT = p.take(4 * splitk_floats);
+  const size_t lo_bytes = m.dtype == CC2_BF16 ? e * align_up(M, 32) * d : 0;  // 32-row interleaved
+  size_t oXLO = p.take(lo_bytes), oALO = p.take(lo_bytes);
   if (w && base) {
     w->E = base + oE; w->X = base + oX; w->QKV = base + oQKV; w->ATT = base + oATT;
     w->ssq = (float*)(base + oSSQ); w->tok = (uint8_t*)(base + oTOK);
@@ -347,17 +352,20 @@ size_t plan_ws(const cc2_model& m, int B, int L, int N, Workspace* w, char* base
     w->members = (int32_t*)(base + oMEM); w->offsets = (int32_t*)(base + oOFF);
     w->O = base + oO; w->PRED = base + oPRED;
     w->splitk = (float*)(base + oSPLIT); w->splitk_floats = splitk_floats;
+    w->XLO = lo_bytes ? base + oXLO : nullptr; w->ALO = lo_bytes ? base + oALO : nullptr;
   }
   return p.off;
 }
 
 // fp32 split-K scratch of the forward being issued on this thread (null outside a forward)
+thread_local int t_gemm_kind = CC2_K_GEMM;  // profiler kind of the next gemm() on this thread
 thread_local float* t_splitk = nullptr;
 thread_local size_t t_splitk_floats = 0;
 
 int gemm(int dtype, const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,
          const cc2_epilogue* e, cudaStream_t st) {
-  ProfScope ps_(CC2_K_GEMM, 2.0 * M * N * K, 0.0, st);
+  ProfScope ps_(t_gemm_kind, 2.0 * M * N * K, 0.0, st);
+  t_gemm_kind = CC2_K_GEMM;
   if (dtype == CC2_BF16) return launch_gemm_tc(A, lda, W, ldw, out, ldo, M, N, K, e, st);
   return launch_gemm_f32(A, lda, W, ldw, out, ldo, M, N, K, e, st, t_splitk, t_splitk_floats);
 }
@@ -566,6 +574,10 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
   const int M = B * S;
   const int KE = std::max(m->kin_pad, dff);
   const float eps = c.layer_norm_epsilon;
+  // bf16: the residual stream is kept as bf16 high halves (what the GEMMs
+  // read) plus bf16 low halves, so the twelve layers' residual additions do
+  // not each round it to 8 significant bits
+  const bool lo = dt == CC2_BF16;
 
   // group structure
   int num_groups = B, max_group = 1;
@@ -598,6 +610,7 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
   {
     cc2_epilogue e1 = epi_m(CC2_EPI_BIAS | CC2_EPI_RELU, M);
     e1.bias = m->b1_in;
+    t_gemm_kind = CC2_K_GEMM_IO;
     CC2_TRY(gemm(dt, w.E + e * dff, m->kin_pad, m->w1_in, m->in_dim, w.E, m->kin_pad, M, dff, m->in_dim, &e1, st));
     cc2_epilogue e2 = epi_m(CC2_EPI_BIAS | CC2_EPI_SSQ | (reg ? CC2_EPI_SPECIAL : 0), M);
     e2.bias = m->b23_in;
@@ -605,11 +618,20 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
     e2.special = m->reg;
     e2.special_period = S;
     e2.special_offset = P;
+    if (lo) { e2.flags |= CC2_EPI_LO; e2.lo_out = w.XLO; e2.ld_lo = d; }
+    t_gemm_kind = CC2_K_GEMM_IO;
     CC2_TRY(gemm(dt, w.E, m->kin_pad, m->w23_in, m->kin_pad, w.X, d, M, d, m->kin_pad, &e2, st));
   }
   // residual stream X and scratch Y swap roles after a one-GEMM group block
+  // (with their low halves XL / YL in bf16 mode)
   char* X = w.X;
   char* Y = w.ATT;
+  char* XL = w.XLO;
+  char* YL = w.ALO;
+  auto with_lo = [&](cc2_epilogue& ep, char* resid_lo, char* out_lo) {
+    if (!lo) return;
+    ep.flags |= CC2_EPI_LO; ep.resid_lo = resid_lo; ep.lo_out = out_lo; ep.ld_lo = d;
+  };
   for (int l = 0; l < c.num_layers; ++l) {
     const cc2_layer_pack& Lw = m->layers[l];
     // time attention
@@ -619,6 +641,7 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
     cc2_epilogue a = epi_m(CC2_EPI_ROWSCALE | (rope_in_gemm ? CC2_EPI_ROPE : 0), M);
     a.ssq_in = ssq(3 * l); a.norm_dim = d; a.eps = eps;
     a.rope_cs = m->rope_bf; a.rope_period = S; a.rope_cols = 2 * d;
+    t_gemm_kind = CC2_K_GEMM_QKV;
     CC2_TRY(gemm(dt, X, d, Lw.wqkv_t, d, w.QKV, 3 * d, M, 3 * d, d, &a, st));
     // TurboQuant K/V hook: K and V replaced by their quantised reconstructions
     // after RoPE (applied here first in fp32, where the attention would)
@@ -636,6 +659,8 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
     }
     cc2_epilogue o = epi_m(CC2_EPI_RESID | CC2_EPI_SSQ, M);
     o.resid = X; o.ld_resid = d; o.ssq_out = ssq(3 * l + 1);
+    with_lo(o, XL, XL);
+    t_gemm_kind = CC2_K_GEMM_O;
     CC2_TRY(gemm(dt, Y, d, Lw.wo_t, d, X, d, M, d, d, &o, st));
     // group attention
     cc2_epilogue g = epi_m(CC2_EPI_ROWSCALE, M);
@@ -646,9 +671,13 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
       // writes the other residual buffer (A and the output must differ).
       g.flags |= CC2_EPI_RESID | CC2_EPI_SSQ;
       g.resid = X; g.ld_resid = d; g.ssq_out = ssq(3 * l + 2);
+      with_lo(g, XL, YL);
+      t_gemm_kind = CC2_K_GEMM_GROUP;
       CC2_TRY(gemm(dt, X, d, Lw.wov_g, d, Y, d, M, d, d, &g, st));
       std::swap(X, Y);
+      std::swap(XL, YL);
     } else {
+      t_gemm_kind = CC2_K_GEMM_GROUP;
       CC2_TRY(gemm(dt, X, d, Lw.wqkv_g, d, w.QKV, 3 * d, M, 3 * d, d, &g, st));
       {
         ProfScope ps_(CC2_K_ATTN_GROUP, 4.0 * (double)S * gsq * d, 0.0, st);
@@ -657,14 +686,19 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
       }
       cc2_epilogue og = epi_m(CC2_EPI_RESID | CC2_EPI_SSQ, M);
       og.resid = X; og.ld_resid = d; og.ssq_out = ssq(3 * l + 2);
+      with_lo(og, XL, XL);
+      t_gemm_kind = CC2_K_GEMM_GROUP;
       CC2_TRY(gemm(dt, Y, d, Lw.wo_g, d, X, d, M, d, d, &og, st));
     }
     // feed-forward
     cc2_epilogue f1 = epi_m(CC2_EPI_ROWSCALE | CC2_EPI_RELU, M);
     f1.ssq_in = ssq(3 * l + 2); f1.norm_dim = d; f1.eps = eps;
+    t_gemm_kind = CC2_K_GEMM_FFN_UP;
     CC2_TRY(gemm(dt, X, d, Lw.wi, d, w.E, dff, M, dff, d, &f1, st));
     cc2_epilogue f2 = epi_m(CC2_EPI_RESID | CC2_EPI_SSQ, M);
     f2.resid = X; f2.ld_resid = d; f2.ssq_out = ssq(3 * l + 3);
+    with_lo(f2, XL, XL);
+    t_gemm_kind = CC2_K_GEMM_FFN_DOWN;
     CC2_TRY(gemm(dt, w.E, dff, Lw.wo_f, dff, X, d, M, d, dff, &f2, st));
   }
   (void)KE;
@@ -678,9 +712,11 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
   {
     cc2_epilogue e1 = epi_m(CC2_EPI_BIAS | CC2_EPI_RELU, M);
     e1.bias = m->b1_out;
+    t_gemm_kind = CC2_K_GEMM_IO;
     CC2_TRY(gemm(dt, w.O + e * dff, m->kout, m->w1_out, d, w.O, m->kout, BN_rows, dff, d, &e1, st));
     cc2_epilogue e2 = epi_m(CC2_EPI_BIAS, M);
     e2.bias = m->b23_out;
+    t_gemm_kind = CC2_K_GEMM_IO;
     CC2_TRY(gemm(dt, w.O, m->kout, m->w23_out, m->kout, w.PRED, m->qps, BN_rows, m->qps, m->kout, &e2, st));
   }
   {
@@ -791,6 +827,11 @@ int cc2_set_attention_variant(int variant) {
   const int old = g_attn_variant;
   g_attn_variant = (variant == 1 || variant == 2) ? variant : 0;
   return old;
+}
+
+int cc2_test_starve_gemm(int on) {
+  clear_error();
+  return set_gemm_starve(on);
 }
 
 int cc2_set_launch_overlap(int enabled) {

@@ -162,6 +162,13 @@ splitk_epilogue_kernel(const float* __restrict__ part, int slices, float* out, i
 
 }  // namespace
 
+size_t gemm_f32_splitk_floats() {
+  // A split GEMM has tiles < num_sms() and at most ceil(2 num_sms / tiles)
+  // slices of M x N <= tiles x TM x TN floats, so this bound never limits the
+  // slice count chosen below.
+  return (size_t)3 * num_sms() * TM * TN;
+}
+
 int launch_gemm_f32(const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,
                     const cc2_epilogue* e, cudaStream_t st, float* scratch, size_t scratch_floats) {
   CC2_REQUIRE(M > 0 && N > 0 && K > 0, "gemm: bad sizes M=%d N=%d K=%d", M, N, K);
@@ -175,6 +182,7 @@ int launch_gemm_f32(const void* A, int lda, const void* W, int ldw, void* out, i
   CC2_REQUIRE(!(ep.flags & (CC2_EPI_SSQ | CC2_EPI_ROWSCALE)) || ep.ssq_ld >= M, "gemm: ssq_ld must be >= M");
   CC2_REQUIRE(!(ep.flags & CC2_EPI_SPECIAL) || (ep.special && ep.special_period > 0), "gemm: special args");
   CC2_REQUIRE(!(ep.flags & CC2_EPI_ROPE), "gemm(f32): CC2_EPI_ROPE is a bf16 epilogue");
+  CC2_REQUIRE(!(ep.flags & CC2_EPI_LO), "gemm(f32): CC2_EPI_LO is a bf16 epilogue");
   const int tiles = ((N + TN - 1) / TN) * ((M + TM - 1) / TM);
   int slices = 1;
   if (scratch && tiles < num_sms() && K >= 8 * TK) {

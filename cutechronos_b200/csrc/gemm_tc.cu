@@ -37,6 +37,12 @@ namespace cc2 {
 // because the library is built without relocatable device code.
 __device__ int g_dev_error = 0;
 
+// Test hook (cc2_test_starve_gemm), one-shot: the first single-SM GEMM CTA
+// that finds it set clears it and skips the load of its first k-block, so the
+// MMA warp's bounded wait on that stage runs out.  Only loads that were issued are in flight when the
+// kernel leaves, and they land within microseconds of the 2 s limit.
+__device__ int g_gemm_starve = 0;
+
 int read_device_error(int clear, int* value) {
   CC2_CUDA(cudaMemcpyFromSymbol(value, g_dev_error, sizeof(int)));
   if (clear) {
@@ -81,6 +87,9 @@ struct Epi {
   const uint32_t* rope_cs;  // [pos][32] packed (cos, sin) bf16 pairs
   int rope_period;
   int rope_cols;
+  bf16* lo_out;          // LO: low halves of the result
+  const bf16* resid_lo;  // LO + RESID: low halves of the residual
+  int ld_lo;
 };
 
 // ---- PTX wrappers -------------------------------------------------------------
@@ -266,10 +275,38 @@ __device__ __forceinline__ void rope_group(uint32_t* r, const uint32_t (&cs)[32]
 // Applies the fused epilogue to one 64-column group of one row (values r[64]
 // from TMEM) and writes the bf16 result into the swizzled box.  Returns the
 // group's sum of squares of the stored values (columns < N).
+// Low halves (CC2_EPI_LO) live in a 32-row interleaved layout, so that the
+// 32 lanes of an epilogue warp (one row each) touch 512 contiguous bytes per
+// 16-byte access: element (row, col) at
+// ((row / 32 * ld / 8 + col / 8) * 32 + row % 32) * 8 + col % 8.
+__device__ __forceinline__ size_t lo_index(int row, int col, int ld) {
+  return (((size_t)(row >> 5) * (size_t)(ld >> 3) + (size_t)(col >> 3)) * 32 + (size_t)(row & 31)) * 8;
+}
+
+// LO (CC2_EPI_LO): the residual's low halves are added after its bf16 high
+// halves, and the result's low halves bf16(v - bf16(v)) go straight to global
+// memory (interleaved layout above: coalesced across the warp's rows).
+// Loads one 64-column group's residual low halves of this lane's row (zeros
+// outside the matrix).
+__device__ __forceinline__ void load_lo_group(uint4 (&rl)[8], const Epi& ep, int row, bool row_ok, int col0, int N) {
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    rl[c] = make_uint4(0u, 0u, 0u, 0u);
+    if (ep.resid_lo && row_ok && col0 + c * 8 < N)
+      asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                   : "=r"(rl[c].x), "=r"(rl[c].y), "=r"(rl[c].z), "=r"(rl[c].w)
+                   : "l"(ep.resid_lo + lo_index(row, col0 + c * 8, ep.ld_lo)));
+  }
+}
+
+// rl: the group's residual low halves (LO with RESID), loaded by the caller
+// ahead of time so that their latency overlaps the accumulator wait.
 __device__ __forceinline__ float epilogue_group(const Epi& ep, const int flags, const uint32_t* r, float rs, bool special, int col0,
-                                                int N, uint32_t box, int lane, bool resid) {
+                                                int N, uint32_t box, int lane, bool resid, int row, bool row_ok,
+                                                const uint4 (&rl)[8]) {
   const uint32_t rsw = (uint32_t)(lane & 7);
   float ssq = 0.0f;
+  const bool lo = (flags & CC2_EPI_LO) != 0;
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     const int col = col0 + c * 8;
@@ -298,6 +335,15 @@ __device__ __forceinline__ float epilogue_group(const Epi& ep, const int flags, 
         v[2 * e] += f.x;
         v[2 * e + 1] += f.y;
       }
+      if (lo) {
+        const __nv_bfloat162* ll = reinterpret_cast<const __nv_bfloat162*>(&rl[c]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __bfloat1622float2(ll[e]);
+          v[2 * e] += f.x;
+          v[2 * e + 1] += f.y;
+        }
+      }
     }
     if (special && col_ok) {
 #pragma unroll
@@ -306,7 +352,28 @@ __device__ __forceinline__ float epilogue_group(const Epi& ep, const int flags, 
     uint4 o;
     o.x = pack_bf16(v[0], v[1]); o.y = pack_bf16(v[2], v[3]);
     o.z = pack_bf16(v[4], v[5]); o.w = pack_bf16(v[6], v[7]);
-    if ((flags & CC2_EPI_SSQ) && col_ok) {
+    if (lo) {
+      const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&o);
+      float d[8];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(hh[e]);
+        d[2 * e] = v[2 * e] - f.x;
+        d[2 * e + 1] = v[2 * e + 1] - f.y;
+      }
+      if (ep.lo_out && row_ok && col_ok) {
+        uint4 lw;
+        lw.x = pack_bf16(d[0], d[1]); lw.y = pack_bf16(d[2], d[3]);
+        lw.z = pack_bf16(d[4], d[5]); lw.w = pack_bf16(d[6], d[7]);
+        asm volatile("st.global.L1::no_allocate.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(ep.lo_out + lo_index(row, col, ep.ld_lo)),
+                     "r"(lw.x), "r"(lw.y), "r"(lw.z), "r"(lw.w)
+                     : "memory");
+      }
+      if ((flags & CC2_EPI_SSQ) && col_ok) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ssq = fmaf(v[j], v[j], ssq);
+      }
+    } else if ((flags & CC2_EPI_SSQ) && col_ok) {
       const __nv_bfloat162* hh = reinterpret_cast<const __nv_bfloat162*>(&o);
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -394,6 +461,11 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         const int mt = tile / n_tiles, nt = tile % n_tiles;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) { ok = false; break; }
+          if (kb == 0 && tile == (int)blockIdx.x && *(volatile int*)&g_gemm_starve &&
+              atomicExch(&g_gemm_starve, 0)) {
+            if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
+            continue;  // test hook: this stage never fills
+          }
           const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
           mbar_arrive_expect_tx(full_bar(stage), C::STAGE_BYTES);
           tma_load_2d(sa, &tmA, full_bar(stage), kb * BK, mt * BM);
@@ -450,12 +522,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         mbar_arrive_expect_tx(rbar(q, b), kEpiBox);
         tma_load_2d(box0 + b * kEpiBox, &tmR, rbar(q, b), nt * BN, row0);
       }
+      const int row = row0 + lane;
+      const bool row_ok = row < M;
       const int acc = it & 1;
       const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
       if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag)) break;
       tc_fence_after();
-      const int row = row0 + lane;
-      const bool row_ok = row < M;
       const float rs = row_scale(ep, ep.flags, row, row_ok);
       const bool special = (ep.flags & CC2_EPI_SPECIAL) && row_ok && (row % ep.sp_period) == ep.sp_offset;
       const bool rope_tile = (ep.flags & CC2_EPI_ROPE) && nt * BN < ep.rope_cols;
@@ -488,7 +560,9 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           rope_group(r, cs, rs);
           rsg = 1.0f;
         }
-        const float ssq = epilogue_group(ep, ep.flags, r, rsg, special, col0, N, box, lane, resid);
+        uint4 rl[8];
+        if ((ep.flags & CC2_EPI_LO) && resid) load_lo_group(rl, ep, row, row_ok, col0, N);
+        const float ssq = epilogue_group(ep, ep.flags, r, rsg, special, col0, N, box, lane, resid, row, row_ok, rl);
         if ((ep.flags & CC2_EPI_SSQ) && row_ok) ep.ssq_out[(size_t)(col0 >> 6) * ep.ssq_ld + row] = ssq;
         fence_proxy_async_smem();
         __syncwarp();
@@ -767,6 +841,13 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
       if constexpr (ROPE) {
         if (rope_tile) load_rope_row(ep, row, row_ok, cs);
       }
+      constexpr bool LOR = F >= 0 && (F & CC2_EPI_LO) && (F & CC2_EPI_RESID);
+      uint4 rl[8];
+      if constexpr (LOR) {  // group 0's residual low halves, in flight during the accumulator wait
+        if (ng > 0) load_lo_group(rl, ep, row, row_ok, nt * BN + g0 * 64, N);
+      } else if (F < 0 && (flags & CC2_EPI_LO) && resid && ng > 0) {
+        load_lo_group(rl, ep, row, row_ok, nt * BN + g0 * 64, N);
+      }
       const int acc = it & 1;
       const uint32_t acc_phase = (uint32_t)(it >> 1) & 1u;
       if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag)) break;
@@ -794,7 +875,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
             rsg = 1.0f;
           }
         }
-        const float ssq = epilogue_group(ep, flags, r, rsg, special, col0, N, box, lane, resid);
+        const float ssq = epilogue_group(ep, flags, r, rsg, special, col0, N, box, lane, resid, row, row_ok, rl);
+        if ((flags & CC2_EPI_LO) && resid && j + 1 < ng) load_lo_group(rl, ep, row, row_ok, col0 + 64, N);  // next group's
         if ((flags & CC2_EPI_SSQ) && row_ok) ep.ssq_out[(size_t)(col0 >> 6) * ep.ssq_ld + row] = ssq;
         fence_proxy_async_smem();
         __syncwarp();
@@ -922,7 +1004,7 @@ static int launch_pair_t(const CUtensorMap& ma, const CUtensorMap& mb, const CUt
 static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mr,
                        int M, int N, int K, const Epi& ep, cudaStream_t st, int variant) {
   constexpr int RS = CC2_EPI_ROWSCALE, BI = CC2_EPI_BIAS, RL = CC2_EPI_RELU, RE = CC2_EPI_RESID,
-                SQ = CC2_EPI_SSQ, SP = CC2_EPI_SPECIAL, RP = CC2_EPI_ROPE;
+                SQ = CC2_EPI_SSQ, SP = CC2_EPI_SPECIAL, RP = CC2_EPI_ROPE, LO = CC2_EPI_LO;
   if (variant == 3)  // measurement only: mainloop with the epilogue reduced to releasing TMEM (no output)
     return launch_pair_t<0, 5, 2, true>(ma, mb, mc, mr, M, N, K, ep, st);
 #define CC2_PAIR(FL) \
@@ -932,8 +1014,11 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
     CC2_PAIR(RP)                 // RoPE alone (component use)
     CC2_PAIR(RS)                 // group QKV
     CC2_PAIR(RS | RL)            // FFN up
-    CC2_PAIR(RE | SQ)            // O-projections, FFN down
-    CC2_PAIR(RS | RE | SQ)       // one-series group block
+    CC2_PAIR(RE | SQ)            // O-projections, FFN down (component use)
+    CC2_PAIR(RE | SQ | LO)       // O-projections, FFN down (hi + lo residual stream)
+    CC2_PAIR(RS | RE | SQ)       // one-series group block (component use)
+    CC2_PAIR(RS | RE | SQ | LO)  // one-series group block (hi + lo residual stream)
+    CC2_PAIR(BI | SQ | SP | LO)  // input ResidualBlock output (+REG row, hi + lo)
     CC2_PAIR(BI | RL)            // ResidualBlock hidden
     CC2_PAIR(BI | SQ | SP)       // input ResidualBlock output (+REG row)
     CC2_PAIR(BI)                 // output ResidualBlock output
@@ -967,6 +1052,12 @@ int encode_bf16_map(CUtensorMap* map, const void* ptr, int cols, int rows, int l
 // Set through cc2_set_gemm_variant.
 int g_gemm_variant = 0;
 
+int set_gemm_starve(int on) {
+  const int v = on ? 1 : 0;
+  CC2_CUDA(cudaMemcpyToSymbol(g_gemm_starve, &v, sizeof(int)));
+  return CC2_OK;
+}
+
 int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,
                    const cc2_epilogue* e, cudaStream_t st) {
   using namespace tc;
@@ -991,7 +1082,14 @@ int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, in
     ep.rope_cs = e->rope_cs;
     ep.rope_period = e->rope_period;
     ep.rope_cols = e->rope_cols;
+    ep.lo_out = (bf16*)e->lo_out;
+    ep.resid_lo = (const bf16*)e->resid_lo;
+    ep.ld_lo = e->ld_lo;
   }
+  CC2_REQUIRE(!(ep.flags & CC2_EPI_LO) ||
+                  (ep.lo_out && ((uintptr_t)ep.lo_out & 15u) == 0 && ep.ld_lo % 8 == 0 && ep.ld_lo >= N &&
+                   (!(ep.flags & CC2_EPI_RESID) || (ep.resid_lo && ((uintptr_t)ep.resid_lo & 15u) == 0))),
+              "gemm: lo args (16-byte aligned lo_out and resid_lo, ld_lo >= N and a multiple of 8)");
   CC2_REQUIRE(!(ep.flags & CC2_EPI_ROPE) ||
                   (ep.rope_cs && ((uintptr_t)ep.rope_cs & 15u) == 0 && ep.rope_period > 0 && ep.rope_cols % 64 == 0),
               "gemm: rope args (16-byte aligned table, period > 0, cols multiple of 64)");

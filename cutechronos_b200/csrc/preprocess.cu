@@ -278,8 +278,13 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
         float z = __int_as_float(0x7fc00000);
         float mk = 0.0f;
         if (src >= 0) {
-          z = (v[c][i] - lo) * rsc;
-          if (use_arcsinh) z = asinh_fast(z);
+          if constexpr (sizeof(T) == 4) {  // fp32 model: the reference's division and accurate asinh
+            z = __fdiv_rn(v[c][i] - lo, sc);
+            if (use_arcsinh) z = asinhf(z);
+          } else {
+            z = (v[c][i] - lo) * rsc;
+            if (use_arcsinh) z = asinh_fast(z);
+          }
           mk = m ? nan_to_zero(m[src]) : (isnan(v[c][i]) ? 0.0f : 1.0f);
         }
         mt[i] = roundT<T>(mk);  // the mask in the model dtype (fractional masks pass through)
@@ -395,7 +400,12 @@ output_transform_vec_kernel(const T* __restrict__ preds, int ld, const float* __
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       float vv = f[i];
-      if (use_arcsinh) vv = sinh_fast(vv);
+      if (use_arcsinh) {
+        if constexpr (sizeof(T) == 4)
+          vv = sinhf(vv);  // fp32 model: the error is not hidden by a bf16 rounding
+        else
+          vv = sinh_fast(vv);
+      }
       f[i] = __fadd_rn(__fmul_rn(vv, sc), lo);
     }
     if constexpr (sizeof(T) == 2) {

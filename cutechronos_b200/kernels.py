@@ -107,17 +107,43 @@ def row_sumsq_parts(x: torch.Tensor) -> torch.Tensor:
     return xp.reshape(M, G, 64).pow(2).sum(-1).T.contiguous()
 
 
+def lo_numel(M: int, N: int) -> int:
+    """Elements of a low-halves buffer (CC2_EPI_LO) for an (M, N) result."""
+    return -(-M // 32) * 32 * N
+
+
+def rows_to_lo(t: torch.Tensor) -> torch.Tensor:
+    """(M, N) row-major -> the 32-row interleaved layout of CC2_EPI_LO buffers:
+    element (row, col) at ((row/32 * N/8 + col/8) * 32 + row%32) * 8 + col%8."""
+    M, N = t.shape
+    Mp = -(-M // 32) * 32
+    p = torch.zeros(Mp, N, dtype=t.dtype, device=t.device)
+    p[:M] = t
+    return p.view(Mp // 32, 32, N // 8, 8).permute(0, 2, 1, 3).contiguous().view(-1)
+
+
+def lo_to_rows(lo: torch.Tensor, M: int, N: int) -> torch.Tensor:
+    """Inverse of :func:`rows_to_lo`."""
+    Mp = -(-M // 32) * 32
+    return lo.view(Mp // 32, N // 8, 32, 8).permute(0, 2, 1, 3).reshape(Mp, N)[:M]
+
+
 def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None, *, relu: bool = False,
            residual: torch.Tensor | None = None, row_ssq: torch.Tensor | None = None, norm_dim: int = 0,
            eps: float = 1e-6, ssq_out: torch.Tensor | None = None, out: torch.Tensor | None = None,
-           rope_period: int = 0, rope_cols: int = 0) -> torch.Tensor:
+           rope_period: int = 0, rope_cols: int = 0, residual_lo: torch.Tensor | None = None,
+           lo_out: torch.Tensor | None = None) -> torch.Tensor:
     """out = epilogue(x @ weight^T): optional row scale
     rsqrt(row_ssq.sum(0) / norm_dim + eps) with ``row_ssq`` (G, M) partial sums
     per 64-column group, + bias (fp32), ReLU, + residual, and ``ssq_out``
     (G', M) <- partial sums of squares of the stored output.  ``rope_period``
     > 0 (bf16 only) rotates every 64-column head below ``rope_cols`` at
-    position row % rope_period with bf16 cos/sin, as the engine does for Q, K."""
-    _cuda(x, weight, bias, residual, row_ssq, ssq_out)
+    position row % rope_period with bf16 cos/sin, as the engine does for Q, K.
+    ``lo_out`` (bf16 only; ``lo_numel(M, N)`` elements in the interleaved layout
+    of :func:`rows_to_lo`) receives the low halves bf16(v - out) of the result
+    v, and ``residual_lo`` (same layout) the residual's low halves (residual +
+    residual_lo is the residual): the engine's hi + lo residual stream."""
+    _cuda(x, weight, bias, residual, row_ssq, ssq_out, residual_lo, lo_out)
     K = x.shape[-1]
     x2 = x.reshape(-1, K).contiguous()
     M, N = x2.shape[0], weight.shape[0]
@@ -154,6 +180,26 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = No
         tab = rope_table_bf16(rope_period, 64, 10000.0, x.device)
         keep.append(tab)
         e.rope_cs, e.rope_period, e.rope_cols = tab.data_ptr(), rope_period, rope_cols
+    if lo_out is not None:
+        n_lo = lo_numel(M, N)
+        if x.dtype != torch.bfloat16 or lo_out.dtype != torch.bfloat16 or lo_out.numel() != n_lo \
+                or not lo_out.is_contiguous() or N % 8:
+            raise ValueError("lo_out must be a contiguous bf16 buffer of lo_numel(M, N) elements "
+                             "(interleaved layout, see rows_to_lo) of a bf16 GEMM with N % 8 == 0")
+        flags |= nat.EPI_LO
+        e.lo_out, e.ld_lo = lo_out.data_ptr(), N
+        if residual_lo is not None:
+            if residual is None:
+                raise ValueError("residual_lo needs residual")
+            if residual_lo.dtype != torch.bfloat16 or residual_lo.numel() != n_lo or not residual_lo.is_contiguous():
+                raise ValueError("residual_lo must be a contiguous bf16 buffer of lo_numel(M, N) elements")
+            e.resid_lo = residual_lo.data_ptr()
+        elif residual is not None:
+            z = torch.zeros(n_lo, dtype=torch.bfloat16, device=x.device)
+            keep.append(z)
+            e.resid_lo = z.data_ptr()
+    elif residual_lo is not None:
+        raise ValueError("residual_lo needs lo_out")
     e.flags = flags
     nat.check(nat.load().cc2_gemm(_code(x.dtype), x2.data_ptr(), K, w.data_ptr(), K, out.data_ptr(), N, M, N, K,
                                   C.byref(e), _stream(x)), "cc2_gemm")

@@ -307,13 +307,34 @@ class CuteChronos2Model(nn.Module):
                 gid_host = g
         cfg = self.config
         if (self._cuda_graphs and gid_host is None and not torch.cuda.is_current_stream_capturing()):
-            return self._forward_graph(eng, dev, ctx, mask, B, L, N)
+            out = self._forward_graph(eng, dev, ctx, mask, B, L, N)
+            self._check_device(dev)
+            return out
         out = torch.empty(B, cfg.num_quantiles, N * cfg.output_patch_size, dtype=eng.dtype, device=dev)
         self._last_loc = torch.empty(B, dtype=torch.float32, device=dev)
         self._last_scale = torch.empty(B, dtype=torch.float32, device=dev)
         self._native_forward(eng, dev, ctx, mask, gid_host, B, L, N, max_group, out, self._last_loc,
                              self._last_scale)
+        self._check_device(dev)
         return out
+
+    def set_device_checks(self, enabled: bool = True) -> "CuteChronos2Model":
+        """After every forward, synchronise the device and raise if a kernel's
+        bounded wait ran out (its outputs are then incomplete although the launch
+        succeeded).  Off by default: the check costs one device synchronisation."""
+        self._device_checks = bool(enabled)
+        return self
+
+    def _check_device(self, dev) -> None:
+        if not getattr(self, "_device_checks", False) or torch.cuda.is_current_stream_capturing():
+            return
+        with torch.cuda.device(dev):
+            st = nat.load().cc2_device_status(1)
+        if st < 0:
+            nat.check(st, "cc2_device_status")
+        if st:
+            raise nat.NativeError(f"a kernel of the forward gave up waiting (device status {st}); "
+                                  "its outputs are incomplete")
 
     def _native_forward(self, eng, dev, ctx, mask, gid_host, B, L, N, max_group, out, loc, scale):
         cfg = self.config

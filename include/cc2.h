@@ -59,8 +59,13 @@ enum {
 CC2_API const char* cc2_last_error(void);
 /* Library version string. */
 CC2_API const char* cc2_version(void);
-/* Device-side error word written by bounded waits inside kernels (0 = none);
- * synchronises the current device.  clear != 0 resets it. */
+/* Device-side error word written by bounded waits inside kernels (0 = none,
+ * else CC2_DEV_* bits); synchronises the current device.  clear != 0 resets
+ * it.  A kernel whose wait ran out returns early and leaves its outputs
+ * incomplete while the launching call has already returned CC2_OK, so callers
+ * that need to know poll this after synchronising (the native bridge and
+ * CuteChronos2Model.set_device_checks(True) do). */
+enum { CC2_DEV_GEMM_TIMEOUT = 1, CC2_DEV_ATTN_TIMEOUT = 2 };
 CC2_API int cc2_device_status(int clear);
 
 /* ------------------------------------------------------------------------ */
@@ -145,7 +150,14 @@ CC2_API int cc2_forward(const cc2_model* m, const float* context, const float* c
  * stores the number of launches in *count and stops profiling. */
 enum {
   CC2_K_PREPROCESS = 1, CC2_K_GEMM = 2, CC2_K_ATTN_TIME = 3, CC2_K_ATTN_GROUP = 4,
-  CC2_K_RMSNORM = 5, CC2_K_OUTPUT = 6
+  CC2_K_RMSNORM = 5, CC2_K_OUTPUT = 6,
+  /* the forward's GEMMs by role (CC2_K_GEMM: any other GEMM) */
+  CC2_K_GEMM_QKV = 7,       /* time-attention Q/K/V (RMSNorm + RoPE)          */
+  CC2_K_GEMM_O = 8,         /* time-attention output projection + residual    */
+  CC2_K_GEMM_GROUP = 9,     /* group block: Wo.Wv fold (g = 1) or group QKV/O */
+  CC2_K_GEMM_FFN_UP = 10,   /* wi (RMSNorm + ReLU)                            */
+  CC2_K_GEMM_FFN_DOWN = 11, /* wo + residual                                  */
+  CC2_K_GEMM_IO = 12        /* input / output ResidualBlocks                  */
 };
 CC2_API int cc2_profile_begin(int capacity);
 CC2_API int cc2_profile_read(int* kinds, float* ms, double* flops, double* bytes, int capacity,
@@ -158,7 +170,8 @@ CC2_API int cc2_profile_read(int* kinds, float* ms, double* flops, double* bytes
  * device.  The scratch lives in one static device array of
  * CC2_NOALLOC_SCRATCH_BYTES (32 MiB) that every GPU loading this library
  * holds until the process exits; it fits about 2,300 token rows of the
- * Chronos-2-base model (e.g. 16 series of context 2048 with N = 4).  Larger
+ * bf16 Chronos-2-base model (e.g. 16 series of context 2048 with N = 4) and
+ * about 900 rows of the fp32 model (e.g. 6 series of context 2048).  Larger
  * requests fail with CC2_E_WORKSPACE and a message giving the bytes needed.
  * The first call on a device looks the array's device address up (once per
  * device, with that device current); make that first call before any stream
@@ -200,9 +213,20 @@ enum {
                             64g..64g+63 of out[row, col]^2 (partial sums per
                             64-column group: deterministic, no atomics)        */
   CC2_EPI_SPECIAL = 32,  /* rows with row % period == offset get special[]     */
-  CC2_EPI_ROPE = 64      /* bf16 only: rotate-half RoPE on every 64-column head
+  CC2_EPI_ROPE = 64,     /* bf16 only: rotate-half RoPE on every 64-column head
                             with col < rope_cols at position row % rope_period,
                             rope_cs[pos*32 + i] = (cos | sin << 16) as bf16 */
+  CC2_EPI_LO = 128       /* bf16 only: the result v (fp32) is stored as out =
+                            bf16(v) plus lo_out = bf16(v - out), so out +
+                            lo_out carries ~16 significant bits; with RESID
+                            the residual is resid + resid_lo; SSQ sums v^2.
+                            lo_out / resid_lo use a 32-row interleaved layout
+                            (coalesced for the epilogue's row-per-lane
+                            access): element (row, col) at
+                            ((row/32 * ld_lo/8 + col/8) * 32 + row%32) * 8 +
+                            col%8, ld_lo a multiple of 8, ceil(M/32)*32 rows
+                            allocated.  The engine keeps the encoder's
+                            residual stream this way */
 };
 
 typedef struct {
@@ -214,6 +238,7 @@ typedef struct {
   int ssq_ld;            /* row stride between 64-column groups of ssq_in / ssq_out */
   const float* special; int special_period; int special_offset;
   const uint32_t* rope_cs; int rope_period; int rope_cols;
+  void* lo_out; const void* resid_lo; int ld_lo;  /* CC2_EPI_LO */
 } cc2_epilogue;
 
 /* Tile variant of the bf16 GEMM: 0 (default) = 2-SM tcgen05 tiles of 256 x 256
@@ -246,6 +271,15 @@ CC2_API int cc2_set_attention_trace(void* device_buffer);
  * activations.  0 launches them strictly one after another.  Process-wide;
  * returns the previous value. */
 CC2_API int cc2_set_launch_overlap(int enabled);
+/* Test hook (no counterpart in the reference): on != 0 arms a one-shot
+ * fault-free failure: the next single-SM bf16 GEMM CTA (cc2_gemm with
+ * M <= 128) withholds the load of its first k-block (and disarms the hook),
+ * so its bounded mbarrier wait runs out after 2 s; the
+ * kernel then sets the device error word (cc2_device_status returns
+ * CC2_DEV_GEMM_TIMEOUT), leaves its loops, frees its TMEM and returns.
+ * Exists so that tests can exercise the failure path without a GPU fault;
+ * keep it off (0) otherwise.  Applies to the current device. */
+CC2_API int cc2_test_starve_gemm(int on);
 
 /* Event trace of the 2-SM GEMM: with a device buffer of 32 x 8 uint64
  * (zeroed by the caller), CTA 0 of every later launch writes, for its first

@@ -391,3 +391,37 @@ def test_group_attention(gids, S, dtype):
     d = (out - ref).abs()[live]
     assert d.max().item() <= tol * max(1.0, ref.abs().max().item())
     assert torch.isfinite(out).all()
+
+
+@pytest.mark.parametrize("M,N,Kd,rowscale", [(37, 768, 768, False), (1000, 768, 768, True), (34048, 768, 3072, False),
+                                             (300, 768, 3136, False)])
+def test_linear_hi_lo_residual_stream(M, N, Kd, rowscale):
+    """CC2_EPI_LO (bf16): out + lo_out carries the fp32 result
+    v = x @ w^T [* rowscale] + (resid + resid_lo) to ~16 significant bits, in
+    place as the engine updates its residual stream; the sums of squares are
+    those of v.  1-SM (M <= 128) and 2-SM tiles."""
+    g = torch.Generator().manual_seed(11 * M + Kd)
+    x = torch.randn(M, Kd, generator=g).to(torch.bfloat16)
+    w = (torch.randn(N, Kd, generator=g) / math.sqrt(Kd)).to(torch.bfloat16)
+    full = 4.0 * torch.randn(M, N, generator=g)
+    hi = full.to(torch.bfloat16)
+    lo = (full - hi.float()).to(torch.bfloat16)
+    kk = K()
+    kw = {}
+    ssq = None
+    if rowscale:
+        kw = dict(row_ssq=kk.row_sumsq_parts(x).to(DEV), norm_dim=Kd, eps=1e-6)
+        ssq = x.float().pow(2).sum(-1)
+    out, out_lo_buf = hi.to(DEV).clone(), kk.rows_to_lo(lo.to(DEV))
+    so = torch.full(((N + 63) // 64, M), float("nan"), device=DEV)
+    kk.linear(x.to(DEV), w.to(DEV), residual=out, residual_lo=out_lo_buf, lo_out=out_lo_buf, ssq_out=so, out=out,
+              **kw)
+    out_lo = kk.lo_to_rows(out_lo_buf, M, N)
+    ref = _gemm_ref(x, w, None, False, hi.double() + lo.double(), ssq, Kd if rowscale else 0, 1e-6)
+    v = out.cpu().double() + out_lo.cpu().double()
+    # fp32 accumulation order of the K-sum bounds the agreement, not the storage
+    assert (v - ref).abs().max().item() <= 2e-6 * Kd ** 0.5 * ref.abs().max().item()
+    assert (out.cpu().double() - ref).abs().max().item() <= 2 ** -8 * ref.abs().max().item()
+    assert (out_lo.cpu().float().abs() <= out.cpu().float().abs() * 2 ** -8 + 1e-30).all()
+    ref_parts = kk.row_sumsq_parts(ref.float())
+    assert torch.allclose(so.cpu(), ref_parts, rtol=1e-4, atol=1e-3)

@@ -1,11 +1,13 @@
 """Whole-forward parity on the GPU: CuteChronos2Model (native engine) against
 fixtures from the reference module and against the CPU oracle.
 
-Tolerances (the parity bar of this path): fp32 mode max-abs 1e-4 in the model's
-normalised output space (|y - ref| / scale_b, scale_b = the series' instance
-norm scale; for the reference's own test inputs the scale is ~0.1 and the
-bound holds in absolute terms as well); bf16 mode 2e-2 relative:
-max|y - ref| <= 2e-2 * max|ref|.
+Tolerances (the parity bar of this path): fp32 mode max-abs 1e-4 in absolute
+terms on the Chronos-2-base configs[0] forward and on the reference's own test
+input; on the small edge-case fixtures (inputs up to 1e6 in magnitude) the same
+1e-4 in the model's normalised output space (|y - ref| / scale_b, scale_b = the
+series' instance-norm scale).  bf16 mode 2e-2 relative per series:
+max over series b of max|y_b - ref_b| / max|ref_b| <= 2e-2.
+Each test prints its measured maximum (run with -s to see them).
 """
 
 import pytest
@@ -13,7 +15,7 @@ import torch
 
 from conftest import case_inputs, oracle_config, small_config
 from cutechronos_b200.model import CuteChronos2Config, CuteChronos2Model
-from cutechronos_b200.workloads import config1, config2, config3, seeded_init_, seeded_state_dict
+from cutechronos_b200.workloads import config1, config2, config3, config4, seeded_init_, seeded_state_dict
 from oracle import chronos2_oracle as orc
 
 pytestmark = pytest.mark.gpu
@@ -30,7 +32,15 @@ def _norm_err(y, ref, scale):
 
 
 def _rel_err(y, ref):
-    return (y.float() - ref.float()).abs().max().item() / ref.float().abs().max().item()
+    """Per-series relative error, worst series: max_b max|y_b - ref_b| / max|ref_b|."""
+    d = (y.float() - ref.float()).abs().flatten(1).amax(1)
+    r = ref.float().abs().flatten(1).amax(1).clamp_min(1e-30)
+    return (d / r).max().item()
+
+
+def _report(name, value):
+    print(f"PARITY {name} {value:.3e}")
+    return value
 
 
 @pytest.fixture(scope="module")
@@ -51,7 +61,7 @@ def test_small_f32_vs_reference(golden_small, small_f32, case):
     ref = torch.from_numpy(c["out_f32"])
     assert y.shape == ref.shape and y.dtype == torch.float32
     scale = torch.from_numpy(c["scale"]).view(-1)
-    assert _norm_err(y, ref, scale) <= 1e-4
+    assert _report(f"small_{case}_f32_norm", _norm_err(y, ref, scale)) <= 1e-4
 
 
 @pytest.mark.parametrize("case", CASES)
@@ -60,8 +70,8 @@ def test_small_bf16_vs_reference(golden_small, small_bf16, case):
     ctx, mask, N, gid = case_inputs(c)
     y = small_bf16(ctx.to(DEV), mask.to(DEV) if mask is not None else None, N, gid).cpu()
     assert y.dtype == torch.bfloat16
-    assert _rel_err(y, torch.from_numpy(c["out_f32"])) <= 2e-2
-    assert _rel_err(y, torch.from_numpy(c["out_bf16"])) <= 2e-2
+    assert _report(f"small_{case}_bf16_rel_vs_f32", _rel_err(y, torch.from_numpy(c["out_f32"]))) <= 2e-2
+    assert _report(f"small_{case}_bf16_rel_vs_bf16", _rel_err(y, torch.from_numpy(c["out_bf16"]))) <= 2e-2
 
 
 @pytest.fixture(scope="module")
@@ -84,8 +94,7 @@ def test_base_cfg0_f32(golden_base, base_f32):
     ctx = torch.from_numpy(golden_base["context"])
     y = base_f32(ctx.to(DEV), num_output_patches=int(golden_base["N"])).cpu()
     ref = torch.from_numpy(golden_base["out_f32"])
-    _, _, _, scale = orc.prepare_patched_context(orc.OracleConfig(), ctx, None, torch.float32)
-    assert _norm_err(y, ref, scale.view(-1)) <= 1e-4
+    assert _report("cfg0_base_f32_maxabs", (y - ref).abs().max().item()) <= 1e-4
 
 
 def test_base_cfg0_reference_style_input_f32(base_f32, base_weights):
@@ -94,13 +103,13 @@ def test_base_cfg0_reference_style_input_f32(base_f32, base_weights):
     ctx = torch.randn(2, 512, generator=g) * 0.1 + 100.0
     y = base_f32(ctx.to(DEV), num_output_patches=4).cpu()
     ref = orc.forward(orc.OracleConfig(), base_weights, ctx, None, 4)
-    assert (y - ref).abs().max().item() <= 1e-4
+    assert _report("reference_style_f32_maxabs", (y - ref).abs().max().item()) <= 1e-4
 
 
 def test_base_cfg0_bf16(golden_base, base_bf16):
     ctx = torch.from_numpy(golden_base["context"])
     y = base_bf16(ctx.to(DEV), num_output_patches=int(golden_base["N"])).cpu()
-    assert _rel_err(y, torch.from_numpy(golden_base["out_f32"])) <= 2e-2
+    assert _report("cfg0_base_bf16_rel", _rel_err(y, torch.from_numpy(golden_base["out_f32"]))) <= 2e-2
 
 
 def _subset_check(model, weights, ctx, gid, N, idx, dtype=torch.float32):
@@ -115,24 +124,35 @@ def _subset_check(model, weights, ctx, gid, N, idx, dtype=torch.float32):
 
 def test_cfg1_full_batch_subset_vs_oracle(base_bf16, base_weights):
     w = config1()
-    err = _subset_check(base_bf16, base_weights, w.context, None, w.num_output_patches, torch.tensor([0, 77, 255]))
-    assert err <= 2e-2
+    idx = torch.arange(0, 256, 8)  # 32 of the 256 series
+    err = _subset_check(base_bf16, base_weights, w.context, None, w.num_output_patches, idx)
+    assert _report("cfg1_bf16_rel_32series", err) <= 2e-2
 
 
 def test_cfg2_groups_subset_vs_oracle(base_bf16, base_weights):
     w = config2()
-    idx = torch.arange(8, 24)  # groups 1 and 2 (8 variates each)
+    idx = torch.cat([torch.arange(8 * g, 8 * g + 8) for g in (1, 2, 30, 63)])  # 4 whole groups
     err = _subset_check(base_bf16, base_weights, w.context, w.group_ids, w.num_output_patches, idx)
-    assert err <= 2e-2
+    assert _report("cfg2_bf16_rel_4groups", err) <= 2e-2
 
 
 def test_cfg3_left_padded_subset_vs_oracle(base_bf16, base_weights):
     w = config3()
     padded = torch.isnan(w.context[:, 0]).nonzero().view(-1)
     full = (~torch.isnan(w.context[:, 0])).nonzero().view(-1)
-    idx = torch.stack([padded[0], full[0]])
+    assert padded.numel() >= 4
+    idx = torch.cat([padded[:4], full[:4]]).sort().values  # 8 series, half of them left-padded
     err = _subset_check(base_bf16, base_weights, w.context, None, w.num_output_patches, idx)
-    assert err <= 2e-2
+    assert _report("cfg3_bf16_rel_8series", err) <= 2e-2
+
+
+def test_cfg4_full_batch_subset_vs_oracle(base_bf16, base_weights):
+    # 4096 series x ctx 512 (37 tokens per series: the short-set
+    # attention path), whole batch on the GPU, 32 series against the oracle
+    w = config4()
+    idx = torch.arange(0, 4096, 128)
+    err = _subset_check(base_bf16, base_weights, w.context, None, w.num_output_patches, idx)
+    assert _report("cfg4_bf16_rel_32series", err) <= 2e-2
 
 
 def test_batch_composition_invariance_and_determinism(base_bf16):
@@ -205,4 +225,4 @@ def test_batch1_equals_batched(base_bf16, base_weights):
     batch = base_bf16(w.context.to(DEV), num_output_patches=4).cpu()[3:4]
     assert torch.equal(one, batch)
     ref = orc.forward(orc.OracleConfig(), base_weights, w.context[3:4], None, 4)
-    assert _rel_err(one, ref) <= 2e-2
+    assert _report("batch1_bf16_rel", _rel_err(one, ref)) <= 2e-2
