@@ -181,34 +181,57 @@ def measured_peaks():
 
 
 class CpuReference:
-    """The reference algorithm on the host cores: the CPU oracle restatement of
-    CuteChronos2Model.forward in fp32 torch, all host threads."""
+    """The reference's own CPU implementation of the path on the host cores:
+    ``cutechronos.model.CuteChronos2Model`` (its torch fallbacks on CPU
+    tensors, fp32, all host threads) as staged into ``oracle/_ref`` by
+    ``oracle/stage_reference.py``; when that folder is absent, the CPU oracle
+    restatement of the same forward (kind "port")."""
 
     def __init__(self):
         from cutechronos_b200.model import CuteChronos2Config, CuteChronos2Model
-        from cutechronos_b200.workloads import seeded_state_dict
+        from cutechronos_b200.workloads import seeded_init_, seeded_state_dict
         from oracle import chronos2_oracle as orc
+        from oracle.stage_reference import load_reference_model_class
 
         self.threads = os.cpu_count() or 1
         torch.set_num_threads(self.threads)
-        m = CuteChronos2Model(CuteChronos2Config())
-        self.W = seeded_state_dict([(n, tuple(p.shape)) for n, p in m.named_parameters()], seed=0)
         self.orc = orc
+        ref = load_reference_model_class()
+        if ref is not None:
+            cfg_cls, mod_cls = ref
+            self.kind = "reference"
+            self.model = seeded_init_(mod_cls(cfg_cls()), seed=0).eval()
+            self.W = None
+        else:
+            self.kind = "port"
+            self.model = None
+            m = CuteChronos2Model(CuteChronos2Config())
+            self.W = seeded_state_dict([(n, tuple(p.shape)) for n, p in m.named_parameters()], seed=0)
+
+    @property
+    def what(self) -> str:
+        if self.kind == "reference":
+            return "reference cutechronos.model.CuteChronos2Model.forward (fp32, torch CPU path, staged in oracle/_ref)"
+        return "CPU oracle restatement of CuteChronos2Model.forward (fp32 torch)"
 
     def forecasts_per_s(self, n_series: int, L: int = 2048, N: int = 4, seed: int = 1) -> float:
         from cutechronos_b200.workloads import series_cfg1
 
         ctx = series_cfg1(n_series, L, seed)
-        t0 = time.perf_counter()
-        self.orc.forward(self.orc.OracleConfig(), self.W, ctx, None, N)
-        return n_series / (time.perf_counter() - t0)
+        with torch.inference_mode():
+            t0 = time.perf_counter()
+            if self.model is not None:
+                self.model(ctx, num_output_patches=N)
+            else:
+                self.orc.forward(self.orc.OracleConfig(), self.W, ctx, None, N)
+            return n_series / (time.perf_counter() - t0)
 
 
 def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    n = 16
+    n = 32
     ref = CpuReference()
     for _ in range(args.warmup):
         ref.forecasts_per_s(2)
@@ -221,10 +244,10 @@ def run_reference(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (configs[1] generator, seed 1)",
         "config": {"workload": "configs[1]: B=256 univariate, ctx 2048, pred 64 (4 patches), Chronos-2-base",
-                   "sample": f"{n} series per step", "l2": "n/a (CPU)"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{n} series of configs[1] per step, fp32 CPU oracle restatement of "
-                                   "CuteChronos2Model.forward"},
+                   "sample": f"{n} series per step (forecasts are independent per series, so the rate "
+                             "scales linearly to the full batch)", "l2": "n/a (CPU)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": ref.kind,
+                         "sample": f"{n} series of configs[1] per step, {ref.what}"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -295,6 +318,56 @@ def other_configs(model_bf16, dev, flush):
     finally:
         model_bf16.disable_turboquant_kv()
     return out
+
+
+def cfg4_sharded(model_bf16, dev, flush, steps, warmup, grouped=False):
+    """configs[4] as the sharding sweep: ONE global batch of 4096 series (ctx
+    512, N = 4), identical on every rank; each rank takes its shard of whole
+    groups (sharding.partition_groups), runs the forward on it and the (B, 21,
+    64) forecasts are all-gathered over NCCL back into the global order inside
+    every timed step (sharding.gather_forecasts).  Total work is fixed, so
+    this is strong scaling; time = max over ranks of the CUDA-event total.
+    grouped: the same series as 512 groups of 8 (group attention inside each
+    group; groups never split across ranks)."""
+    import torch.distributed as dist
+
+    from cutechronos_b200.sharding import gather_forecasts, partition_groups
+    from cutechronos_b200.workloads import config4
+
+    rank, world, _ = dist_env()
+    w = config4()
+    B = w.context.shape[0]
+    gid = torch.arange(B) // 8 if grouped else None
+    shards = partition_groups(gid, B, world)
+    mine = shards[rank]
+    ctx = w.context[mine].to(dev)
+    gid_local = gid[mine] if gid is not None else None
+    N = w.num_output_patches
+
+    def step():
+        y = model_bf16(ctx, num_output_patches=N, group_ids=gid_local)
+        return gather_forecasts(y, shards) if world > 1 else y
+
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for i in range(steps):
+        flush.fill_(i & 0xFF)
+        evs[i][0].record()
+        y = step()
+        evs[i][1].record()
+    torch.cuda.synchronize()
+    t = torch.tensor([sum(a.elapsed_time(b) for a, b in evs)], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / steps
+    assert y.shape[0] == B
+    return {"forecasts_per_s": B / (ms / 1e3), "ms_per_step": ms, "series_per_rank": int(mine.numel()),
+            "groups": "512 x 8" if grouped else "4096 x 1", "collective": "NCCL all_gather of the padded "
+            "(B_r, 21, 64) bf16 shards" if world > 1 else "none (one GPU)"}
 
 
 def pipeline_rates(model_bf16, dev, steps=3, warmup=1):
@@ -483,6 +556,12 @@ def run_b200(args):
         lat_p50 = None
         if rank == 0 and not args.no_latency:
             lat_p50 = graph_latency_ms(model, ctx[:1].clone(), N)
+        # ---- configs[4] sharding sweep: one global batch partitioned over the ranks
+        sharded = None
+        if not args.no_configs:
+            sharded = {"univariate": cfg4_sharded(model, dev, flush, max(3, args.steps // 2), 2),
+                       "grouped": cfg4_sharded(model, dev, flush, max(3, args.steps // 2), 2, grouped=True),
+                       "scaling": "strong (4096 series in total, split over the ranks)"}
         other = pipe_rates = None
         if rank == 0 and not args.no_configs:
             other = other_configs(model, dev, flush)
@@ -521,7 +600,7 @@ def run_b200(args):
         if not args.no_cpu and world == 1:
             ref = CpuReference()
             ref.forecasts_per_s(1, L, N)
-            cpu_v, cpu_threads = ref.forecasts_per_s(8, L, N), ref.threads
+            cpu_v, cpu_threads = ref.forecasts_per_s(32, L, N), ref.threads
         clk = clocks.summary()
         roofline = {
             "bound": "tensor", "kernel": "gemm_pair_kernel / gemm_tc_kernel (tcgen05, all GEMM launches of the step)",
@@ -539,7 +618,9 @@ def run_b200(args):
         if pre:
             kernels["preprocess"]["hbm_gbs"] = pre["bytes"] / (pre["ms"] / 1e3) / 1e9
         result = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": value, "unit": UNIT,
+            "value_is": "whole job: forecasts/s summed over all ranks (per GPU = value / n_gpus)",
+            "value_per_gpu": value / world, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (configs[1] generator; random-init weights seed 0)",
@@ -557,13 +638,15 @@ def run_b200(args):
             "gflop_per_forecast": gflop,
             "latency_b1_p50_ms": lat_p50,
             "graph_mode": graph_mode,
+            "cfg4_sharded": sharded,
             "other_configs": other,
             "pipeline": pipe_rates,
             "kernels": kernels,
             "clocks": clk,
-            "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads, "kind": "port",
-                             "sample": ("8 series of configs[1] (ctx 2048, N=4), fp32 CPU oracle restatement "
-                                        "of CuteChronos2Model.forward, one forward") if world == 1 else
+            "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads,
+                             "kind": ref.kind if cpu_v is not None else None,
+                             "sample": (f"32 series of configs[1] (ctx 2048, N=4), {ref.what}, one forward")
+                             if cpu_v is not None else
                              "not measured at N > 1 (taken on rank 0 of the N = 1 run)"},
         }
         print(json.dumps(result), flush=True)
