@@ -48,9 +48,16 @@ def rotate_inverse(x, signs=None, inv_perm=None, matrix=None):
 
 
 def fake_quant(x: torch.Tensor, *, mode: str, bits: int, codebook, boundaries, signs=None, perm=None,
-               inv_perm=None, matrix=None, proj=None, norm_dtype=torch.float16):
+               inv_perm=None, matrix=None, proj=None, norm_dtype=torch.float16, idx_override=None,
+               sign_override=None, internals=None):
     """-> (decoded float32, stats dict) as TurboQuantizer.forward
-    (quantizer.py:119-178) computes them; x (..., 64) any float dtype."""
+    (quantizer.py:119-178) computes them; x (..., 64) any float dtype.
+
+    Test hooks (not in the reference): ``idx_override`` / ``sign_override``
+    replace the bucket indices / QJL signs (for re-running a vector with one
+    decision at a bucket edge taken the other way); a dict passed as
+    ``internals`` receives the rotated unit vector ``y``, the indices ``idx``,
+    the QJL projections ``sr`` and the signs ``sgn``."""
     dim = x.shape[-1]
     mse_bits = bits if mode == "mse" else max(bits - 1, 0)
     xf = x.float()
@@ -59,7 +66,10 @@ def fake_quant(x: torch.Tensor, *, mode: str, bits: int, codebook, boundaries, s
     if mse_bits == 0:
         mse_unit = torch.zeros_like(unit)
     else:
-        idx = torch.bucketize(rotate(unit, signs, perm, matrix), boundaries)
+        y = rotate(unit, signs, perm, matrix)
+        idx = torch.bucketize(y, boundaries) if idx_override is None else idx_override
+        if internals is not None:
+            internals.update(y=y, idx=idx)
         mse_unit = rotate_inverse(codebook[idx].float(), signs, inv_perm, matrix)
     recon = mse_unit
     if mode == "prod":
@@ -69,7 +79,9 @@ def fake_quant(x: torch.Tensor, *, mode: str, bits: int, codebook, boundaries, s
             sgn = torch.ones_like(residual)
         else:
             sr = torch.einsum("...d,ed->...e", residual, proj.float())
-            sgn = torch.where(sr >= 0, 1.0, -1.0)
+            sgn = torch.where(sr >= 0, 1.0, -1.0) if sign_override is None else sign_override
+            if internals is not None:
+                internals.update(sr=sr, sgn=sgn)
         coeff = math.sqrt(math.pi / 2.0) / dim
         recon = mse_unit + coeff * rnorm * torch.einsum("...e,ed->...d", sgn, proj.float())
     out = recon * norms.to(norm_dtype).float()

@@ -58,11 +58,16 @@ def test_parameters_match_reference(gold, ci):
         assert np.array_equal(p["proj"].numpy(), gold[pre + "proj"])
 
 
-def _oracle(case, x, params):
+def _oracle(case, x, params, internals=None, idx=None, sgn=None):
     t = params.tensors
-    return tqo.fake_quant(x, mode=case[0], bits=case[1], codebook=t["codebook"], boundaries=t["boundaries"][
-        :max((1 << params.mse_bits) - 1, 0)], signs=t.get("signs"), perm=t.get("perm"), inv_perm=t.get("inv_perm"),
-        matrix=t.get("matrix"), proj=t.get("proj"))
+    return tqo.fake_quant(x, mode=case[0], bits=case[1], codebook=t["codebook"], boundaries=_bounds(params),
+                          signs=t.get("signs"), perm=t.get("perm"), inv_perm=t.get("inv_perm"),
+                          matrix=t.get("matrix"), proj=t.get("proj"), idx_override=idx, sign_override=sgn,
+                          internals=internals)
+
+
+def _bounds(params):
+    return params.tensors["boundaries"][:max((1 << params.mse_bits) - 1, 0)]
 
 
 @pytest.mark.parametrize("ci", range(len(CASES)))
@@ -100,42 +105,98 @@ def test_argument_errors():
 
 
 # ---------------------------------------------------------------------------------------- GPU --
-def _close_fraction(out, ref, scale):
-    """Fraction of vectors whose reconstruction matches within 1e-4 of the
-    vector's norm (the rest differ by a centroid or QJL-sign decision at a
-    bucket edge, where the reduction order of the norm decides)."""
-    err = (out - ref).abs().amax(dim=-1) / scale.clamp_min(1e-6)
-    return (err <= 1e-4).float().mean().item(), err.max().item()
+EDGE = 1e-5  # margin of an fp32 summation-order difference on a unit vector's coordinate / projection
+
+
+def _differs(got, ref, norm):
+    """Vectors whose stored (bf16) reconstruction differs from the oracle's by
+    more than one bf16 rounding step of an element (plus 1e-5 of the norm)."""
+    r = ref.to(torch.bfloat16).float()
+    return ((got - r).abs() > r.abs() * 2.0 ** -8 + 1e-5 * norm[:, None]).any(dim=-1)
+
+
+def _explain(case, x, params, got):
+    """Every vector whose kernel reconstruction differs from the oracle's must
+    be reproduced by the oracle with one or two decisions taken the other way
+    where the oracle itself sits on an edge: a rotated coordinate within EDGE of
+    a bucket boundary (centroid choice), or a QJL projection within EDGE of
+    zero (sign choice).  There the kernel's warp-reduction order of the norm and
+    of the dot products can decide either way.  Returns (mismatches, explained)."""
+    inn = {}
+    ref, _ = _oracle(case, x, params, internals=inn)
+    norm = x.float().norm(dim=-1)
+    bad = _differs(got, ref, norm).nonzero().view(-1).tolist()
+    b = _bounds(params)
+    explained = 0
+    for v in bad:
+        xv = x[v:v + 1]
+        cands = []
+        if "y" in inn:
+            y, idx = inn["y"][v], inn["idx"][v]
+            for i in range(y.numel()):
+                k = int(idx[i])
+                for kk, edge in ((k - 1, k - 1), (k + 1, k)):
+                    if 0 <= edge < b.numel() and 0 <= kk <= b.numel() and abs(float(y[i] - b[edge])) < EDGE:
+                        j = idx.clone().view(1, -1)
+                        j[0, i] = kk
+                        cands.append(("idx", j))
+        if "sr" in inn:
+            sr, sg = inn["sr"][v], inn["sgn"][v]
+            for e in (sr.abs() < EDGE).nonzero().view(-1).tolist():
+                g = sg.clone().view(1, -1)
+                g[0, e] = -g[0, e]
+                cands.append(("sgn", g))
+        tries = [[c] for c in cands] + [[c1, c2] for n, c1 in enumerate(cands) for c2 in cands[n + 1:]
+                                        if c1[0] != c2[0]]
+        for t in tries:
+            kw = {("idx" if k == "idx" else "sgn"): val for k, val in t}
+            alt, _ = _oracle(case, xv, params, **kw)
+            if not _differs(got[v:v + 1], alt, norm[v:v + 1]).any():
+                explained += 1
+                break
+    return len(bad), explained
 
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("heads", [12, 3])  # 4 heads per warp / one vector per warp
 @pytest.mark.parametrize("ci", range(len(CASES)))
 def test_kernel_matches_oracle(gold, ci, heads):
+    """Bucket and sign decisions agree with the oracle on every vector except
+    at an edge the test identifies (all mismatches explained, and at most 2 %
+    of vectors); the statistics equal the oracle's with the kernel's edge
+    decisions."""
     case = CASES[ci]
     g = torch.Generator().manual_seed(ci)
     rows = 40
     qkv = (torch.randn(rows, 3 * heads * 64, generator=g) * 1.5).to(torch.bfloat16)
     qkv[3, heads * 64: heads * 64 + 64] = 0  # a zero K vector
     kp = _params(case, "cuda")
-    vp = _params(("mse", 4, "hadamard", 100 + ci), "cuda")
+    vcase = ("mse", 4, "hadamard", 100 + ci)
+    vp = _params(vcase, "cuda")
     d = qkv.cuda()
     stats = torch.zeros(4, device="cuda")
     tq.kv_quant(d, rows, heads, kp, vp, q_col=0, k_col=heads * 64, v_col=2 * heads * 64, stats=stats)
     out = d.cpu()
     assert torch.equal(out[:, :heads * 64], qkv[:, :heads * 64])  # Q untouched without RoPE
-    for col, case_, par in ((heads * 64, case, _params(case)), (2 * heads * 64, ("mse", 4, "hadamard", 100 + ci),
-                                                                 _params(("mse", 4, "hadamard", 100 + ci)))):
+    for col, case_ in ((heads * 64, case), (2 * heads * 64, vcase)):
         x = qkv[:, col:col + heads * 64].reshape(-1, 64)
-        ref, st = _oracle(case_, x, par)
         got = out[:, col:col + heads * 64].reshape(-1, 64).float()
-        frac, worst = _close_fraction(got, ref.to(torch.bfloat16).float(), x.float().norm(dim=-1))
-        assert frac >= 0.99 and worst <= 0.5, (frac, worst)
+        n_bad, n_expl = _explain(case_, x, _params(case_), got)
+        print(f"TQ {case_} heads={heads}: {n_bad} of {x.shape[0]} vectors at an edge, {n_expl} explained")
+        assert n_expl == n_bad, (n_bad, n_expl)
+        assert n_bad <= 0.02 * x.shape[0]
+    # statistics (keys): the kernel's sums against the oracle's, within fp32
+    # accumulation-order differences and the effect of the explained edge decisions
     s = stats.cpu()
     x = qkv[:, heads * 64:2 * heads * 64].reshape(-1, 64)
-    _, st = _oracle(case, x, _params(case))
-    assert s[0].item() == pytest.approx(st["sse"], rel=2e-2)
-    assert s[1].item() == pytest.approx(st["max_abs_error"], rel=2e-1)
+    ref, st = _oracle(case, x, _params(case))
+    got = out[:, heads * 64:2 * heads * 64].reshape(-1, 64).float()
+    bad = _differs(got, ref, x.float().norm(dim=-1))
+    if not bad.any():
+        assert s[0].item() == pytest.approx(st["sse"], rel=1e-4)
+        assert s[1].item() == pytest.approx(st["max_abs_error"], rel=1e-4)
+    else:
+        assert s[0].item() == pytest.approx(st["sse"], rel=2e-2)
 
 
 @pytest.mark.gpu
@@ -160,11 +221,11 @@ def test_kernel_rope_then_quant_fp32():
 
     q_ref = rope(qkv[:, :heads * 64])
     assert torch.allclose(out[:, :heads * 64], q_ref, atol=1e-5)
-    k_ref, _ = _oracle(("prod", 4, "hadamard", 1), rope(qkv[:, heads * 64:2 * heads * 64]).reshape(-1, 64),
-                       _params(("prod", 4, "hadamard", 1)))
-    frac, worst = _close_fraction(out[:, heads * 64:2 * heads * 64].reshape(-1, 64), k_ref,
-                                  k_ref.norm(dim=-1))
-    assert frac >= 0.99 and worst <= 0.5
+    case = ("prod", 4, "hadamard", 1)
+    xk = rope(qkv[:, heads * 64:2 * heads * 64]).reshape(-1, 64)
+    n_bad, n_expl = _explain(case, xk, _params(case), out[:, heads * 64:2 * heads * 64].reshape(-1, 64))
+    print(f"TQ fp32 rope+{case}: {n_bad} of {xk.shape[0]} vectors at an edge, {n_expl} explained")
+    assert n_expl == n_bad and n_bad <= 0.02 * xk.shape[0]
 
 
 @pytest.mark.gpu
