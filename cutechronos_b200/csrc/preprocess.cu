@@ -25,6 +25,17 @@ __device__ __forceinline__ uint32_t pack2bf(float a, float b) {
 
 // Two sums in one pass over the block (one pair of barriers); red holds
 // 2 * warps doubles.
+// s + e += x with an error-free transformation (Knuth's two-sum): s + e keeps
+// the exact sum of the values added so far, up to the rounding of e itself
+// (below 2^-48 of the sum for the <= 32 values a thread adds).
+__device__ __forceinline__ void two_sum_acc(float& s, float& e, float x) {
+  const float t = __fadd_rn(s, x);
+  const float bp = __fsub_rn(t, s);
+  const float err = __fadd_rn(__fsub_rn(s, __fsub_rn(t, bp)), __fsub_rn(x, bp));
+  s = t;
+  e = __fadd_rn(e, err);
+}
+
 __device__ __forceinline__ void block_sum2(double& a, double& b, double* red) {
   for (int o = 16; o > 0; o >>= 1) {
     a += __shfl_xor_sync(0xffffffffu, a, o);
@@ -189,8 +200,8 @@ preprocess_kernel(const float* __restrict__ ctx, const float* __restrict__ cmask
 // registers across the mean, variance and patching passes; 16-byte loads and
 // stores.  (A warp per series, with up to 64 positions per lane, ran slower:
 // fewer series fit on an SM and each warp's chain of work grew.)
-template <typename T, int CH>
-__global__ void __launch_bounds__(kPreThreads, CH == 1 ? 5 : 1)
+template <typename T, int CH, int NTH>
+__global__ void __launch_bounds__(NTH, NTH == 128 ? 8 : (CH == 1 ? 5 : 1))
 preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ cmask, int B, int L, int Leff, int P,
                       int ps, float te_scale, float te_inv, int use_arcsinh, int use_reg, int N,
                       T* __restrict__ out, int ld, int pad_cols, uint8_t* __restrict__ tok_mask,
@@ -198,7 +209,7 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
                       int vec_loads) {
   pdl_launch_dependents();
   pdl_wait();
-  __shared__ double red[2 * (kPreThreads / 32)];
+  __shared__ double red[2 * (NTH / 32)];
   const int b = (int)blockIdx.x;
   const int tid = (int)threadIdx.x;
   const int G = (int)blockDim.x;
@@ -207,7 +218,6 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
   const float* m = cmask ? cmask + (size_t)b * L + (L - Leff) : nullptr;
   const int total = P * ps, pad = total - Leff;
   float v[CH][8];
-  double sum = 0.0, cnt = 0.0;
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
     const int j0 = 8 * (tid + c * G);
@@ -230,32 +240,52 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
       }
     }
   }
+  // per-thread sums as an unevaluated fp32 pair (error-free additions): the
+  // same exact partial sums as accumulating in double, without a conversion
+  // to double per value; the block then reduces them in double
+  // (one pair per chunk: independent dependency chains)
+  float s_hi[CH], s_lo[CH];
+  int n_ok = 0;
 #pragma unroll
-  for (int c = 0; c < CH; ++c)
+  for (int c = 0; c < CH; ++c) {
+    s_hi[c] = s_lo[c] = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (!isnan(v[c][i])) {
-        sum += v[c][i];
-        cnt += 1.0;
-      }
+    for (int i = 0; i < 8; ++i) {
+      const bool ok = !isnan(v[c][i]);
+      n_ok += ok ? 1 : 0;
+      two_sum_acc(s_hi[c], s_lo[c], ok ? v[c][i] : 0.0f);
+    }
+  }
+  double sum = 0.0, cnt = (double)n_ok;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) sum += (double)s_hi[c] + (double)s_lo[c];
   block_sum2(sum, cnt, red);
   const float lo = cnt > 0.0 ? (float)(sum / cnt) : 0.0f;
-  double ss = 0.0;
+  float q_hi[CH], q_lo[CH];
 #pragma unroll
-  for (int c = 0; c < CH; ++c)
+  for (int c = 0; c < CH; ++c) {
+    q_hi[c] = q_lo[c] = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (!isnan(v[c][i])) {
-        const float d = v[c][i] - lo;
-        ss += (double)(d * d);
-      }
-  ss = block_sum(ss, red);
-  float sc = cnt > 0.0 ? sqrtf((float)(ss / cnt)) : 1.0f;
-  if (sc == 0.0f) sc = 1e-5f;
-  if (tid == 0) {
-    loc_out[b] = lo;
-    scale_out[b] = sc;
+    for (int i = 0; i < 8; ++i) {
+      const float d = v[c][i] - lo;
+      two_sum_acc(q_hi[c], q_lo[c], isnan(v[c][i]) ? 0.0f : d * d);
+    }
   }
+  double ssp = 0.0;
+#pragma unroll
+  for (int c = 0; c < CH; ++c) ssp += (double)q_hi[c] + (double)q_lo[c];
+  double ss = block_sum(ssp, red);
+  // the scale is computed once (thread 0) and shared
+  __shared__ float sc_sh;
+  if (tid == 0) {
+    float sc0 = cnt > 0.0 ? sqrtf((float)(ss / cnt)) : 1.0f;
+    if (sc0 == 0.0f) sc0 = 1e-5f;
+    sc_sh = sc0;
+    loc_out[b] = lo;
+    scale_out[b] = sc0;
+  }
+  __syncthreads();
+  const float sc = sc_sh;
   // (x - loc) / scale as a product with the reciprocal: within 1.5 ulp of the
   // quotient, one division per series instead of one per value
   const float rsc = 1.0f / sc;
@@ -272,6 +302,34 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
       // product with its exact reciprocal is the same number (positions are
       // integers of magnitude < 2^24, so base + i is exact)
       const float tbase = (float)(j0 - total);
+      // uniform conditions are tested once per chunk, outside the per-value
+      // loops, so no value pays for the path it does not take
+      if (te_inv != 0.0f) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) te[i] = (tbase + (float)i) * te_inv;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) te[i] = (float)(j0 + i - total) / te_scale;
+      }
+      if (sizeof(T) == 2 && m == nullptr && j0 - pad >= 0) {  // bf16, NaN mask, all 8 positions in the series
+        if (use_arcsinh) {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const bool ok = !isnan(v[c][i]);
+            mt[i] = ok ? 1.0f : 0.0f;
+            val[i] = ok ? asinh_fast((v[c][i] - lo) * rsc) : 0.0f;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const bool ok = !isnan(v[c][i]);
+            mt[i] = ok ? 1.0f : 0.0f;
+            val[i] = ok ? (v[c][i] - lo) * rsc : 0.0f;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) acc += mt[i];
+      } else {
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int src = j0 + i - pad;
@@ -290,8 +348,8 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
         mt[i] = roundT<T>(mk);  // the mask in the model dtype (fractional masks pass through)
         // bf16: rounded once when packed below
         val[i] = mt[i] > 0.0f ? (sizeof(T) == 2 ? z : roundT<T>(z)) : 0.0f;
-        te[i] = te_inv != 0.0f ? (tbase + (float)i) * te_inv : (float)(j0 + i - total) / te_scale;
         acc += mt[i];
+      }
       }
       const int p = j0 / ps, c0 = j0 % ps;
       T* r = out + (row0 + p) * ld + c0;
@@ -326,23 +384,29 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
       if (attn_out) attn_out[(size_t)b * P + p] = on ? 1.0f : 0.0f;
     }
   }
-  // REG row (zeros) and future rows ([future time enc | 0 | 0])
+  // REG row (zeros) and future rows ([future time enc | 0 | 0]); no integer
+  // division per element
   const int extra = use_reg + N;
-  for (int idx = tid; idx < extra * 3 * ps; idx += G) {
-    const int e = idx / (3 * ps), c = idx % (3 * ps);
-    T* r = out + (row0 + P + e) * ld;
-    float fv = 0.0f;
-    const int n = e - use_reg;
-    if (n >= 0 && c < ps) fv = (float)(n * ps + c) / te_scale;
-    r[c] = fromf<T>(fv);
-  }
-  for (int e = tid; e < extra; e += G) tok_mask[row0 + P + e] = 1;
-  const int pc = pad_cols - 3 * ps;
-  if (pc > 0)
-    for (int idx = tid; idx < S * pc; idx += G) {
-      const int rr = idx / pc, c = idx % pc;
-      out[(row0 + rr) * ld + 3 * ps + c] = fromf<T>(0.0f);
+  for (int c = tid; c < 3 * ps; c += G)
+    for (int e = 0; e < extra; ++e) {
+      const int n = e - use_reg;
+      const float fv = n >= 0 && c < ps ? (float)(n * ps + c) / te_scale : 0.0f;
+      out[(row0 + P + e) * ld + c] = fromf<T>(fv);
     }
+  for (int e = tid; e < extra; e += G) tok_mask[row0 + P + e] = 1;
+  // zero the padding columns [3*ps, pad_cols) of every token row: one row per thread
+  const int pc = pad_cols - 3 * ps;
+  if (pc > 0) {
+    const bool vec16 = (pc * (int)sizeof(T)) % 16 == 0;  // 3*ps*sizeof(T) is a multiple of 16 here
+    for (int rr = tid; rr < S; rr += G) {
+      T* r = out + (row0 + rr) * ld + 3 * ps;
+      if (vec16) {
+        for (int q = 0; q < pc * (int)sizeof(T) / 16; ++q) reinterpret_cast<uint4*>(r)[q] = make_uint4(0u, 0u, 0u, 0u);
+      } else {
+        for (int c = 0; c < pc; ++c) r[c] = fromf<T>(0.0f);
+      }
+    }
+  }
 }
 
 // sinh for the output transform, from its definition: |x| < 1/2 by the odd
@@ -525,13 +589,17 @@ int launch_preprocess(const float* context, const float* cmask, int B, int L, in
   const bool vec = (ps == 8 || ps == 16 || ps == 32) && ((uintptr_t)patched & 15u) == 0 && (ld * esz) % 16 == 0 &&
                    total <= 4 * 8 * kPreThreads;
   const int vec_loads = ((uintptr_t)context & 15u) == 0 && L % 4 == 0 && (L - Leff) % 4 == 0 && (total - Leff) % 4 == 0;
-  const int CH = total <= 8 * kPreThreads ? 1 : total <= 16 * kPreThreads ? 2 : 4;
+  // 128 threads per series up to 2048 positions (two chunks of 8 per thread:
+  // the per-thread reductions and statistics are shared by 16 values), 256 above
+  const int NTH = total <= 16 * 128 ? 128 : kPreThreads;
+  const int CH = total <= 8 * NTH ? 1 : total <= 16 * NTH ? 2 : 4;
   // exact reciprocal of a power-of-two time-encoding scale (0: divide instead)
   int te_exp = 0;
   const float te_frac = std::frexp(te_scale, &te_exp);
   const float te_inv = te_frac == 0.5f && te_exp > -120 && te_exp < 120 ? std::ldexp(1.0f, 1 - te_exp) : 0.0f;
 #define CC2_PRE_VEC(TT, C_)                                                                                       \
-  CC2_CUDA(launch_k(preprocess_vec_kernel<TT, C_>, B, kPreThreads, 0, st, context, cmask, B, L, Leff, P, ps,       \
+  CC2_CUDA(launch_k(NTH == 128 ? preprocess_vec_kernel<TT, C_, 128> : preprocess_vec_kernel<TT, C_, kPreThreads>, \
+                    B, NTH, 0, st, context, cmask, B, L, Leff, P, ps,                                           \
                     te_scale, te_inv, use_arcsinh, use_reg ? 1 : 0, N, (TT*)patched, ld, pad_cols, tok, attn, loc, \
                     scale, vec_loads))
 #define CC2_PRE_VEC_ALL(TT)       \
