@@ -169,9 +169,9 @@ CC2_API int cc2_profile_read(int* kinds, float* ms, double* flops, double* bytes
  * latency-sensitive serving loops where a cudaMalloc would synchronise the
  * device.  The scratch lives in one static device array of
  * CC2_NOALLOC_SCRATCH_BYTES (32 MiB) that every GPU loading this library
- * holds until the process exits; it fits about 2,300 token rows of the
- * bf16 Chronos-2-base model (e.g. 16 series of context 2048 with N = 4) and
- * about 900 rows of the fp32 model (e.g. 6 series of context 2048).  Larger
+ * holds until the process exits; it fits about 1,950 token rows of the
+ * bf16 Chronos-2-base model (e.g. 14 series of context 2048 with N = 4) and
+ * about 930 rows of the fp32 model (e.g. 7 series of context 2048).  Larger
  * requests fail with CC2_E_WORKSPACE and a message giving the bytes needed.
  * The first call on a device looks the array's device address up (once per
  * device, with that device current); make that first call before any stream
