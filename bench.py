@@ -553,9 +553,11 @@ def run_b200(args):
             model.enable_cuda_graphs(False)
 
         # ---- p50 batch-1 latency (CUDA graph of one B=1 forward) ---------------
-        lat_p50 = None
+        lat_p50 = lat_p50_512 = None
         if rank == 0 and not args.no_latency:
             lat_p50 = graph_latency_ms(model, ctx[:1].clone(), N)
+            # the reference's published batch-1 configuration: context 512 (README: B=1, L=512)
+            lat_p50_512 = graph_latency_ms(model, series_cfg1(1, 512, 7).to(dev), N)
         # ---- configs[4] sharding sweep: one global batch partitioned over the ranks
         sharded = None
         if not args.no_configs:
@@ -637,6 +639,9 @@ def run_b200(args):
             "model_flops_frac": value / world * gflop * 1e9 / (tf_burst * 1e12),
             "gflop_per_forecast": gflop,
             "latency_b1_p50_ms": lat_p50,
+            "latency_b1_ctx512_p50_ms": lat_p50_512,
+            "latency_path": "bf16, one series, N = 4: a CUDA graph of one CuteChronos2Model.forward (input "
+                            "resident), p50 over 50 single replays timed with CUDA events",
             "graph_mode": graph_mode,
             "cfg4_sharded": sharded,
             "other_configs": other,
