@@ -739,6 +739,9 @@ def run_micro(args):
         "kv_quant prod4/mse4 M=34048": (
             lambda: tqm.kv_quant(qkv_tq, M, 12, kq_p, vq_p, q_col=0, k_col=d, v_col=2 * d), 0, M * 2 * d * 2 * 2),
         "group attn 64x8 S=133 bf16": (group_attn, 0, Bg * Sg * d * 2 * 4),
+        "group attn 64x8 S=133 bf16 (tcgen05)": (
+            lambda: kk.group_attention_contig(qkvg.view(Bg, Sg, 3 * d), tokg.view(Bg, Sg), 8, 12), 0,
+            Bg * Sg * d * 2 * 4),
         "preprocess B=16384 L=2048 bf16": (
             lambda: kk.fused_preprocess(ctxp, 16, 8192, True, dtype=torch.bfloat16), 0,
             Bp * (4 * Lp + 2 * 48 * Pp + Pp + 4 * Pp + 8)),

@@ -57,6 +57,11 @@ int g_attn_variant = 0;
 // Error word of the attention kernels' bounded waits (1 = a wait ran out).
 __device__ int g_attn_error = 0;
 
+int attention_error_word(int** p) {
+  CC2_CUDA(cudaGetSymbolAddress((void**)p, g_attn_error));
+  return CC2_OK;
+}
+
 int read_attention_error(int clear, int* value) {
   CC2_CUDA(cudaMemcpyFromSymbol(value, g_attn_error, sizeof(int)));
   if (clear) {

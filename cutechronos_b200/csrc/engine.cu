@@ -90,6 +90,10 @@ size_t gemm_f32_splitk_floats();
 int launch_kv_quant(int dtype, void* qkv, int ld, int rows, int q_col, int k_col, int v_col, int heads,
                     const cc2_kvq* key, const cc2_kvq* value, const float* rope_cs, int rope_period, float* stats,
                     cudaStream_t st);
+bool attn_group_tc_supported(int g, int ld, int ldo, const void* qkv, const void* out);
+int launch_attn_group_tc(const void* qkv, int ld, int qcol, int kcol, int vcol, void* out, int ldo,
+                         const uint8_t* tok, int B, int S, int heads, int g, int* err, cudaStream_t st);
+int attention_error_word(int** p);
 int launch_gemm_f32(const void*, int, const void*, int, void*, int, int, int, int, const cc2_epilogue*,
                     cudaStream_t, float* scratch = nullptr, size_t scratch_floats = 0);
 int launch_attention(int, int, const void*, int, int, int, int, void*, int, const uint8_t*, int, int, int, int,
@@ -581,12 +585,18 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
 
   // group structure
   int num_groups = B, max_group = 1;
+  int contig_g = 0;  // > 0: every group is a run of contig_g consecutive series (the tcgen05 group kernel)
   double gsq = (double)B;  // sum over groups of size^2 (attention FLOP count)
   if (group_ids) {
     std::vector<int32_t> mem(B), off(B + 1);
     CC2_TRY(cc2_group_layout(group_ids, B, mem.data(), off.data(), &num_groups, &max_group));
     gsq = 0.0;
     for (int g = 0; g < num_groups; ++g) gsq += (double)(off[g + 1] - off[g]) * (off[g + 1] - off[g]);
+    contig_g = max_group;
+    for (int g = 0; g < num_groups && contig_g; ++g)
+      if (off[g + 1] - off[g] != max_group) contig_g = 0;
+    for (int i = 0; i < B && contig_g; ++i)
+      if (mem[i] != i) contig_g = 0;
     if (max_group > 1) {
       CC2_CUDA(cudaMemcpyAsync(w.members, mem.data(), sizeof(int32_t) * B, cudaMemcpyHostToDevice, st));
       CC2_CUDA(cudaMemcpyAsync(w.offsets, off.data(), sizeof(int32_t) * (num_groups + 1), cudaMemcpyHostToDevice, st));
@@ -681,8 +691,15 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
       CC2_TRY(gemm(dt, X, d, Lw.wqkv_g, d, w.QKV, 3 * d, M, 3 * d, d, &g, st));
       {
         ProfScope ps_(CC2_K_ATTN_GROUP, 4.0 * (double)S * gsq * d, 0.0, st);
-        CC2_TRY(launch_attention(dt, 1, w.QKV, 3 * d, 0, d, 2 * d, Y, d, w.tok, S * num_groups, S, c.num_heads,
-                                 c.d_kv, w.members, w.offsets, num_groups, max_group, nullptr, st));
+        if (dt == CC2_BF16 && g_attn_variant == 0 && contig_g > 1 && c.d_kv == 64 &&
+            attn_group_tc_supported(contig_g, 3 * d, d, w.QKV, Y)) {
+          int* err = nullptr;
+          CC2_TRY(attention_error_word(&err));
+          CC2_TRY(launch_attn_group_tc(w.QKV, 3 * d, 0, d, 2 * d, Y, d, w.tok, B, S, c.num_heads, contig_g, err, st));
+        } else {
+          CC2_TRY(launch_attention(dt, 1, w.QKV, 3 * d, 0, d, 2 * d, Y, d, w.tok, S * num_groups, S, c.num_heads,
+                                   c.d_kv, w.members, w.offsets, num_groups, max_group, nullptr, st));
+        }
       }
       cc2_epilogue og = epi_m(CC2_EPI_RESID | CC2_EPI_SSQ, M);
       og.resid = X; og.ld_resid = d; og.ssq_out = ssq(3 * l + 2);
@@ -896,6 +913,17 @@ int cc2_attention(int dtype, int mode, const void* qkv, int ld_qkv, int q_col, i
   clear_error();
   return launch_attention(dtype, mode, qkv, ld_qkv, q_col, k_col, v_col, out, ld_out, token_mask, num_sets, S,
                           num_heads, d_kv, members, offsets, num_groups, max_group, rope_cs, (cudaStream_t)stream);
+}
+
+int cc2_group_attention_tc(const void* qkv, int ld_qkv, int q_col, int k_col, int v_col, void* out, int ld_out,
+                           const uint8_t* token_mask, int B, int S, int num_heads, int g, void* stream) {
+  clear_error();
+  CC2_REQUIRE(qkv && out && token_mask, "group_attention_tc: null pointer");
+  CC2_REQUIRE(attn_group_tc_supported(g, ld_qkv, ld_out, qkv, out), "group_attention_tc: unsupported g=%d or alignment", g);
+  int* err = nullptr;
+  CC2_TRY(attention_error_word(&err));
+  return launch_attn_group_tc(qkv, ld_qkv, q_col, k_col, v_col, out, ld_out, token_mask, B, S, num_heads, g, err,
+                              (cudaStream_t)stream);
 }
 
 int cc2_output_transform(int dtype, const void* preds, int ld_preds, const float* loc, const float* scale, void* out,

@@ -269,6 +269,22 @@ def attention_rows(qkv: torch.Tensor, token_mask: torch.Tensor, num_sets: int, S
     return out
 
 
+def group_attention_contig(qkv: torch.Tensor, token_mask: torch.Tensor, group_size: int, num_heads: int,
+                           ) -> torch.Tensor:
+    """Group self-attention on the tensor cores for groups of ``group_size``
+    consecutive series (2..32, a power of two): qkv (B, S, 3*H*64) bf16
+    packed [Q|K|V], token_mask (B, S) -> (B, S, H*64)."""
+    _cuda(qkv, token_mask)
+    B, S, W = qkv.shape
+    HD = W // 3
+    q = qkv.contiguous()
+    tok = token_mask.to(torch.uint8).contiguous()
+    out = torch.empty(B, S, HD, dtype=qkv.dtype, device=qkv.device)
+    nat.check(nat.load().cc2_group_attention_tc(q.data_ptr(), W, 0, HD, 2 * HD, out.data_ptr(), HD, tok.data_ptr(),
+                                                B, S, num_heads, group_size, _stream(qkv)), "cc2_group_attention_tc")
+    return out
+
+
 def group_attention(qkv: torch.Tensor, token_mask: torch.Tensor, group_ids: torch.Tensor, num_heads: int,
                     ) -> torch.Tensor:
     """Group self-attention core over token rows: qkv (B, S, 3*H*64) packed

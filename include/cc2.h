@@ -314,6 +314,17 @@ CC2_API int cc2_attention(int dtype, int mode, const void* qkv, int ld_qkv, int 
                   const int32_t* offsets, int num_groups, int max_group,
                   const float* rope_cs, void* stream);
 
+/* Group attention (mode 1 of cc2_attention) on the tensor cores for the common
+ * layout of model.py:295-312's batches: B series in groups of g consecutive
+ * series (g = 2, 4, 8, 16 or 32, B a multiple of g), bf16, d_kv = 64; S token
+ * rows per series (row b*S + t), heads heads.  Same result as cc2_attention
+ * mode 1 on that layout (P rounded to bf16 as the reference's softmax
+ * .to(dtype)); the forward uses it whenever the group ids have this layout.
+ * Returns CC2_E_INVALID for another g or misaligned operands. */
+CC2_API int cc2_group_attention_tc(const void* qkv, int ld_qkv, int q_col, int k_col, int v_col, void* out,
+                                   int ld_out, const uint8_t* token_mask, int B, int S, int num_heads, int g,
+                                   void* stream);
+
 /* Rearrange b n (q p) -> b q (n p), sinh (if use_arcsinh), * scale + loc
  * (model.py:816-829).  preds (B*N, Q*ps) dtype with row pitch ld_preds;
  * out (B, Q, N*ps) dtype. */

@@ -425,3 +425,29 @@ def test_linear_hi_lo_residual_stream(M, N, Kd, rowscale):
     assert (out_lo.cpu().float().abs() <= out.cpu().float().abs() * 2 ** -8 + 1e-30).all()
     ref_parts = kk.row_sumsq_parts(ref.float())
     assert torch.allclose(so.cpu(), ref_parts, rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("B,S,gsize", [(512, 133, 8), (64, 37, 2), (96, 20, 4), (128, 9, 16), (160, 5, 32), (200, 7, 8)])
+def test_group_attention_tensor_core(B, S, gsize):
+    """cc2_group_attention_tc (groups of gsize consecutive series on tcgen05)
+    against the oracle's attention with the group-time mask; 20 % of tokens
+    masked; B not a multiple of 128 for the last cases (a partial block)."""
+    H = 12
+    g = torch.Generator().manual_seed(B + S + gsize)
+    qkv = (torch.randn(B, S, 3 * 768, generator=g) * 0.5).to(torch.bfloat16)
+    tok = torch.rand(B, S, generator=g) > 0.2
+    gid = torch.arange(B) // gsize
+    q, k, v = (qkv.float()[..., i * 768:(i + 1) * 768].transpose(0, 1).reshape(S, B, H, 64).permute(0, 2, 1, 3)
+               for i in range(3))
+    same = (gid[:, None] == gid[None, :]).float()
+    gm = torch.einsum("qb,bt->qbt", same, tok.float()).permute(2, 0, 1).unsqueeze(1)
+    ref = orc.unscaled_attention(q, k, v, (1.0 - gm) * torch.finfo(torch.float32).min)
+    ref = ref.permute(0, 2, 1, 3).reshape(S, B, 768).transpose(0, 1)
+    out = K().group_attention_contig(qkv.to(DEV), tok.to(DEV), gsize, H).cpu().float()
+    live = (same @ tok.float()) > 0
+    d = (out - ref).abs()[live]
+    assert d.max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
+    assert torch.isfinite(out).all()
+    # the same as the mma.sync group kernel on every live query, within bf16 rounding of P
+    mma = K().group_attention(qkv.to(DEV), tok.to(DEV), gid, H).cpu().float()
+    assert (out - mma).abs()[live].max().item() <= 2e-2 * max(1.0, ref.abs().max().item())
