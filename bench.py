@@ -773,8 +773,10 @@ def run_micro(args):
             4 * args.batch * 12 * 133 * 133 * 64),
         "attn time S=37 B=4096": (lambda: kk.attention_rows(qkv4, tok4, B4, 37, 12, False, att4),
                                   4 * B4 * 12 * 37 * 37 * 64),
-        "attn time S=37 B=4096 (tcgen05)": (
+        "attn time S=37 B=4096 (one set per tcgen05 tile)": (
             variant(2, lambda: kk.attention_rows(qkv4, tok4, B4, 37, 12, False, att4)), 4 * B4 * 12 * 37 * 37 * 64),
+        "attn time S=37 B=4096 (mma.sync)": (
+            variant(1, lambda: kk.attention_rows(qkv4, tok4, B4, 37, 12, False, att4)), 4 * B4 * 12 * 37 * 37 * 64),
         "attn time S=521 B=32": (lambda: kk.attention_rows(qkvr, tok, 32, 521, 12, False, att),
                                  4 * 32 * 12 * 521 * 521 * 64),
         "attn time S=521 B=32 (mma.sync)": (

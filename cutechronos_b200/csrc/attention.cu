@@ -40,6 +40,9 @@ namespace cc2 {
 
 int encode_bf16_map(CUtensorMap* map, const void* ptr, int cols, int rows, int ld, int box_cols, int box_rows);
 bool attn_tc_supported(int S, int ld, int ldo, const void* qkv);
+bool attn_pack_tc_supported(int S, int ld, int ldo, const void* qkv, const void* out);
+int launch_attn_pack_tc(const void* qkv, int ld, int qcol, int kcol, int vcol, void* out, int ldo, const uint8_t* tok,
+                        int num_sets, int S, int heads, int* err, cudaStream_t st);
 bool attn_tc_long_supported(int S, int ld, int ldo, const void* qkv, const void* out);
 int launch_attn_tc_long(const void* qkv, int ld, int qcol, int kcol, int vcol, void* out, int ldo,
                         const uint8_t* tok, int num_sets, int S, int heads, int* err, cudaStream_t st);
@@ -1155,7 +1158,12 @@ int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int
     const bool aligned = ((uintptr_t)qkv & 15u) == 0 && (ld * 2) % 16 == 0;
     // (sets of fewer than 8 query tiles run faster in the whole-set kernel below)
     const bool tc_pick = g_attn_variant == 2 || (g_attn_variant == 0 && S >= 112);
-    if (mode == 0 && !cs && tc_pick && ((uintptr_t)out & 15u) == 0 && attn_tc_supported(S, ld, ldo, qkv)) {
+    if (mode == 0 && !cs && g_attn_variant == 0 && attn_pack_tc_supported(S, ld, ldo, qkv, out)) {
+      // short sets (16 < S <= 64): two per tcgen05 tile
+      int* err = nullptr;
+      CC2_CUDA(cudaGetSymbolAddress((void**)&err, g_attn_error));
+      return launch_attn_pack_tc(qkv, ld, qcol, kcol, vcol, out, ldo, tok, num_sets, S, heads, err, st);
+    } else if (mode == 0 && !cs && tc_pick && ((uintptr_t)out & 15u) == 0 && attn_tc_supported(S, ld, ldo, qkv)) {
       int* err = nullptr;
       CC2_CUDA(cudaGetSymbolAddress((void**)&err, g_attn_error));
       return launch_attn_tc(qkv, ld, qcol, kcol, vcol, out, ldo, tok, num_sets, S, heads, err, st);

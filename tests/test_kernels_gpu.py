@@ -294,7 +294,7 @@ def attn_variant():
 # tiles, 64/128/144-key widths, one or two buffer stages, many items per CTA,
 # a series whose keys are all masked; long sets of 2..5 key blocks with a
 # ragged last block (145, 200, 257, 521) or full blocks (256, 640)
-@pytest.mark.parametrize("B,S", [(1, 17), (3, 37), (2, 64), (5, 128), (4, 129), (7, 133), (2, 144), (3, 160),
+@pytest.mark.parametrize("B,S", [(1, 17), (3, 37), (2, 64), (5, 20), (9, 50), (4, 63), (5, 128), (4, 129), (7, 133), (2, 144), (3, 160),
                                  (2, 160), (2, 192), (300, 133), (700, 37), (3, 145), (4, 200), (2, 256),
                                  (3, 257), (5, 521), (3, 640), (30, 521)])
 @pytest.mark.parametrize("variant", [0, 1, 2])
