@@ -836,7 +836,7 @@ int cc2_preprocess(const float* context, const float* context_mask, int B, int L
 
 int cc2_set_gemm_variant(int variant) {
   const int old = g_gemm_variant;
-  g_gemm_variant = (variant == 1 || variant == 3) ? variant : 0;
+  g_gemm_variant = (variant >= 1 && variant <= 3) ? variant : 0;
   return old;
 }
 

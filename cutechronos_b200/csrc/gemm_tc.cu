@@ -262,13 +262,17 @@ __device__ __forceinline__ void load_rope_row(const Epi& ep, int row, bool row_o
   }
 }
 // Rotate-half RoPE on one 64-column head held in r (row-scaled first).
+// Here and in the epilogue every product and sum is an explicit round-to-
+// nearest intrinsic: the compiler may not contract them into FMAs one way in
+// one tile kernel and another way in the next, so every tile path rounds the
+// same (results do not depend on which kernel a batch size selects).
 __device__ __forceinline__ void rope_group(uint32_t* r, const uint32_t (&cs)[32], float rs) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) {
     const float c = __uint_as_float(cs[i] << 16), sn = __uint_as_float(cs[i] & 0xffff0000u);
-    const float x1 = __uint_as_float(r[i]) * rs, x2 = __uint_as_float(r[i + 32]) * rs;
-    r[i] = __float_as_uint(x1 * c - x2 * sn);
-    r[i + 32] = __float_as_uint(x2 * c + x1 * sn);
+    const float x1 = __fmul_rn(__uint_as_float(r[i]), rs), x2 = __fmul_rn(__uint_as_float(r[i + 32]), rs);
+    r[i] = __float_as_uint(__fmaf_rn(x1, c, -__fmul_rn(x2, sn)));
+    r[i + 32] = __float_as_uint(__fmaf_rn(x2, c, __fmul_rn(x1, sn)));
   }
 }
 
@@ -313,13 +317,14 @@ __device__ __forceinline__ float epilogue_group(const Epi& ep, const int flags, 
     const uint32_t addr = box + (uint32_t)lane * 128u + (((uint32_t)c ^ rsw) << 4);
     float v[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[c * 8 + j]) * rs;
+    for (int j = 0; j < 8; ++j) v[j] = __fmul_rn(__uint_as_float(r[c * 8 + j]), rs);
     const bool col_ok = col < N;
     if ((flags & CC2_EPI_BIAS) && col_ok) {
       const float4 b0 = __ldg(reinterpret_cast<const float4*>(ep.bias + col));
       const float4 b1 = __ldg(reinterpret_cast<const float4*>(ep.bias + col) + 1);
-      v[0] += b0.x; v[1] += b0.y; v[2] += b0.z; v[3] += b0.w;
-      v[4] += b1.x; v[5] += b1.y; v[6] += b1.z; v[7] += b1.w;
+      v[0] = __fadd_rn(v[0], b0.x); v[1] = __fadd_rn(v[1], b0.y); v[2] = __fadd_rn(v[2], b0.z);
+      v[3] = __fadd_rn(v[3], b0.w); v[4] = __fadd_rn(v[4], b1.x); v[5] = __fadd_rn(v[5], b1.y);
+      v[6] = __fadd_rn(v[6], b1.z); v[7] = __fadd_rn(v[7], b1.w);
     }
     if (flags & CC2_EPI_RELU) {
 #pragma unroll
@@ -332,16 +337,16 @@ __device__ __forceinline__ float epilogue_group(const Epi& ep, const int flags, 
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 f = __bfloat1622float2(hh[e]);
-        v[2 * e] += f.x;
-        v[2 * e + 1] += f.y;
+        v[2 * e] = __fadd_rn(v[2 * e], f.x);
+        v[2 * e + 1] = __fadd_rn(v[2 * e + 1], f.y);
       }
       if (lo) {
         const __nv_bfloat162* ll = reinterpret_cast<const __nv_bfloat162*>(&rl[c]);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float2 f = __bfloat1622float2(ll[e]);
-          v[2 * e] += f.x;
-          v[2 * e + 1] += f.y;
+          v[2 * e] = __fadd_rn(v[2 * e], f.x);
+          v[2 * e + 1] = __fadd_rn(v[2 * e + 1], f.y);
         }
       }
     }
@@ -358,8 +363,8 @@ __device__ __forceinline__ float epilogue_group(const Epi& ep, const int flags, 
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const float2 f = __bfloat1622float2(hh[e]);
-        d[2 * e] = v[2 * e] - f.x;
-        d[2 * e + 1] = v[2 * e + 1] - f.y;
+        d[2 * e] = __fsub_rn(v[2 * e], f.x);
+        d[2 * e + 1] = __fsub_rn(v[2 * e + 1], f.y);
       }
       if (ep.lo_out && row_ok && col_ok) {
         uint4 lw;
@@ -391,8 +396,8 @@ __device__ __forceinline__ float epilogue_group(const Epi& ep, const int flags, 
 __device__ __forceinline__ float row_scale(const Epi& ep, const int flags, int row, bool row_ok) {
   if (!(flags & CC2_EPI_ROWSCALE) || !row_ok) return 1.0f;
   float t = 0.0f;
-  for (int g = 0; g < ep.ssq_parts; ++g) t += ep.ssq_in[(size_t)g * ep.ssq_ld + row];
-  return rsqrtf(t * ep.inv_dim + ep.eps);
+  for (int g = 0; g < ep.ssq_parts; ++g) t = __fadd_rn(t, ep.ssq_in[(size_t)g * ep.ssq_ld + row]);
+  return rsqrtf(__fmaf_rn(t, ep.inv_dim, ep.eps));
 }
 
 template <int BN>
@@ -1108,6 +1113,16 @@ int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, in
     CC2_TRY(make_map_box(&mr, ep.resid, N, M, ep.ld_resid, 64, 32));
   } else {
     mr = mc;
+  }
+  // Few token rows (batch-1 serving: 133 rows per series): the 256 x 256 pair
+  // tiles would put the whole GEMM on a handful of SMs, each running a
+  // K-long chain of 128 x 256 MMAs.  128 x 64 tiles on single SMs spread the
+  // weight stream and the MMAs over 4-8x more SMs (same per-element
+  // accumulation order, so the results do not change).
+  const int pair_ctas = 2 * ((M + 255) / 256) * ((N + 255) / 256);
+  if (g_gemm_variant == 0 && N >= 64 && 2 * pair_ctas <= num_sms()) {
+    CC2_TRY(make_map(&mb, W, K, N, ldw, 64));
+    return launch<64>(ma, mb, mc, mr, M, N, K, ep, st);
   }
   if (g_gemm_variant != 1 && M > BM) {  // 2-SM tiles (256 x 256 per CTA pair)
     CC2_TRY(make_map(&mb, W, K, N, ldw, 128));

@@ -241,10 +241,14 @@ typedef struct {
   void* lo_out; const void* resid_lo; int ld_lo;  /* CC2_EPI_LO */
 } cc2_epilogue;
 
-/* Tile variant of the bf16 GEMM: 0 (default) = 2-SM tcgen05 tiles of 256 x 256
- * per CTA pair when M > 128, else 1-SM 128 x 256 / 128 x 128 tiles; 1 = 1-SM
- * tiles only; 3 = measurement only: the 2-SM mainloop with the epilogue
- * skipped (nothing is written).  Process-wide; returns the previous value. */
+/* Tile variant of the bf16 GEMM: 0 (default) = 1-SM 128 x 64 tiles when the
+ * 2-SM grid would occupy at most half the SMs (few token rows, e.g. batch-1
+ * serving), else 2-SM tcgen05 tiles of 256 x 256 per CTA pair when M > 128,
+ * else 1-SM 128 x 256 / 128 x 128 tiles; 1 = 1-SM 128 x 256 / 128 x 128 tiles
+ * only; 2 = as 0 without the 128 x 64 tiles; 3 = measurement only: the 2-SM
+ * mainloop with the epilogue skipped (nothing is written).  All variants
+ * except 3 give bit-identical results.  Process-wide; returns the previous
+ * value. */
 CC2_API int cc2_set_gemm_variant(int variant);
 
 /* Time-attention kernel choice for bf16 sets (RoPE applied beforehand):

@@ -230,6 +230,43 @@ def test_gemm_pair_vs_single_sm_tiles(M, N, Kd):
     assert (outs[0][0].double() - ref).abs().max().item() <= 8e-3 * ref.abs().max().item()
 
 
+# few token rows (batch-1 serving): 128 x 64 single-SM tiles instead of the
+# 256 x 256 pair tiles; the per-element accumulation is the same, so the
+# results must be too, bit for bit
+@pytest.mark.parametrize("M,N,Kd", [(4, 3072, 768), (133, 768, 768), (133, 2304, 768), (133, 768, 3072),
+                                    (266, 3072, 768), (532, 768, 768), (100, 336, 256)])
+def test_gemm_small_m_tiles_bit_identical(M, N, Kd):
+    from cutechronos_b200 import _native as nat
+    g = torch.Generator().manual_seed(M + N)
+    x = torch.randn(M, Kd, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(N, Kd, generator=g) / math.sqrt(Kd)).to(torch.bfloat16).to(DEV)
+    resid = torch.randn(M, N, generator=g).to(torch.bfloat16).to(DEV)
+    bias = torch.randn(N, generator=g).to(DEV)
+    lib = nat.load()
+    outs = []
+    try:
+        for variant in (0, 2):
+            lib.cc2_set_gemm_variant(variant)
+            out = resid.clone()
+            so = torch.zeros(((N + 63) // 64, M), device=DEV)
+            K().linear(x, w, residual=out, ssq_out=so, out=out)
+            plain = K().linear(x, w)
+            # hi + lo residual stream with the row scale (the engine's O / FFN-down form)
+            hl, lo_buf = resid.clone(), K().rows_to_lo((resid.float() * 2 ** -9).to(torch.bfloat16))
+            K().linear(x, w, residual=hl, residual_lo=lo_buf, lo_out=lo_buf, out=hl,
+                       row_ssq=K().row_sumsq_parts(x.float()), norm_dim=Kd, eps=1e-6)
+            # the QKV form (row scale + RoPE on the first 2/3 of the columns) and bias + ReLU
+            rc = (2 * N // 3) // 64 * 64
+            qkv = K().linear(x, w, row_ssq=K().row_sumsq_parts(x.float()), norm_dim=Kd, eps=1e-6,
+                             rope_period=133, rope_cols=rc) if rc else plain
+            br = K().linear(x, w, bias, relu=True)
+            outs.append((out.cpu(), so.cpu(), plain.cpu(), hl.cpu(), lo_buf.cpu(), qkv.cpu(), br.cpu()))
+    finally:
+        lib.cc2_set_gemm_variant(0)
+    for i, (a, b) in enumerate(zip(outs[0], outs[1])):
+        assert torch.equal(a, b), i
+
+
 @pytest.mark.parametrize("M,S", [(133 * 3, 133), (37, 37), (521 * 2, 521)])
 def test_qkv_epilogue_rope(M, S):
     # RoPE applied in the QKV GEMM epilogue (Q and K columns, position = row % S)
