@@ -21,10 +21,12 @@ EXPORTED = (
     "cc2_profile_begin", "cc2_profile_read", "cc2_set_gemm_variant", "cc2_forward_noalloc",
     "cc2_stack_series", "cc2_select_quantiles", "cc2_set_attention_variant",
     "cc2_set_attention_trace", "cc2_set_gemm_trace", "cc2_kv_quant", "cc2_model_set_kv_quant",
-    "cc2_set_launch_overlap", "cc2_test_starve_gemm", "cc2_group_attention_tc",
+    "cc2_set_launch_overlap", "cc2_test_starve_gemm", "cc2_group_attention_tc", "cc2_set_layer_chain",
+    "cc2_test_starve_layer_barrier", "cc2_set_layer_trace",
 )
 KIND_NAMES = {1: "preprocess", 2: "gemm_tc", 3: "attn_time", 4: "attn_group", 5: "rmsnorm", 6: "output_transform",
-              7: "gemm_qkv", 8: "gemm_o", 9: "gemm_group", 10: "gemm_ffn_up", 11: "gemm_ffn_down", 12: "gemm_io"}
+              7: "gemm_qkv", 8: "gemm_o", 9: "gemm_group", 10: "gemm_ffn_up", 11: "gemm_ffn_down", 12: "gemm_io",
+              13: "layers"}
 GEMM_KINDS = (2, 7, 8, 9, 10, 11, 12)
 
 
@@ -108,6 +110,9 @@ def load(path: Path | str | None = None) -> C.CDLL:
     lib.cc2_model_set_kv_quant.argtypes = [v, i, v, v, v]
     lib.cc2_set_launch_overlap.argtypes = [i]
     lib.cc2_test_starve_gemm.argtypes = [i]
+    lib.cc2_set_layer_chain.argtypes = [i]
+    lib.cc2_test_starve_layer_barrier.argtypes = [i]
+    lib.cc2_set_layer_trace.argtypes = [v]
     lib.cc2_group_attention_tc.argtypes = [v, i, i, i, i, v, i, v, i, i, i, i, v]
     lib.cc2_forward_noalloc.argtypes = [v, v, v, i, i, i, v, v, v, v, v]
     lib.cc2_profile_read.argtypes = [v, v, v, v, i, C.POINTER(i)]

@@ -35,6 +35,7 @@
 #include <cuda.h>
 
 #include "common.cuh"
+#include "attn_set_tile.cuh"
 
 namespace cc2 {
 
@@ -53,7 +54,9 @@ int launch_attn_tc(const void* qkv, int ld, int qcol, int kcol, int vcol, void* 
 // is faster than the mma.sync kernels, and the long-set tcgen05 kernel for
 // 145..640 tokens; 1: the mma.sync kernels only for time attention and the
 // scalar kernel for small groups; 2: tcgen05 for every set it supports
-// (17..640 tokens).  Set through
+// (17..640 tokens); 3: the whole-set mma.sync kernel (attn_set_kernel) for
+// every time-attention set that fits its shared memory - the arithmetic of
+// the layer-persistent forward's attention stage.  Set through
 // cc2_set_attention_variant.
 int g_attn_variant = 0;
 
@@ -77,6 +80,7 @@ int read_attention_error(int clear, int* value) {
 namespace {
 
 typedef __nv_bfloat16 bf16;
+using namespace aset;
 
 struct SetInfo {
   int mode;  // 0 time, 1 group
@@ -106,34 +110,12 @@ __device__ __forceinline__ SetGeom set_geom(const SetInfo& si, int set) {
   return g;
 }
 
-constexpr float kMaskedScore = -1e30f;
-constexpr float kLog2e = 1.4426950408889634f;
 
 // ---------------------------------------------------------------------------
 // tensor-core flash kernel (bf16)
 // ---------------------------------------------------------------------------
 constexpr int QT = 64, KT = 64, DH = 64, LDS = DH + 8;  // padded smem rows (144 B)
 
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
-}
-__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                         uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ uint32_t pack2(float a, float b) {
-  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&h);
-}
 
 // Rotate-half RoPE on a [rows][LDS] bf16 tile in shared memory (fp32 math,
 // one rounding), positions pos0 + r for rows r < valid.
@@ -307,22 +289,10 @@ attn_mma_kernel(const bf16* __restrict__ qkv, int ld, int qcol, int kcol, int vc
 // of the set are skipped, so a set of n keys costs ceil(n/8) score tiles per
 // query tile.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
-}
 
 constexpr int kSetMaxWarps = 8;
 constexpr size_t kSetSmemLimit = 225 * 1024;  // larger sets use the blocked kernel
 
-// Q, K, V tiles live in shared memory as [row][64] bf16 with 128-byte rows;
-// 16-byte chunk c of row r is stored at chunk c ^ (r & 7), so ldmatrix on 8
-// consecutive rows touches 8 distinct bank groups.
-__device__ __forceinline__ uint32_t swz(uint32_t base, int r, int chunk) {
-  return base + (uint32_t)r * 128u + ((uint32_t)(chunk ^ (r & 7)) << 4);
-}
 
 inline size_t set_kernel_smem(int npad) { return (size_t)npad * (3 * 128 + sizeof(float)); }
 
@@ -408,107 +378,10 @@ attn_set_kernel(const bf16* __restrict__ qkv, int ld, int qcol, int kcol, int vc
     __syncthreads();
   }
 
-  for (int q0 = warp * 16; q0 < n; q0 += nwarps * 16) {
-    uint32_t qf[4][4];
-#pragma unroll
-    for (int ks = 0; ks < 4; ++ks)
-      ldsm_x4(swz(qb, q0 + (lane & 15), 2 * ks + (lane >> 4)), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
-    float o[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
-    float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
-
-    for (int k0 = 0; k0 < n; k0 += KTT) {
-      const int kvalid = n - k0;
-      float s[KTT / 8][4];
-#pragma unroll
-      for (int nt = 0; nt < KTT / 8; ++nt) {
-        s[nt][0] = s[nt][1] = s[nt][2] = s[nt][3] = 0.0f;
-        if (nt * 8 < kvalid) {
-          const int kr = k0 + nt * 8 + (lane & 7);
-#pragma unroll
-          for (int ks = 0; ks < 4; ks += 2) {
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4(swz(kb, kr, 2 * ks + (lane >> 3)), b0, b1, b2, b3);
-            mma16816(s[nt], qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3], b0, b1);
-            mma16816(s[nt], qf[ks + 1][0], qf[ks + 1][1], qf[ks + 1][2], qf[ks + 1][3], b2, b3);
-          }
-        }
-      }
-      float mx0 = -INFINITY, mx1 = -INFINITY;
-#pragma unroll
-      for (int nt = 0; nt < KTT / 8; ++nt) {
-        const int c = nt * 8 + 2 * (lane & 3);
-        const float b0 = c < kvalid ? kbias[k0 + c] : -INFINITY;
-        const float b1 = c + 1 < kvalid ? kbias[k0 + c + 1] : -INFINITY;
-        s[nt][0] = b0 == 0.0f ? s[nt][0] * kLog2e : b0;
-        s[nt][1] = b1 == 0.0f ? s[nt][1] * kLog2e : b1;
-        s[nt][2] = b0 == 0.0f ? s[nt][2] * kLog2e : b0;
-        s[nt][3] = b1 == 0.0f ? s[nt][3] * kLog2e : b1;
-        mx0 = fmaxf(mx0, fmaxf(s[nt][0], s[nt][1]));
-        mx1 = fmaxf(mx1, fmaxf(s[nt][2], s[nt][3]));
-      }
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-      mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-      mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-      const float mn0 = fmaxf(m0, mx0), mn1 = fmaxf(m1, mx1);
-      const float c0 = exp2f(m0 - mn0), c1 = exp2f(m1 - mn1);
-      m0 = mn0; m1 = mn1;
-      l0 *= c0; l1 *= c1;
-#pragma unroll
-      for (int dt = 0; dt < 8; ++dt) { o[dt][0] *= c0; o[dt][1] *= c0; o[dt][2] *= c1; o[dt][3] *= c1; }
-#pragma unroll
-      for (int nt = 0; nt < KTT / 8; ++nt) {
-        s[nt][0] = exp2f(s[nt][0] - mn0); s[nt][1] = exp2f(s[nt][1] - mn0);
-        s[nt][2] = exp2f(s[nt][2] - mn1); s[nt][3] = exp2f(s[nt][3] - mn1);
-        l0 += s[nt][0] + s[nt][1];
-        l1 += s[nt][2] + s[nt][3];
-      }
-#pragma unroll
-      for (int j = 0; j < KTT / 16; ++j) {
-        if (j * 16 < kvalid) {
-          const uint32_t a0 = pack2(s[2 * j][0], s[2 * j][1]);
-          const uint32_t a1 = pack2(s[2 * j][2], s[2 * j][3]);
-          const uint32_t a2 = pack2(s[2 * j + 1][0], s[2 * j + 1][1]);
-          const uint32_t a3 = pack2(s[2 * j + 1][2], s[2 * j + 1][3]);
-          const int vr = k0 + 16 * j + (lane & 15);
-#pragma unroll
-          for (int dt = 0; dt < 8; dt += 2) {
-            uint32_t b0, b1, b2, b3;
-            ldsm_x4_t(swz(vb, vr, dt + (lane >> 4)), b0, b1, b2, b3);
-            mma16816(o[dt], a0, a1, a2, a3, b0, b1);
-            mma16816(o[dt + 1], a0, a1, a2, a3, b2, b3);
-          }
-        }
-      }
-    }
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-    l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-    l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-    const float i0 = 1.0f / l0, i1 = 1.0f / l1;
-    // stage the 16 x 64 output in this warp's own (already consumed) Q rows
-    __syncwarp();
-    const int r0 = q0 + (lane >> 2);
-#pragma unroll
-    for (int dt = 0; dt < 8; ++dt) {
-      const uint32_t off = 4u * (lane & 3);
-      asm volatile("st.shared.b32 [%0], %1;" ::"r"(swz(qb, r0, dt) + off), "r"(pack2(o[dt][0] * i0, o[dt][1] * i0)));
-      asm volatile("st.shared.b32 [%0], %1;" ::"r"(swz(qb, r0 + 8, dt) + off), "r"(pack2(o[dt][2] * i1, o[dt][3] * i1)));
-    }
-    __syncwarp();
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int rr = q0 + (lane >> 3) + 4 * i, c = lane & 7;
-      if (rr < n) {
-        uint4 v;
-        asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                     : "r"(swz(qb, rr, c)));
-        *reinterpret_cast<uint4*>(out + (size_t)g.row(rr, si.S) * ldo + h * DH + c * 8) = v;
-      }
-    }
-  }
+  for (int q0 = warp * 16; q0 < n; q0 += nwarps * 16)
+    set_tile<KTT>(qb, kb, vb, kbias, n, q0, lane, [&](int rr, int c, const uint4& v) {
+      *reinterpret_cast<uint4*>(out + (size_t)g.row(rr, si.S) * ldo + h * DH + c * 8) = v;
+    });
 }
 
 // ---------------------------------------------------------------------------
@@ -1172,7 +1045,7 @@ int launch_attention(int dtype, int mode, const void* qkv, int ld, int qcol, int
       int* err = nullptr;
       CC2_CUDA(cudaGetSymbolAddress((void**)&err, g_attn_error));
       return launch_attn_tc_long(qkv, ld, qcol, kcol, vcol, out, ldo, tok, num_sets, S, heads, err, st);
-    } else if (mode == 0 && !cs && pbufs >= 1 && aligned && (S + 15) / 16 >= 8) {
+    } else if (mode == 0 && !cs && g_attn_variant != 3 && pbufs >= 1 && aligned && (S + 15) / 16 >= 8) {
       CUtensorMap map;
       CC2_TRY(encode_bf16_map(&map, qkv, ld, num_sets * S, ld, 64, npad_t / nbox));
       PersistArgs pa{S, npad_t, heads, num_sets * heads, qcol, kcol, vcol, npad_t / nbox, nbox, pbufs, pbuf};

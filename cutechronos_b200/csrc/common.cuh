@@ -58,6 +58,7 @@ int num_sms();
 enum : int {
   DEV_ERR_GEMM_TIMEOUT = 1,
   DEV_ERR_ATTN_TIMEOUT = 2,
+  DEV_ERR_LAYER_TIMEOUT = 4,  // grid barrier of the layer-persistent forward
 };
 // Read (and optionally clear) the device error words of the current device.
 int read_device_error(int clear, int* value);

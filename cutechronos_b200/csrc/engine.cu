@@ -86,6 +86,8 @@ int set_attn_trace(void* buf);
 int set_attn_long_trace(void* buf);
 int set_gemm_trace(void* buf);
 int set_gemm_starve(int on);
+int set_chain_starve(int on);
+int set_chain_trace(void* buf);
 size_t gemm_f32_splitk_floats();
 int launch_kv_quant(int dtype, void* qkv, int ld, int rows, int q_col, int k_col, int v_col, int heads,
                     const cc2_kvq* key, const cc2_kvq* value, const float* rope_cs, int rope_period, float* stats,
@@ -94,6 +96,18 @@ bool attn_group_tc_supported(int g, int ld, int ldo, const void* qkv, const void
 int launch_attn_group_tc(const void* qkv, int ld, int qcol, int kcol, int vcol, void* out, int ldo,
                          const uint8_t* tok, int B, int S, int heads, int g, int* err, cudaStream_t st);
 int attention_error_word(int** p);
+int chain_max_stages();
+int chain_max_set();
+int chain_begin(int M);
+void chain_abandon();
+int chain_add_gemm(const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,
+                   const cc2_epilogue* e);
+int chain_add_attention(const void* qkv, int ld, int qcol, int kcol, int vcol, void* out, int ldo,
+                        const uint8_t* tok, int sets, int S, int heads);
+int chain_launch(unsigned int* bar, cudaStream_t st);
+// 1 (default): the encoder layers of a bf16 forward with few token rows run as
+// one layer-persistent kernel (cc2_set_layer_chain)
+int g_layer_chain = 1;
 int launch_gemm_f32(const void*, int, const void*, int, void*, int, int, int, int, const cc2_epilogue*,
                     cudaStream_t, float* scratch = nullptr, size_t scratch_floats = 0);
 int launch_attention(int, int, const void*, int, int, int, int, void*, int, const uint8_t*, int, int, int, int,
@@ -328,6 +342,7 @@ struct Workspace {
   char* XLO; char* ALO;  // bf16: low halves of the residual stream X and of its alternate buffer ATT
   int32_t* members; int32_t* offsets; char* O; char* PRED;
   float* splitk; size_t splitk_floats;  // fp32 mode: K-slice partial sums of the small-M GEMMs
+  unsigned int* chain_bar;              // grid barrier of the layer-persistent forward
 };
 
 size_t plan_ws(const cc2_model& m, int B, int L, int N, Workspace* w, char* base) {
@@ -349,6 +364,7 @@ size_t plan_ws(const cc2_model& m, int B, int L, int N, Workspace* w, char* base
   size_t oSPLIT = p.take(4 * splitk_floats);
   const size_t lo_bytes = m.dtype == CC2_BF16 ? e * align_up(M, 32) * d : 0;  // 32-row interleaved
   size_t oXLO = p.take(lo_bytes), oALO = p.take(lo_bytes);
+  size_t oBAR = p.take(16);
   if (w && base) {
     w->E = base + oE; w->X = base + oX; w->QKV = base + oQKV; w->ATT = base + oATT;
     w->ssq = (float*)(base + oSSQ); w->tok = (uint8_t*)(base + oTOK);
@@ -357,6 +373,7 @@ size_t plan_ws(const cc2_model& m, int B, int L, int N, Workspace* w, char* base
     w->O = base + oO; w->PRED = base + oPRED;
     w->splitk = (float*)(base + oSPLIT); w->splitk_floats = splitk_floats;
     w->XLO = lo_bytes ? base + oXLO : nullptr; w->ALO = lo_bytes ? base + oALO : nullptr;
+    w->chain_bar = (unsigned int*)(base + oBAR);
   }
   return p.off;
 }
@@ -365,14 +382,36 @@ size_t plan_ws(const cc2_model& m, int B, int L, int N, Workspace* w, char* base
 thread_local int t_gemm_kind = CC2_K_GEMM;  // profiler kind of the next gemm() on this thread
 thread_local float* t_splitk = nullptr;
 thread_local size_t t_splitk_floats = 0;
+thread_local bool t_chain_rec = false;  // gemm() records a stage of the layer-persistent forward
 
 int gemm(int dtype, const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,
          const cc2_epilogue* e, cudaStream_t st) {
+  if (t_chain_rec) {
+    t_gemm_kind = CC2_K_GEMM;
+    return chain_add_gemm(A, lda, W, ldw, out, ldo, M, N, K, e);
+  }
   ProfScope ps_(t_gemm_kind, 2.0 * M * N * K, 0.0, st);
   t_gemm_kind = CC2_K_GEMM;
   if (dtype == CC2_BF16) return launch_gemm_tc(A, lda, W, ldw, out, ldo, M, N, K, e, st);
   return launch_gemm_f32(A, lda, W, ldw, out, ldo, M, N, K, e, st, t_splitk, t_splitk_floats);
 }
+
+// Records the layers' GEMMs and time attentions as stages of one
+// layer-persistent launch for its lifetime.
+struct ChainScope {
+  bool on;
+  explicit ChainScope(bool enable, int M) : on(enable && chain_begin(M) == CC2_OK) { t_chain_rec = on; }
+  ~ChainScope() {
+    if (on) chain_abandon();
+    t_chain_rec = false;
+  }
+  int launch(unsigned int* bar, double flops, cudaStream_t st) {
+    t_chain_rec = false;
+    on = false;
+    ProfScope ps_(CC2_K_LAYERS, flops, 0.0, st);
+    return chain_launch(bar, st);
+  }
+};
 
 struct SplitKScope {
   SplitKScope(float* p, size_t n) { t_splitk = p; t_splitk_floats = n; }
@@ -642,6 +681,13 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
     if (!lo) return;
     ep.flags |= CC2_EPI_LO; ep.resid_lo = resid_lo; ep.lo_out = out_lo; ep.ld_lo = d;
   };
+  // Few token rows (batch-1 serving): the layers' GEMMs and time attentions
+  // are recorded as stages and run as one layer-persistent launch.
+  bool kvq_on = false;
+  for (const auto& q : m->kvq) kvq_on = kvq_on || q.has_k || q.has_v;
+  const bool chain = lo && g_layer_chain && g_gemm_variant == 0 && max_group == 1 && !kvq_on && c.d_kv == 64 &&
+                     M <= 384 && S <= chain_max_set() && 6 * c.num_layers <= chain_max_stages();
+  ChainScope chain_scope(chain, M);
   for (int l = 0; l < c.num_layers; ++l) {
     const cc2_layer_pack& Lw = m->layers[l];
     // time attention
@@ -662,7 +708,9 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
                               q.has_v ? &q.value : nullptr, rope_done ? nullptr : m->rope, S, q.stats, st));
       rope_done = true;
     }
-    {
+    if (t_chain_rec) {
+      CC2_TRY(chain_add_attention(w.QKV, 3 * d, 0, d, 2 * d, Y, d, w.tok, B, S, c.num_heads));
+    } else {
       ProfScope ps_(CC2_K_ATTN_TIME, 4.0 * B * (double)S * S * d, 0.0, st);
       CC2_TRY(launch_attention(dt, 0, w.QKV, 3 * d, 0, d, 2 * d, Y, d, w.tok, B, S, c.num_heads, c.d_kv,
                                nullptr, nullptr, 0, 0, rope_done ? nullptr : m->rope, st));
@@ -717,6 +765,10 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
     with_lo(f2, XL, XL);
     t_gemm_kind = CC2_K_GEMM_FFN_DOWN;
     CC2_TRY(gemm(dt, w.E, dff, Lw.wo_f, dff, X, d, M, d, dff, &f2, st));
+  }
+  if (chain_scope.on) {
+    const double per_layer = 2.0 * M * (5.0 * d * d + 2.0 * d * dff) + 4.0 * B * (double)S * S * d;
+    CC2_TRY(chain_scope.launch(w.chain_bar, per_layer * c.num_layers, st));
   }
   (void)KE;
   // final RMSNorm of the N future rows -> O[:, dff:]
@@ -842,13 +894,24 @@ int cc2_set_gemm_variant(int variant) {
 
 int cc2_set_attention_variant(int variant) {
   const int old = g_attn_variant;
-  g_attn_variant = (variant == 1 || variant == 2) ? variant : 0;
+  g_attn_variant = (variant >= 1 && variant <= 3) ? variant : 0;
   return old;
 }
 
 int cc2_test_starve_gemm(int on) {
   clear_error();
   return set_gemm_starve(on);
+}
+
+int cc2_test_starve_layer_barrier(int on) {
+  clear_error();
+  return set_chain_starve(on);
+}
+
+int cc2_set_layer_chain(int enabled) {
+  const int old = g_layer_chain;
+  g_layer_chain = enabled ? 1 : 0;
+  return old;
 }
 
 int cc2_set_launch_overlap(int enabled) {
@@ -884,6 +947,11 @@ int cc2_model_set_kv_quant(cc2_model* m, int layer, const cc2_kvq* key, const cc
 int cc2_set_gemm_trace(void* device_buffer) {
   clear_error();
   return set_gemm_trace(device_buffer);
+}
+
+int cc2_set_layer_trace(void* device_buffer) {
+  clear_error();
+  return set_chain_trace(device_buffer);
 }
 
 int cc2_set_attention_trace(void* device_buffer) {

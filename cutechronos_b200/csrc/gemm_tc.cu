@@ -27,9 +27,11 @@
 // DEV_ERR_GEMM_TIMEOUT, all roles leave their loops, TMEM is freed and the
 // kernel returns.
 #include <cuda.h>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
+#include "attn_set_tile.cuh"
 
 namespace cc2 {
 
@@ -42,6 +44,9 @@ __device__ int g_dev_error = 0;
 // MMA warp's bounded wait on that stage runs out.  Only loads that were issued are in flight when the
 // kernel leaves, and they land within microseconds of the 2 s limit.
 __device__ int g_gemm_starve = 0;
+// Test hook (cc2_test_starve_layer_barrier), one-shot: CTA 0 of the next
+// layer-persistent launch leaves at its first grid barrier without arriving.
+__device__ int g_chain_starve = 0;
 
 int read_device_error(int clear, int* value) {
   CC2_CUDA(cudaMemcpyFromSymbol(value, g_dev_error, sizeof(int)));
@@ -292,14 +297,23 @@ __device__ __forceinline__ size_t lo_index(int row, int col, int ld) {
 // memory (interleaved layout above: coalesced across the warp's rows).
 // Loads one 64-column group's residual low halves of this lane's row (zeros
 // outside the matrix).
+// CG: through L2 only - for data that other SMs wrote earlier in the same
+// kernel (the layer-persistent forward); otherwise the read-only path.
+template <bool CG = false>
 __device__ __forceinline__ void load_lo_group(uint4 (&rl)[8], const Epi& ep, int row, bool row_ok, int col0, int N) {
 #pragma unroll
   for (int c = 0; c < 8; ++c) {
     rl[c] = make_uint4(0u, 0u, 0u, 0u);
-    if (ep.resid_lo && row_ok && col0 + c * 8 < N)
-      asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
-                   : "=r"(rl[c].x), "=r"(rl[c].y), "=r"(rl[c].z), "=r"(rl[c].w)
-                   : "l"(ep.resid_lo + lo_index(row, col0 + c * 8, ep.ld_lo)));
+    if (ep.resid_lo && row_ok && col0 + c * 8 < N) {
+      if (CG)
+        asm volatile("ld.global.cg.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(rl[c].x), "=r"(rl[c].y), "=r"(rl[c].z), "=r"(rl[c].w)
+                     : "l"(ep.resid_lo + lo_index(row, col0 + c * 8, ep.ld_lo)));
+      else
+        asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(rl[c].x), "=r"(rl[c].y), "=r"(rl[c].z), "=r"(rl[c].w)
+                     : "l"(ep.resid_lo + lo_index(row, col0 + c * 8, ep.ld_lo)));
+    }
   }
 }
 
@@ -393,10 +407,14 @@ __device__ __forceinline__ float epilogue_group(const Epi& ep, const int flags, 
   return ssq;
 }
 
+template <bool CG = false>
 __device__ __forceinline__ float row_scale(const Epi& ep, const int flags, int row, bool row_ok) {
   if (!(flags & CC2_EPI_ROWSCALE) || !row_ok) return 1.0f;
   float t = 0.0f;
-  for (int g = 0; g < ep.ssq_parts; ++g) t = __fadd_rn(t, ep.ssq_in[(size_t)g * ep.ssq_ld + row]);
+  for (int g = 0; g < ep.ssq_parts; ++g) {
+    const float* q = ep.ssq_in + (size_t)g * ep.ssq_ld + row;
+    t = __fadd_rn(t, CG ? __ldcg(q) : *q);
+  }
   return rsqrtf(__fmaf_rn(t, ep.inv_dim, ep.eps));
 }
 
@@ -1039,6 +1057,356 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
   return launch_pair_t<-1, 5, 2>(ma, mb, mc, mr, M, N, K, ep, st);
 }
 
+// ---------------------------------------------------------------------------------
+// Layer-persistent forward for few token rows (batch-1 serving).
+//
+// With a few hundred token rows every GEMM of an encoder layer is a handful of
+// 128 x 64 tiles and the time attention a dozen (head, set) items; launched
+// one kernel each, the forward is a chain of ~72 launches whose fixed costs
+// (launch, prologue, first load, drain) exceed the work.  Here one
+// cooperative launch of one CTA per SM runs the whole list of stages (QKV
+// GEMM, time attention, O-projection, group block, FFN up, FFN down, per
+// layer), with a grid-wide barrier between stages.  TMEM, the mbarriers and
+// the shared-memory ring are set up once; the producer / MMA / epilogue roles
+// keep their ring and accumulator phases across stages.
+//
+// Each GEMM stage is the 1-SM 128 x 64 tile GEMM above (same MMAs, same
+// epilogue functions), so its results equal those of gemm_tc_kernel<64>; the
+// time-attention stage runs aset::set_tile, the body of the whole-set
+// attention kernel, so it equals that kernel (attention variant 3).
+//
+// Coherence inside the kernel: activations written by one stage are read by
+// other SMs in the next, so loads that could hit a stale L1 line go through
+// L2 (ld.global.cg / cp.async.cg / TMA), and every thread fences its generic
+// and async proxies around the grid barrier.  The barrier (arrival counter,
+// generation, abort word in caller-zeroed global memory) waits with the same
+// wall-clock bound as the mbarrier waits; on expiry it raises
+// DEV_ERR_LAYER_TIMEOUT and the abort word, every CTA leaves its stage loop,
+// frees its TMEM and returns.
+// ---------------------------------------------------------------------------------
+namespace chain {
+
+constexpr int BN = 64;
+using C = Cfg<BN>;
+constexpr int kMaxMaps = 72;
+constexpr int kMaxStages = 76;
+constexpr int kWarps = kThreads / 32;
+
+struct Stage {
+  Epi ep;
+  int kind;  // 0: GEMM, 1: time attention
+  int N, K;
+  int a, b, c, r;  // tensor-map indices (GEMM)
+  const bf16* qkv;  // attention: [sets * S, ld] rows with Q, K, V column blocks
+  bf16* out;
+  const uint8_t* tok;
+  int ld, ldo, qcol, kcol, vcol, sets, S, heads;
+};
+
+struct Params {
+  CUtensorMap maps[kMaxMaps];
+  Stage st[kMaxStages];
+  int nstages, M;
+  unsigned int* bar;  // [0] arrivals, [1] generation, [2] abort (zeroed before the launch)
+};
+static_assert(sizeof(Params) <= 32000, "kernel parameter block too large");
+
+__device__ __forceinline__ void fence_proxy_async_all() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Optional stage trace (cc2_set_layer_trace): CTAs < kTraceCtas record, per
+// stage, the %globaltimer when all their roles finished the stage and when
+// the grid barrier released them.
+constexpr int kTraceCtas = 8;
+__device__ unsigned long long* g_chain_trace = nullptr;
+
+// Grid-wide barrier (all threads of every CTA call it).  False: abort.
+__device__ __noinline__ bool grid_sync(unsigned* bar, volatile int* abort_flag, int si) {
+  fence_proxy_async_all();
+  __threadfence();
+  __syncthreads();
+  unsigned long long* tr = g_chain_trace;
+  if (tr && threadIdx.x == 0 && blockIdx.x < kTraceCtas)
+    tr[((size_t)blockIdx.x * kMaxStages + si) * 2] = globaltimer_ns();
+  if (threadIdx.x == 0) {
+    bool ok = *abort_flag == 0;
+    if (ok && blockIdx.x == 0 && *(volatile int*)&g_chain_starve && atomicExch(&g_chain_starve, 0)) {
+      *abort_flag = 1;  // test hook: this CTA never arrives, so the others' bounded waits run out
+    } else if (ok) {
+      const unsigned gen = ld_acquire(bar + 1);
+      if (atomicAdd(bar, 1u) == gridDim.x - 1) {
+        atomicExch(bar, 0u);
+        __threadfence();
+        atomicAdd(bar + 1, 1u);
+      } else {
+        const unsigned long long t0 = globaltimer_ns();
+        for (uint32_t n = 1;; ++n) {
+          if (ld_acquire(bar + 1) != gen) break;
+          if ((n & 15u) == 0) {
+            if (*(volatile unsigned*)(bar + 2)) { ok = false; break; }
+            if (globaltimer_ns() - t0 > kWaitLimitNs) {
+              atomicOr(&g_dev_error, DEV_ERR_LAYER_TIMEOUT);
+              ok = false;
+              break;
+            }
+          }
+        }
+      }
+    }
+    if (!ok) {
+      atomicExch(bar + 2, 1u);
+      *abort_flag = 1;
+    }
+    __threadfence();
+    if (tr && blockIdx.x < kTraceCtas) tr[((size_t)blockIdx.x * kMaxStages + si) * 2 + 1] = globaltimer_ns();
+  }
+  __syncthreads();
+  fence_proxy_async_all();
+  return *abort_flag == 0;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constant__ Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* epi_smem = smem + C::STAGES * C::STAGE_BYTES;
+  uint64_t* bars = (uint64_t*)(epi_smem + 8 * kEpiBox);
+  uint32_t* tmem_slot = (uint32_t*)(bars + 2 * C::STAGES + 12);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t bar0 = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (C::STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * C::STAGES + 2 + a); };
+  auto rbar = [&](int q, int b) { return bar0 + 8u * (2 * C::STAGES + 4 + 2 * q + b); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    for (int i = 0; i < 8; ++i) mbar_init(bar0 + 8u * (2 * C::STAGES + 4 + i), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int M = p.M;
+  const int m_tiles = (M + BM - 1) / BM;
+
+  // role state carried across stages
+  int pstage = 0; uint32_t pphase = 0;             // producer ring position
+  int mstage = 0; uint32_t mphase = 0; int mit = 0;  // MMA ring position, tiles issued
+  int eit = 0; uint32_t use = 0, rphase = 0;        // epilogue tiles, residual boxes
+
+  for (int si = 0; si < p.nstages; ++si) {
+    const Stage& s = p.st[si];
+    if (s.kind == 0) {
+      const int N = s.N;
+      const int n_tiles = (N + BN - 1) / BN;
+      const int num_tiles = m_tiles * n_tiles;
+      const int kblocks = (s.K + BK - 1) / BK;
+      const CUtensorMap* tmA = &p.maps[s.a];
+      const CUtensorMap* tmB = &p.maps[s.b];
+      const CUtensorMap* tmC = &p.maps[s.c];
+      const CUtensorMap* tmR = &p.maps[s.r];
+      if (warp == 0) {
+        if (lane == 0) {
+          bool ok = true;
+          for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+            const int mt = tile / n_tiles, nt = tile % n_tiles;
+            for (int kb = 0; kb < kblocks; ++kb) {
+              if (!mbar_wait(empty_bar(pstage), pphase ^ 1u, abort_flag)) { ok = false; break; }
+              const uint32_t sa = smem_u32(smem + pstage * C::STAGE_BYTES);
+              mbar_arrive_expect_tx(full_bar(pstage), C::STAGE_BYTES);
+              tma_load_2d(sa, tmA, full_bar(pstage), kb * BK, mt * BM);
+              tma_load_2d(sa + C::A_BYTES, tmB, full_bar(pstage), kb * BK, nt * BN);
+              if (++pstage == C::STAGES) { pstage = 0; pphase ^= 1u; }
+            }
+          }
+        }
+        __syncwarp();
+      } else if (warp == 1) {
+        if (lane == 0) {
+          constexpr uint32_t idesc = idesc_bf16<BN>();
+          bool ok = true;
+          for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++mit) {
+            const int acc = mit & 1;
+            const uint32_t acc_phase = (uint32_t)(mit >> 1) & 1u;
+            if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) break;
+            tc_fence_after();
+            const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+            for (int kb = 0; kb < kblocks; ++kb) {
+              if (!mbar_wait(full_bar(mstage), mphase, abort_flag)) { ok = false; break; }
+              tc_fence_after();
+              const uint32_t sa = smem_u32(smem + mstage * C::STAGE_BYTES);
+              const uint32_t sb = sa + C::A_BYTES;
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k)
+                mma_bf16(d_tmem, sw128_desc(sa + 32u * k), sw128_desc(sb + 32u * k), idesc, (kb | k) != 0 ? 1u : 0u);
+              mma_commit(empty_bar(mstage));
+              if (++mstage == C::STAGES) { mstage = 0; mphase ^= 1u; }
+            }
+            if (ok) mma_commit(tfull_bar(acc));
+          }
+        }
+        __syncwarp();
+      } else {
+        // epilogue warps 2..5: TMEM lane quarter q = tile rows 32q..32q+31
+        const Epi& ep = s.ep;
+        const int q = warp & 3;
+        const bool resid = (ep.flags & CC2_EPI_RESID) != 0;
+        const uint32_t box0 = smem_u32(epi_smem + (size_t)q * 2 * kEpiBox);
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++eit, ++use) {
+          const int mt = tile / n_tiles, nt = tile % n_tiles;
+          const int row0 = mt * BM + q * 32;
+          const int col0 = nt * BN;
+          const int b = use & 1;
+          const uint32_t box = box0 + b * kEpiBox;
+          if (lane == 0) {
+            bulk_wait_read0();  // the store that last used this box has read it
+            if (resid) {
+              mbar_arrive_expect_tx(rbar(q, b), kEpiBox);
+              tma_load_2d(box, tmR, rbar(q, b), col0, row0);
+            }
+          }
+          __syncwarp();
+          const int row = row0 + lane;
+          const bool row_ok = row < M;
+          const float rs = row_scale<true>(ep, ep.flags, row, row_ok);
+          const bool special = (ep.flags & CC2_EPI_SPECIAL) && row_ok && (row % ep.sp_period) == ep.sp_offset;
+          const bool rope_tile = (ep.flags & CC2_EPI_ROPE) && col0 < ep.rope_cols;
+          uint32_t cs[32];
+          if (rope_tile) load_rope_row(ep, row, row_ok, cs);
+          uint4 rl[8];
+          if ((ep.flags & CC2_EPI_LO) && resid) load_lo_group<true>(rl, ep, row, row_ok, col0, N);
+          const int acc = eit & 1;
+          const uint32_t acc_phase = (uint32_t)(eit >> 1) & 1u;
+          if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag)) break;
+          tc_fence_after();
+          const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
+          uint32_t r[64];
+          tmem_ld32(tbase, r);
+          tmem_ld32(tbase + 32, r + 32);
+          tmem_ld_wait();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(tempty_bar(acc));  // accumulator is in registers
+          if (resid) {
+            if (!mbar_wait(rbar(q, b), (rphase >> b) & 1u, abort_flag)) break;
+            rphase ^= 1u << b;
+          }
+          float rsg = rs;
+          if (rope_tile) {
+            rope_group(r, cs, rs);
+            rsg = 1.0f;
+          }
+          const float ssq = epilogue_group(ep, ep.flags, r, rsg, special, col0, N, box, lane, resid, row, row_ok, rl);
+          if ((ep.flags & CC2_EPI_SSQ) && row_ok) ep.ssq_out[(size_t)(col0 >> 6) * ep.ssq_ld + row] = ssq;
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(tmC, box, col0, row0);
+            bulk_commit();
+          }
+        }
+        if (lane == 0) bulk_wait_all();  // this stage's outputs are in global memory
+        __syncwarp();
+      }
+    } else {
+      // time attention: items (set, head, chunk of up to kWarps query tiles);
+      // Q / K / V of the item's set and head staged in the ring's memory
+      const int n = s.S;
+      const int npad = (n + 15) & ~15;
+      const int nqt = npad / 16;
+      const int chunks = (nqt + kWarps - 1) / kWarps;
+      const int items = s.sets * s.heads * chunks;
+      const uint32_t qb = smem_u32(smem);
+      const uint32_t kb = qb + (uint32_t)npad * 128u;
+      const uint32_t vb = kb + (uint32_t)npad * 128u;
+      float* kbias = reinterpret_cast<float*>(smem + (size_t)npad * 384);
+      for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int set = item / (s.heads * chunks);
+        const int h = (item / chunks) % s.heads;
+        const int ch = item % chunks;
+        const int q_lo = ch * kWarps * 16, q_hi = min(npad, q_lo + kWarps * 16);
+        const size_t row0 = (size_t)set * n;
+        for (int idx = threadIdx.x; idx < npad * 8; idx += blockDim.x) {
+          const int rr = idx >> 3, c = idx & 7;
+          const bool q_row = rr >= q_lo && rr < q_hi;
+          if (rr < n) {
+            const bf16* src = s.qkv + (row0 + rr) * s.ld + c * 8;
+            if (q_row) aset::cp_async16(aset::swz(qb, rr, c), src + s.qcol + h * 64);
+            aset::cp_async16(aset::swz(kb, rr, c), src + s.kcol + h * 64);
+            aset::cp_async16(aset::swz(vb, rr, c), src + s.vcol + h * 64);
+          } else {
+            const uint4 z = make_uint4(0, 0, 0, 0);
+            if (q_row) *reinterpret_cast<uint4*>(smem + (aset::swz(qb, rr, c) - qb)) = z;
+            *reinterpret_cast<uint4*>(smem + (aset::swz(kb, rr, c) - qb)) = z;
+            *reinterpret_cast<uint4*>(smem + (aset::swz(vb, rr, c) - qb)) = z;
+          }
+        }
+        for (int rr = threadIdx.x; rr < npad; rr += blockDim.x)
+          kbias[rr] = rr < n ? (s.tok[row0 + rr] ? 0.0f : aset::kMaskedScore) : -INFINITY;
+        aset::cp_async_wait_all();
+        __syncthreads();
+        const int q0 = q_lo + warp * 16;
+        if (q0 < n)
+          aset::set_tile<64>(qb, kb, vb, kbias, n, q0, lane, [&](int rr, int c, const uint4& v) {
+            *reinterpret_cast<uint4*>(s.out + (row0 + rr) * s.ldo + h * 64 + c * 8) = v;
+          });
+        __syncthreads();
+      }
+    }
+    if (si + 1 < p.nstages && !grid_sync(p.bar, abort_flag, si)) break;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ---- host side: stages are recorded by the forward, then launched at once ----
+struct Rec {
+  Params p;
+  int nmaps = 0;
+  bool active = false;
+};
+static thread_local Rec t_rec;
+
+static int map_index(const CUtensorMap& m) {
+  Rec& r = t_rec;
+  for (int i = 0; i < r.nmaps; ++i)
+    if (std::memcmp(&r.p.maps[i], &m, sizeof(CUtensorMap)) == 0) return i;
+  if (r.nmaps >= kMaxMaps) return -1;
+  r.p.maps[r.nmaps] = m;
+  return r.nmaps++;
+}
+
+}  // namespace chain
+
 }  // namespace tc
 
 // bf16 2-D tensor map with 128-byte swizzle (shared with the attention kernels).
@@ -1052,14 +1420,70 @@ int encode_bf16_map(CUtensorMap* map, const void* ptr, int cols, int rows, int l
   return tc::make_map_box(map, ptr, cols, rows, ld, box_cols, box_rows);
 }
 
-// 0: 2-SM tiles when M > 128 (default); 1: single-SM tiles only; 3: 2-SM
-// mainloop with the epilogue skipped (measurement only, output not written).
-// Set through cc2_set_gemm_variant.
+// 0 (default): 1-SM 128 x 64 tiles for few rows, else 2-SM tiles when
+// M > 128; 1: single-SM 128 x 256 / 128 x 128 tiles only; 2: as 0 without the
+// 128 x 64 tiles; 3: 2-SM mainloop with the epilogue skipped (measurement
+// only, output not written).  Set through cc2_set_gemm_variant.
 int g_gemm_variant = 0;
+
+int set_chain_trace(void* buf) {
+  unsigned long long* p = (unsigned long long*)buf;
+  CC2_CUDA(cudaMemcpyToSymbol(tc::chain::g_chain_trace, &p, sizeof(p)));
+  return CC2_OK;
+}
+
+int set_chain_starve(int on) {
+  const int v = on ? 1 : 0;
+  CC2_CUDA(cudaMemcpyToSymbol(g_chain_starve, &v, sizeof(int)));
+  return CC2_OK;
+}
 
 int set_gemm_starve(int on) {
   const int v = on ? 1 : 0;
   CC2_CUDA(cudaMemcpyToSymbol(g_gemm_starve, &v, sizeof(int)));
+  return CC2_OK;
+}
+
+// Device epilogue arguments from the public ones, validated.
+static int build_epi(const cc2_epilogue* e, int M, int N, tc::Epi* ep) {
+  using namespace tc;
+  *ep = Epi{};
+  ep->flags = e ? e->flags : 0;
+  if (e) {
+    ep->ssq_in = e->ssq_in;
+    ep->ssq_parts = (e->norm_dim + 63) / 64;
+    ep->ssq_ld = e->ssq_ld;
+    ep->inv_dim = e->norm_dim > 0 ? 1.0f / (float)e->norm_dim : 0.0f;
+    ep->eps = e->eps;
+    ep->bias = e->bias;
+    ep->resid = (const bf16*)e->resid;
+    ep->ld_resid = e->ld_resid;
+    ep->ssq_out = e->ssq_out;
+    ep->special = e->special;
+    ep->sp_period = e->special_period;
+    ep->sp_offset = e->special_offset;
+    ep->rope_cs = e->rope_cs;
+    ep->rope_period = e->rope_period;
+    ep->rope_cols = e->rope_cols;
+    ep->lo_out = (bf16*)e->lo_out;
+    ep->resid_lo = (const bf16*)e->resid_lo;
+    ep->ld_lo = e->ld_lo;
+  }
+  CC2_REQUIRE(!(ep->flags & CC2_EPI_LO) ||
+                  (ep->lo_out && ((uintptr_t)ep->lo_out & 15u) == 0 && ep->ld_lo % 8 == 0 && ep->ld_lo >= N &&
+                   (!(ep->flags & CC2_EPI_RESID) || (ep->resid_lo && ((uintptr_t)ep->resid_lo & 15u) == 0))),
+              "gemm: lo args (16-byte aligned lo_out and resid_lo, ld_lo >= N and a multiple of 8)");
+  CC2_REQUIRE(!(ep->flags & CC2_EPI_ROPE) ||
+                  (ep->rope_cs && ((uintptr_t)ep->rope_cs & 15u) == 0 && ep->rope_period > 0 && ep->rope_cols % 64 == 0),
+              "gemm: rope args (16-byte aligned table, period > 0, cols multiple of 64)");
+  CC2_REQUIRE(!(ep->flags & CC2_EPI_ROWSCALE) || (ep->ssq_in && e->norm_dim > 0), "gemm: rowscale args");
+  CC2_REQUIRE(!(ep->flags & CC2_EPI_BIAS) || (ep->bias && ((uintptr_t)ep->bias & 15u) == 0),
+              "gemm: bias must be non-null and 16-byte aligned");
+  CC2_REQUIRE(!(ep->flags & CC2_EPI_RESID) || (ep->resid && ((uintptr_t)ep->resid & 15u) == 0 && ep->ld_resid % 8 == 0),
+              "gemm: resid alignment");
+  CC2_REQUIRE(!(ep->flags & CC2_EPI_SSQ) || ep->ssq_out, "gemm: ssq_out null");
+  CC2_REQUIRE(!(ep->flags & (CC2_EPI_SSQ | CC2_EPI_ROWSCALE)) || ep->ssq_ld >= M, "gemm: ssq_ld must be >= M");
+  CC2_REQUIRE(!(ep->flags & CC2_EPI_SPECIAL) || (ep->special && ep->sp_period > 0), "gemm: special args");
   return CC2_OK;
 }
 
@@ -1070,42 +1494,7 @@ int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, in
   CC2_REQUIRE(N % 16 == 0, "gemm(bf16): N must be a multiple of 16 (got %d)", N);
   CC2_REQUIRE(((uintptr_t)out & 15u) == 0 && ldo % 8 == 0, "gemm(bf16): out alignment");
   Epi ep{};
-  ep.flags = e ? e->flags : 0;
-  if (e) {
-    ep.ssq_in = e->ssq_in;
-    ep.ssq_parts = (e->norm_dim + 63) / 64;
-    ep.ssq_ld = e->ssq_ld;
-    ep.inv_dim = e->norm_dim > 0 ? 1.0f / (float)e->norm_dim : 0.0f;
-    ep.eps = e->eps;
-    ep.bias = e->bias;
-    ep.resid = (const bf16*)e->resid;
-    ep.ld_resid = e->ld_resid;
-    ep.ssq_out = e->ssq_out;
-    ep.special = e->special;
-    ep.sp_period = e->special_period;
-    ep.sp_offset = e->special_offset;
-    ep.rope_cs = e->rope_cs;
-    ep.rope_period = e->rope_period;
-    ep.rope_cols = e->rope_cols;
-    ep.lo_out = (bf16*)e->lo_out;
-    ep.resid_lo = (const bf16*)e->resid_lo;
-    ep.ld_lo = e->ld_lo;
-  }
-  CC2_REQUIRE(!(ep.flags & CC2_EPI_LO) ||
-                  (ep.lo_out && ((uintptr_t)ep.lo_out & 15u) == 0 && ep.ld_lo % 8 == 0 && ep.ld_lo >= N &&
-                   (!(ep.flags & CC2_EPI_RESID) || (ep.resid_lo && ((uintptr_t)ep.resid_lo & 15u) == 0))),
-              "gemm: lo args (16-byte aligned lo_out and resid_lo, ld_lo >= N and a multiple of 8)");
-  CC2_REQUIRE(!(ep.flags & CC2_EPI_ROPE) ||
-                  (ep.rope_cs && ((uintptr_t)ep.rope_cs & 15u) == 0 && ep.rope_period > 0 && ep.rope_cols % 64 == 0),
-              "gemm: rope args (16-byte aligned table, period > 0, cols multiple of 64)");
-  CC2_REQUIRE(!(ep.flags & CC2_EPI_ROWSCALE) || (ep.ssq_in && e->norm_dim > 0), "gemm: rowscale args");
-  CC2_REQUIRE(!(ep.flags & CC2_EPI_BIAS) || (ep.bias && ((uintptr_t)ep.bias & 15u) == 0),
-              "gemm: bias must be non-null and 16-byte aligned");
-  CC2_REQUIRE(!(ep.flags & CC2_EPI_RESID) || (ep.resid && ((uintptr_t)ep.resid & 15u) == 0 && ep.ld_resid % 8 == 0),
-              "gemm: resid alignment");
-  CC2_REQUIRE(!(ep.flags & CC2_EPI_SSQ) || ep.ssq_out, "gemm: ssq_out null");
-  CC2_REQUIRE(!(ep.flags & (CC2_EPI_SSQ | CC2_EPI_ROWSCALE)) || ep.ssq_ld >= M, "gemm: ssq_ld must be >= M");
-  CC2_REQUIRE(!(ep.flags & CC2_EPI_SPECIAL) || (ep.special && ep.sp_period > 0), "gemm: special args");
+  CC2_TRY(build_epi(e, M, N, &ep));
   CUtensorMap ma, mb, mc, mr;
   CC2_TRY(make_map(&ma, A, K, M, lda, BM));
   CC2_TRY(make_map_box(&mc, out, N, M, ldo, 64, 32));
@@ -1135,6 +1524,108 @@ int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, in
   }
   CC2_TRY(make_map(&mb, W, K, N, ldw, 128));
   return launch<128>(ma, mb, mc, mr, M, N, K, ep, st);
+}
+
+// ---- layer-persistent forward (see tc::chain) ----------------------------------
+int chain_max_stages() { return tc::chain::kMaxStages; }
+int chain_max_set() { return (tc::chain::C::STAGES * tc::chain::C::STAGE_BYTES) / (3 * 128 + 4) / 16 * 16; }
+
+int chain_begin(int M) {
+  tc::chain::Rec& r = tc::chain::t_rec;
+  CC2_REQUIRE(M > 0, "layer chain: M must be positive");
+  r.p.nstages = 0;
+  r.p.M = M;
+  r.p.bar = nullptr;
+  r.nmaps = 0;
+  r.active = true;
+  return CC2_OK;
+}
+
+void chain_abandon() { tc::chain::t_rec.active = false; }
+
+int chain_add_gemm(const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,
+                   const cc2_epilogue* e) {
+  using namespace tc;
+  chain::Rec& r = chain::t_rec;
+  CC2_REQUIRE(r.active && M == r.p.M, "layer chain: GEMM of %d rows in a chain of %d", M, r.p.M);
+  CC2_REQUIRE(r.p.nstages < chain::kMaxStages, "layer chain: more than %d stages", chain::kMaxStages);
+  CC2_REQUIRE(N > 0 && K > 0 && N % 16 == 0, "layer chain: bad GEMM sizes N=%d K=%d", N, K);
+  CC2_REQUIRE(((uintptr_t)out & 15u) == 0 && ldo % 8 == 0, "gemm(bf16): out alignment");
+  chain::Stage& s = r.p.st[r.p.nstages];
+  s = chain::Stage{};
+  CC2_TRY(build_epi(e, M, N, &s.ep));
+  CUtensorMap ma, mb, mc, mr;
+  CC2_TRY(make_map(&ma, A, K, M, lda, BM));
+  CC2_TRY(make_map(&mb, W, K, N, ldw, chain::BN));
+  CC2_TRY(make_map_box(&mc, out, N, M, ldo, 64, 32));
+  if (s.ep.flags & CC2_EPI_RESID) {
+    CC2_TRY(make_map_box(&mr, s.ep.resid, N, M, s.ep.ld_resid, 64, 32));
+  } else {
+    mr = mc;
+  }
+  s.a = chain::map_index(ma); s.b = chain::map_index(mb); s.c = chain::map_index(mc); s.r = chain::map_index(mr);
+  CC2_REQUIRE(s.a >= 0 && s.b >= 0 && s.c >= 0 && s.r >= 0, "layer chain: more than %d tensor maps",
+              chain::kMaxMaps);
+  s.kind = 0;
+  s.N = N;
+  s.K = K;
+  ++r.p.nstages;
+  return CC2_OK;
+}
+
+int chain_add_attention(const void* qkv, int ld, int qcol, int kcol, int vcol, void* out, int ldo,
+                        const uint8_t* tok, int sets, int S, int heads) {
+  using namespace tc;
+  chain::Rec& r = chain::t_rec;
+  CC2_REQUIRE(r.active && sets * S == r.p.M, "layer chain: attention over %d x %d rows in a chain of %d", sets, S,
+              r.p.M);
+  CC2_REQUIRE(r.p.nstages < chain::kMaxStages, "layer chain: more than %d stages", chain::kMaxStages);
+  CC2_REQUIRE(qkv && out && tok && sets > 0 && heads > 0 && S > 0 && S <= chain_max_set(),
+              "layer chain: attention sets of 1..%d tokens", chain_max_set());
+  CC2_REQUIRE(((uintptr_t)qkv & 15u) == 0 && ((uintptr_t)out & 15u) == 0 && ld % 8 == 0 && ldo % 8 == 0 &&
+                  qcol % 8 == 0 && kcol % 8 == 0 && vcol % 8 == 0,
+              "layer chain: attention operands must be 16-byte aligned");
+  chain::Stage& s = r.p.st[r.p.nstages];
+  s = chain::Stage{};
+  s.kind = 1;
+  s.qkv = (const bf16*)qkv; s.out = (bf16*)out; s.tok = tok;
+  s.ld = ld; s.ldo = ldo; s.qcol = qcol; s.kcol = kcol; s.vcol = vcol;
+  s.sets = sets; s.S = S; s.heads = heads;
+  ++r.p.nstages;
+  return CC2_OK;
+}
+
+// Launches the recorded stages; bar: 16 bytes of device memory for the grid
+// barrier (zeroed here on the stream).
+int chain_launch(unsigned int* bar, cudaStream_t st) {
+  using namespace tc;
+  chain::Rec& r = chain::t_rec;
+  CC2_REQUIRE(r.active, "layer chain: nothing recorded");
+  r.active = false;
+  if (r.p.nstages == 0) return CC2_OK;
+  CC2_REQUIRE(bar && ((uintptr_t)bar & 15u) == 0, "layer chain: barrier word must be 16-byte aligned");
+  r.p.bar = bar;
+  static unsigned long long attr_set = 0;  // one bit per device
+  int dev = 0;
+  CC2_CUDA(cudaGetDevice(&dev));
+  if (dev >= 64 || !((attr_set >> dev) & 1ull)) {
+    CC2_CUDA(cudaFuncSetAttribute(chain::chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, chain::C::SMEM));
+    if (dev < 64) attr_set |= 1ull << dev;
+  }
+  CC2_CUDA(cudaMemsetAsync(bar, 0, 16, st));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(num_sms());
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = chain::C::SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  CC2_CUDA(cudaLaunchKernelEx(&cfg, chain::chain_kernel, r.p));
+  CC2_CHECK_LAUNCH();
+  return CC2_OK;
 }
 
 }  // namespace cc2

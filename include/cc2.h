@@ -65,7 +65,7 @@ CC2_API const char* cc2_version(void);
  * incomplete while the launching call has already returned CC2_OK, so callers
  * that need to know poll this after synchronising (the native bridge and
  * CuteChronos2Model.set_device_checks(True) do). */
-enum { CC2_DEV_GEMM_TIMEOUT = 1, CC2_DEV_ATTN_TIMEOUT = 2 };
+enum { CC2_DEV_GEMM_TIMEOUT = 1, CC2_DEV_ATTN_TIMEOUT = 2, CC2_DEV_LAYER_TIMEOUT = 4 };
 CC2_API int cc2_device_status(int clear);
 
 /* ------------------------------------------------------------------------ */
@@ -157,7 +157,8 @@ enum {
   CC2_K_GEMM_GROUP = 9,     /* group block: Wo.Wv fold (g = 1) or group QKV/O */
   CC2_K_GEMM_FFN_UP = 10,   /* wi (RMSNorm + ReLU)                            */
   CC2_K_GEMM_FFN_DOWN = 11, /* wo + residual                                  */
-  CC2_K_GEMM_IO = 12        /* input / output ResidualBlocks                  */
+  CC2_K_GEMM_IO = 12,       /* input / output ResidualBlocks                  */
+  CC2_K_LAYERS = 13         /* all encoder layers as one layer-persistent launch (cc2_set_layer_chain) */
 };
 CC2_API int cc2_profile_begin(int capacity);
 CC2_API int cc2_profile_read(int* kinds, float* ms, double* flops, double* bytes, int capacity,
@@ -254,7 +255,9 @@ CC2_API int cc2_set_gemm_variant(int variant);
 /* Time-attention kernel choice for bf16 sets (RoPE applied beforehand):
  * 0 (default) = tcgen05 (scores and outputs in TMEM) for 112..144 tokens,
  * the mma.sync kernels otherwise; 1 = the mma.sync kernels only; 2 = tcgen05
- * for every set of 17..144 tokens.  Process-wide; returns the previous value. */
+ * for every set of 17..144 tokens; 3 = the whole-set mma.sync kernel only (the
+ * arithmetic of the layer-persistent forward, see cc2_set_layer_chain).
+ * Process-wide; returns the previous value. */
 CC2_API int cc2_set_attention_variant(int variant);
 
 /* Event trace of the tcgen05 time-attention kernels: with a device buffer of
@@ -275,6 +278,17 @@ CC2_API int cc2_set_attention_trace(void* device_buffer);
  * activations.  0 launches them strictly one after another.  Process-wide;
  * returns the previous value. */
 CC2_API int cc2_set_launch_overlap(int enabled);
+
+/* Layer-persistent forward (default 1): a bf16 forward with at most 384 token
+ * rows (B x S; batch-1 serving), no series groups and no K/V quantiser runs
+ * its encoder layers as ONE cooperative launch of one CTA per SM instead of
+ * six launches per layer: the QKV GEMM, time attention, O-projection, group
+ * block, FFN up and FFN down of every layer are stages separated by a
+ * grid-wide barrier.  Its GEMMs compute exactly what the 128 x 64-tile GEMMs
+ * compute and its attention exactly what the whole-set mma.sync kernel
+ * (cc2_set_attention_variant(3)) computes.  0 launches the layers kernel by
+ * kernel.  Process-wide; returns the previous value. */
+CC2_API int cc2_set_layer_chain(int enabled);
 /* Test hook (no counterpart in the reference): on != 0 arms a one-shot
  * fault-free failure: the next single-SM bf16 GEMM CTA (cc2_gemm with
  * M <= 128) withholds the load of its first k-block (and disarms the hook),
@@ -284,6 +298,20 @@ CC2_API int cc2_set_launch_overlap(int enabled);
  * Exists so that tests can exercise the failure path without a GPU fault;
  * keep it off (0) otherwise.  Applies to the current device. */
 CC2_API int cc2_test_starve_gemm(int on);
+
+/* Test hook, one-shot: CTA 0 of the next layer-persistent launch
+ * (cc2_set_layer_chain) leaves at its first grid barrier without arriving, so
+ * every other CTA's bounded wait there runs out (2 s); they raise
+ * CC2_DEV_LAYER_TIMEOUT, leave their stage loops, free TMEM and return.  For
+ * tests of the failure path without a GPU fault; keep it off (0) otherwise. */
+CC2_API int cc2_test_starve_layer_barrier(int on);
+
+/* Stage trace of the layer-persistent forward: with a device buffer of
+ * 8 x 76 x 2 uint64 (zeroed by the caller), CTAs 0..7 of every later launch
+ * write, for stage s, [cta][s][0] = %globaltimer (ns) when the CTA finished
+ * the stage and [cta][s][1] when the grid barrier after it released the CTA.
+ * NULL turns it off.  Process-wide. */
+CC2_API int cc2_set_layer_trace(void* device_buffer);
 
 /* Event trace of the 2-SM GEMM: with a device buffer of 32 x 8 uint64
  * (zeroed by the caller), CTA 0 of every later launch writes, for its first

@@ -63,3 +63,26 @@ def test_model_device_check_raises_then_recovers():
         lib.cc2_device_status(1)
     again = m(ctx, num_output_patches=2)
     assert torch.equal(again, good)
+
+
+def test_layer_barrier_timeout_sets_status_and_recovers():
+    """The layer-persistent forward's grid barrier: one CTA withholds its
+    arrival (test hook), every other CTA's bounded wait runs out, the launch
+    ends with CC2_DEV_LAYER_TIMEOUT, and the next forward is correct again."""
+    lib = nat.load()
+    m = seeded_init_(CuteChronos2Model(small_config()), seed=0).to(DEV, torch.bfloat16).eval()
+    ctx = torch.randn(1, 300).to(DEV)  # one series: 23 token rows, the layers in one launch
+    good = m(ctx, num_output_patches=3).clone()
+    torch.cuda.synchronize()
+    assert lib.cc2_device_status(1) == 0
+    nat.check(lib.cc2_test_starve_layer_barrier(1), "cc2_test_starve_layer_barrier")
+    try:
+        m(ctx, num_output_patches=3)
+        status = lib.cc2_device_status(1)
+    finally:
+        nat.check(lib.cc2_test_starve_layer_barrier(0), "cc2_test_starve_layer_barrier")
+    assert status == 4  # CC2_DEV_LAYER_TIMEOUT
+    again = m(ctx, num_output_patches=3)
+    torch.cuda.synchronize()
+    assert lib.cc2_device_status(0) == 0
+    assert torch.equal(again, good)

@@ -217,12 +217,71 @@ def test_cuda_graph_replay_equals_eager(small_bf16):
 
 
 def test_batch1_equals_batched(base_bf16, base_weights):
-    """A single series (batch-1 serving, 133 token rows) gives the same
-    forecast, bit for bit, as inside a batch, and stays within the bf16 bar of
-    the oracle."""
+    """A single series (batch-1 serving, 133 token rows) run kernel by kernel
+    gives the same forecast, bit for bit, as inside a batch, and stays within
+    the bf16 bar of the oracle."""
+    from cutechronos_b200 import _native as nat
+    lib = nat.load()
     w = config1(B=8, L=2048)
-    one = base_bf16(w.context[3:4].to(DEV), num_output_patches=4).cpu()
-    batch = base_bf16(w.context.to(DEV), num_output_patches=4).cpu()[3:4]
+    old = lib.cc2_set_layer_chain(0)
+    try:
+        one = base_bf16(w.context[3:4].to(DEV), num_output_patches=4).cpu()
+        batch = base_bf16(w.context.to(DEV), num_output_patches=4).cpu()[3:4]
+    finally:
+        lib.cc2_set_layer_chain(old)
     assert torch.equal(one, batch)
     ref = orc.forward(orc.OracleConfig(), base_weights, w.context[3:4], None, 4)
     assert _report("batch1_bf16_rel", _rel_err(one, ref)) <= 2e-2
+
+
+def _chain_pair(model, ctx, N):
+    """(layer-persistent forward, kernel-by-kernel forward with the same
+    attention arithmetic), both eager."""
+    from cutechronos_b200 import _native as nat
+    lib = nat.load()
+    old_v = lib.cc2_set_attention_variant(3)
+    try:
+        lib.cc2_set_layer_chain(1)
+        a = model(ctx.to(DEV), num_output_patches=N).cpu()
+        lib.cc2_set_layer_chain(0)
+        b = model(ctx.to(DEV), num_output_patches=N).cpu()
+    finally:
+        lib.cc2_set_layer_chain(1)
+        lib.cc2_set_attention_variant(old_v)
+    return a, b
+
+
+# (B, L): 133 token rows (ctx 2048), 2 x 37 rows (ctx 512), 3 x 81 rows with
+# left padding and NaN gaps (token masks), 384 rows (the largest chained M)
+@pytest.mark.parametrize("B,L", [(1, 2048), (2, 512), (3, 1200), (3, 1968)])
+def test_layer_chain_equals_kernel_by_kernel(base_bf16, base_weights, B, L):
+    """The layer-persistent forward (one cooperative launch for all encoder
+    layers) computes the same forecasts, bit for bit, as the per-kernel
+    forward with the same tile GEMMs and attention kernel, and stays within
+    the bf16 bar of the oracle."""
+    w = config1(B=B, L=L)
+    ctx = w.context.clone()
+    if B == 3:
+        ctx[1, : L // 3] = float("nan")  # left padding
+        ctx[2, 100:140] = float("nan")   # a gap inside the context
+    a, b = _chain_pair(base_bf16, ctx, 4)
+    assert torch.equal(a, b)
+    ref = orc.forward(orc.OracleConfig(), base_weights, ctx, None, 4)
+    assert _report(f"layer_chain_B{B}_L{L}_bf16_rel", _rel_err(a, ref)) <= 2e-2
+
+
+def test_layer_chain_small_model_and_graph(small_bf16):
+    """Other model shapes (small config: different d_model / heads / layers),
+    and replay of the cooperative launch from a CUDA graph."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn(2, 300, generator=g)
+    a, b = _chain_pair(small_bf16, x, 3)
+    assert torch.equal(a, b)
+    small_bf16.enable_cuda_graphs(True)
+    try:
+        outs = [small_bf16(x.to(DEV), num_output_patches=3).cpu() for _ in range(3)]
+    finally:
+        small_bf16.enable_cuda_graphs(False)
+    eager = small_bf16(x.to(DEV), num_output_patches=3).cpu()
+    for o in outs:
+        assert torch.equal(o, eager)
