@@ -55,24 +55,26 @@ __device__ __forceinline__ uint32_t swz(uint32_t base, int r, int chunk) {
   return base + (uint32_t)r * 128u + ((uint32_t)(chunk ^ (r & 7)) << 4);
 }
 
-// Query rows [q0, q0 + 16) of a set of n tokens (qb / kb / vb: shared-memory
-// bases of the swizzled tiles, rows up to n rounded to 16 zero-filled; kbias:
-// one bias per key row).  The normalised bf16 output is staged in the tile's
-// own Q rows and handed out as store(row, chunk, 16 bytes) for rows < n.
-template <int KTT, typename Store>
-__device__ __forceinline__ void set_tile(uint32_t qb, uint32_t kb, uint32_t vb, const float* kbias, int n, int q0,
-                                         int lane, Store&& store) {
+// Online softmax of query rows [q0, q0 + 16) over keys [k_lo, k_hi) in key
+// tiles of KTT (qb / kb / vb: shared-memory bases of the swizzled tiles, rows
+// up to the tile ends zero-filled; kbias: one bias per key row).  Leaves the
+// unnormalised output o (m16n8 accumulator layout: rows lane / 4 and
+// lane / 4 + 8, columns 8 dt + 2 (lane % 4) + {0, 1}), the running maxima
+// m0 / m1 (log2 domain) and this lane's partial row sums l0 / l1.
+template <int KTT>
+__device__ __forceinline__ void tile_range(uint32_t qb, uint32_t kb, uint32_t vb, const float* kbias, int k_lo,
+                                           int k_hi, int q0, int lane, float (&o)[8][4], float& m0, float& m1,
+                                           float& l0, float& l1) {
   uint32_t qf[4][4];
 #pragma unroll
   for (int ks = 0; ks < 4; ++ks)
     ldsm_x4(swz(qb, q0 + (lane & 15), 2 * ks + (lane >> 4)), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
-  float o[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.0f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.0f, l1 = 0.0f;
+  m0 = -INFINITY; m1 = -INFINITY; l0 = 0.0f; l1 = 0.0f;
 
-  for (int k0 = 0; k0 < n; k0 += KTT) {
-    const int kvalid = n - k0;
+  for (int k0 = k_lo; k0 < k_hi; k0 += KTT) {
+    const int kvalid = k_hi - k0;
     float s[KTT / 8][4];
 #pragma unroll
     for (int nt = 0; nt < KTT / 8; ++nt) {
@@ -136,6 +138,17 @@ __device__ __forceinline__ void set_tile(uint32_t qb, uint32_t kb, uint32_t vb, 
       }
     }
   }
+}
+
+// Query rows [q0, q0 + 16) of a set of n tokens over all its keys (tiles of
+// KTT), normalised; the bf16 output is staged in the tile's own Q rows and
+// handed out as store(row, chunk, 16 bytes) for rows < n.
+template <int KTT, typename Store>
+__device__ __forceinline__ void set_tile(uint32_t qb, uint32_t kb, uint32_t vb, const float* kbias, int n, int q0,
+                                         int lane, Store&& store) {
+  float o[8][4];
+  float m0, m1, l0, l1;
+  tile_range<KTT>(qb, kb, vb, kbias, 0, n, q0, lane, o, m0, m1, l0, l1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
   l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
   l1 += __shfl_xor_sync(0xffffffffu, l1, 1);

@@ -104,10 +104,13 @@ int chain_add_gemm(const void* A, int lda, const void* W, int ldw, void* out, in
                    const cc2_epilogue* e);
 int chain_add_attention(const void* qkv, int ld, int qcol, int kcol, int vcol, void* out, int ldo,
                         const uint8_t* tok, int sets, int S, int heads);
-int chain_launch(unsigned int* bar, cudaStream_t st);
-// 1 (default): the encoder layers of a bf16 forward with few token rows run as
-// one layer-persistent kernel (cc2_set_layer_chain)
-int g_layer_chain = 1;
+int chain_launch(void* scratch, size_t scratch_bytes, int exact, cudaStream_t st);
+size_t chain_scratch_bytes();
+// 1: the encoder layers of a bf16 forward with few token rows run as one
+// layer-persistent kernel; 2: the same in its exact mode; 0 (default): kernel
+// by kernel - the persistent launch measured no faster (cc2_set_layer_chain)
+int g_layer_chain = 0;
+constexpr int kChainMaxRows = 384;  // token rows (B x S) up to which the layers run as one launch
 int launch_gemm_f32(const void*, int, const void*, int, void*, int, int, int, int, const cc2_epilogue*,
                     cudaStream_t, float* scratch = nullptr, size_t scratch_floats = 0);
 int launch_attention(int, int, const void*, int, int, int, int, void*, int, const uint8_t*, int, int, int, int,
@@ -342,7 +345,7 @@ struct Workspace {
   char* XLO; char* ALO;  // bf16: low halves of the residual stream X and of its alternate buffer ATT
   int32_t* members; int32_t* offsets; char* O; char* PRED;
   float* splitk; size_t splitk_floats;  // fp32 mode: K-slice partial sums of the small-M GEMMs
-  unsigned int* chain_bar;              // grid barrier of the layer-persistent forward
+  char* chain; size_t chain_bytes;      // layer-persistent forward: barrier, split-K counters and partials
 };
 
 size_t plan_ws(const cc2_model& m, int B, int L, int N, Workspace* w, char* base) {
@@ -364,7 +367,9 @@ size_t plan_ws(const cc2_model& m, int B, int L, int N, Workspace* w, char* base
   size_t oSPLIT = p.take(4 * splitk_floats);
   const size_t lo_bytes = m.dtype == CC2_BF16 ? e * align_up(M, 32) * d : 0;  // 32-row interleaved
   size_t oXLO = p.take(lo_bytes), oALO = p.take(lo_bytes);
-  size_t oBAR = p.take(16);
+  // the layer-persistent forward's scratch, for the forwards that may use it
+  const size_t chain_bytes = (m.dtype == CC2_BF16 && M <= (size_t)kChainMaxRows) ? chain_scratch_bytes() : 0;
+  size_t oCHAIN = p.take(chain_bytes);
   if (w && base) {
     w->E = base + oE; w->X = base + oX; w->QKV = base + oQKV; w->ATT = base + oATT;
     w->ssq = (float*)(base + oSSQ); w->tok = (uint8_t*)(base + oTOK);
@@ -373,7 +378,8 @@ size_t plan_ws(const cc2_model& m, int B, int L, int N, Workspace* w, char* base
     w->O = base + oO; w->PRED = base + oPRED;
     w->splitk = (float*)(base + oSPLIT); w->splitk_floats = splitk_floats;
     w->XLO = lo_bytes ? base + oXLO : nullptr; w->ALO = lo_bytes ? base + oALO : nullptr;
-    w->chain_bar = (unsigned int*)(base + oBAR);
+    w->chain = chain_bytes ? base + oCHAIN : nullptr;
+    w->chain_bytes = chain_bytes;
   }
   return p.off;
 }
@@ -405,11 +411,11 @@ struct ChainScope {
     if (on) chain_abandon();
     t_chain_rec = false;
   }
-  int launch(unsigned int* bar, double flops, cudaStream_t st) {
+  int launch(void* scratch, size_t bytes, double flops, cudaStream_t st) {
     t_chain_rec = false;
     on = false;
     ProfScope ps_(CC2_K_LAYERS, flops, 0.0, st);
-    return chain_launch(bar, st);
+    return chain_launch(scratch, bytes, g_layer_chain == 2, st);
   }
 };
 
@@ -686,7 +692,8 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
   bool kvq_on = false;
   for (const auto& q : m->kvq) kvq_on = kvq_on || q.has_k || q.has_v;
   const bool chain = lo && g_layer_chain && g_gemm_variant == 0 && max_group == 1 && !kvq_on && c.d_kv == 64 &&
-                     M <= 384 && S <= chain_max_set() && 6 * c.num_layers <= chain_max_stages();
+                     M <= kChainMaxRows && w.chain && S <= chain_max_set() &&
+                     6 * c.num_layers <= chain_max_stages();
   ChainScope chain_scope(chain, M);
   for (int l = 0; l < c.num_layers; ++l) {
     const cc2_layer_pack& Lw = m->layers[l];
@@ -768,7 +775,7 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
   }
   if (chain_scope.on) {
     const double per_layer = 2.0 * M * (5.0 * d * d + 2.0 * d * dff) + 4.0 * B * (double)S * S * d;
-    CC2_TRY(chain_scope.launch(w.chain_bar, per_layer * c.num_layers, st));
+    CC2_TRY(chain_scope.launch(w.chain, w.chain_bytes, per_layer * c.num_layers, st));
   }
   (void)KE;
   // final RMSNorm of the N future rows -> O[:, dff:]
@@ -910,7 +917,7 @@ int cc2_test_starve_layer_barrier(int on) {
 
 int cc2_set_layer_chain(int enabled) {
   const int old = g_layer_chain;
-  g_layer_chain = enabled ? 1 : 0;
+  g_layer_chain = (enabled == 1 || enabled == 2) ? enabled : 0;
   return old;
 }
 

@@ -27,6 +27,7 @@
 // DEV_ERR_GEMM_TIMEOUT, all roles leave their loops, TMEM is freed and the
 // kernel returns.
 #include <cuda.h>
+#include <algorithm>
 #include <cstring>
 #include <mutex>
 
@@ -1071,9 +1072,20 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
 // keep their ring and accumulator phases across stages.
 //
 // Each GEMM stage is the 1-SM 128 x 64 tile GEMM above (same MMAs, same
-// epilogue functions), so its results equal those of gemm_tc_kernel<64>; the
-// time-attention stage runs aset::set_tile, the body of the whole-set
-// attention kernel, so it equals that kernel (attention variant 3).
+// epilogue functions); stages with a long k-loop and few tiles split it over
+// 2 or 4 CTAs whose fp32 partials are summed in split order.  The time
+// attention gives each CTA one 16-row query tile and splits the keys over
+// its warps (softmax states merged in warp order).  In exact mode (no split,
+// attention by aset::set_tile, the body of the whole-set attention kernel)
+// the results equal those of the per-kernel forward with gemm_tc_kernel<64>
+// and attention variant 3, bit for bit.
+//
+// Measured at batch 1 (133 token rows) a stage costs ~10 us (K = 768) - the
+// first load ~0.7 us, the k-loop at one SM's TMA rate (~0.3 us per 24 KB
+// k-block), the epilogue ~2.3 us (one warp per 64 columns), the grid barrier
+// ~1.5 us - so the launch is about as fast as the per-kernel forward, whose
+// programmatic launches already overlapped the same latencies; it is off by
+// default (cc2_set_layer_chain).
 //
 // Coherence inside the kernel: activations written by one stage are read by
 // other SMs in the next, so loads that could hit a stale L1 line go through
@@ -1091,12 +1103,17 @@ using C = Cfg<BN>;
 constexpr int kMaxMaps = 72;
 constexpr int kMaxStages = 76;
 constexpr int kWarps = kThreads / 32;
+constexpr int SMEM = C::SMEM + 512;  // + the current stage's descriptor
 
 struct Stage {
   Epi ep;
   int kind;  // 0: GEMM, 1: time attention
   int N, K;
   int a, b, c, r;  // tensor-map indices (GEMM)
+  const void* w;    // GEMM: the weight matrix (contiguous, prefetched into L2 one stage ahead)
+  unsigned long long wbytes;
+  int split;        // GEMM: k-ranges per tile (1, 2 or 4)
+  int cnt_off;      // GEMM with split > 1: this stage's partial counters (tiles x 4) in cnt
   const bf16* qkv;  // attention: [sets * S, ld] rows with Q, K, V column blocks
   bf16* out;
   const uint8_t* tok;
@@ -1107,9 +1124,13 @@ struct Params {
   CUtensorMap maps[kMaxMaps];
   Stage st[kMaxStages];
   int nstages, M;
-  unsigned int* bar;  // [0] arrivals, [1] generation, [2] abort (zeroed before the launch)
+  int exact;          // 1: no split-K, attention as aset::set_tile (the per-kernel forward's arithmetic)
+  unsigned int* bar;  // [0] arrivals (monotonic), [2] abort (zeroed before the launch)
+  unsigned int* cnt;  // split-K partial counters (zeroed before the launch)
+  float* part;        // split-K partials: [unit][4][16][32] float4 (grid x 32 KB)
 };
 static_assert(sizeof(Params) <= 32000, "kernel parameter block too large");
+static_assert(sizeof(Stage) <= 448, "stage descriptor must fit its shared-memory slot");
 
 __device__ __forceinline__ void fence_proxy_async_all() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -1127,11 +1148,23 @@ __device__ __forceinline__ unsigned ld_acquire(const unsigned* p) {
 constexpr int kTraceCtas = 8;
 __device__ unsigned long long* g_chain_trace = nullptr;
 
+// Copies a stage descriptor from the parameter block into shared memory (all
+// threads but 0 take part): the roles then read their arguments from shared
+// memory instead of through the constant cache, which a 26 KB parameter block
+// overflows.
+__device__ __forceinline__ void copy_stage(Stage* dst, const Stage* src) {
+  const uint32_t* a = reinterpret_cast<const uint32_t*>(src);
+  uint32_t* b = reinterpret_cast<uint32_t*>(dst);
+  for (int i = (int)threadIdx.x - 1; i >= 0 && i < (int)(sizeof(Stage) / 4); i += blockDim.x - 1) b[i] = a[i];
+}
+
 // Grid-wide barrier (all threads of every CTA call it).  False: abort.
-__device__ __noinline__ bool grid_sync(unsigned* bar, volatile int* abort_flag, int si) {
+// next: the following stage, copied into sst while thread 0 waits.
+__device__ __noinline__ bool grid_sync(unsigned* bar, volatile int* abort_flag, int si, const Stage* next,
+                                       Stage* sst) {
   fence_proxy_async_all();
-  __threadfence();
-  __syncthreads();
+  __syncthreads();  // then thread 0's fence makes the CTA's writes visible before its arrival
+  copy_stage(sst, next);
   unsigned long long* tr = g_chain_trace;
   if (tr && threadIdx.x == 0 && blockIdx.x < kTraceCtas)
     tr[((size_t)blockIdx.x * kMaxStages + si) * 2] = globaltimer_ns();
@@ -1140,15 +1173,13 @@ __device__ __noinline__ bool grid_sync(unsigned* bar, volatile int* abort_flag, 
     if (ok && blockIdx.x == 0 && *(volatile int*)&g_chain_starve && atomicExch(&g_chain_starve, 0)) {
       *abort_flag = 1;  // test hook: this CTA never arrives, so the others' bounded waits run out
     } else if (ok) {
-      const unsigned gen = ld_acquire(bar + 1);
-      if (atomicAdd(bar, 1u) == gridDim.x - 1) {
-        atomicExch(bar, 0u);
-        __threadfence();
-        atomicAdd(bar + 1, 1u);
-      } else {
+      // barrier k (after stage k) completes when (k + 1) x gridDim arrivals are counted
+      const unsigned target = (unsigned)(si + 1) * gridDim.x;
+      __threadfence();
+      if (atomicAdd(bar, 1u) + 1u < target) {
         const unsigned long long t0 = globaltimer_ns();
         for (uint32_t n = 1;; ++n) {
-          if (ld_acquire(bar + 1) != gen) break;
+          if (ld_acquire(bar) >= target) break;
           if ((n & 15u) == 0) {
             if (*(volatile unsigned*)(bar + 2)) { ok = false; break; }
             if (globaltimer_ns() - t0 > kWaitLimitNs) {
@@ -1179,6 +1210,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
   uint64_t* bars = (uint64_t*)(epi_smem + 8 * kEpiBox);
   uint32_t* tmem_slot = (uint32_t*)(bars + 2 * C::STAGES + 12);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  Stage* sst = (Stage*)(((uintptr_t)(tmem_slot + 2) + 15) & ~(uintptr_t)15);  // the current stage
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -1202,6 +1234,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
     *abort_flag = 0;
     fence_mbar_init();
   }
+  copy_stage(sst, &p.st[0]);
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
     tmem_relinquish();
@@ -1219,12 +1252,41 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
   int eit = 0; uint32_t use = 0, rphase = 0;        // epilogue tiles, residual boxes
 
   for (int si = 0; si < p.nstages; ++si) {
-    const Stage& s = p.st[si];
+    const Stage& s = *sst;
+    if (warp == 1 && lane == 1 && si + 1 < p.nstages && p.st[si + 1].kind == 0) {
+      // the next GEMM's weights into L2 (each CTA a slice) and its tensor maps
+      // into the descriptor cache, while this stage runs
+      const Stage& nx = p.st[si + 1];
+      const unsigned long long slice = ((nx.wbytes + gridDim.x - 1) / gridDim.x + 255) & ~255ull;
+      const unsigned long long lo = slice * blockIdx.x;
+      const unsigned long long hi = lo + slice < nx.wbytes ? lo + slice : nx.wbytes;
+      for (unsigned long long o = lo; o < hi; o += 16384) {
+        const unsigned n = (unsigned)(hi - o < 16384 ? hi - o : 16384);
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"((const char*)nx.w + o), "r"(n) : "memory");
+      }
+      tma_prefetch_desc(&p.maps[nx.a]);
+      tma_prefetch_desc(&p.maps[nx.b]);
+      tma_prefetch_desc(&p.maps[nx.c]);
+      tma_prefetch_desc(&p.maps[nx.r]);
+    }
     if (s.kind == 0) {
+      // Work units: tile x split.  With split S > 1 the tile's k-blocks are
+      // divided into S ranges on S CTAs; each unit's epilogue warp q either
+      // writes its fp32 partial of rows 32q..32q+31 to the scratch and counts
+      // it (q % S != split), or (q % S == split) waits for the other S - 1
+      // partials of those rows, sums all S in split order and runs the
+      // epilogue.  Units never exceed the grid, so all of a tile's units are
+      // resident at once.
+      unsigned long long* ktr = nullptr;
+      if (g_chain_trace && blockIdx.x == 0 && (si == 2 || si == 4))
+        ktr = g_chain_trace + (size_t)kTraceCtas * kMaxStages * 2 + (si == 4 ? 160 : 0);
+      if (ktr && threadIdx.x == 0) ktr[131] = globaltimer_ns();
       const int N = s.N;
       const int n_tiles = (N + BN - 1) / BN;
-      const int num_tiles = m_tiles * n_tiles;
+      const int S = s.split;
+      const int num_units = m_tiles * n_tiles * S;
       const int kblocks = (s.K + BK - 1) / BK;
+      const int kpb = (kblocks + S - 1) / S;  // k-blocks per split
       const CUtensorMap* tmA = &p.maps[s.a];
       const CUtensorMap* tmB = &p.maps[s.b];
       const CUtensorMap* tmC = &p.maps[s.c];
@@ -1232,10 +1294,13 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
       if (warp == 0) {
         if (lane == 0) {
           bool ok = true;
-          for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+          for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+            const int tile = u / S, sp = u % S;
             const int mt = tile / n_tiles, nt = tile % n_tiles;
-            for (int kb = 0; kb < kblocks; ++kb) {
+            const int kb1 = min(kblocks, (sp + 1) * kpb);
+            for (int kb = sp * kpb; kb < kb1; ++kb) {
               if (!mbar_wait(empty_bar(pstage), pphase ^ 1u, abort_flag)) { ok = false; break; }
+              if (ktr && u == (int)blockIdx.x && kb < 64) ktr[kb] = globaltimer_ns();
               const uint32_t sa = smem_u32(smem + pstage * C::STAGE_BYTES);
               mbar_arrive_expect_tx(full_bar(pstage), C::STAGE_BYTES);
               tma_load_2d(sa, tmA, full_bar(pstage), kb * BK, mt * BM);
@@ -1249,20 +1314,24 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
         if (lane == 0) {
           constexpr uint32_t idesc = idesc_bf16<BN>();
           bool ok = true;
-          for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++mit) {
+          for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++mit) {
+            const int sp = u % S;
+            const int kb0 = sp * kpb, kb1 = min(kblocks, (sp + 1) * kpb);
             const int acc = mit & 1;
             const uint32_t acc_phase = (uint32_t)(mit >> 1) & 1u;
             if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) break;
             tc_fence_after();
             const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-            for (int kb = 0; kb < kblocks; ++kb) {
+            for (int kb = kb0; kb < kb1; ++kb) {
               if (!mbar_wait(full_bar(mstage), mphase, abort_flag)) { ok = false; break; }
+              if (ktr && u == (int)blockIdx.x && kb < 64) ktr[64 + kb] = globaltimer_ns();
               tc_fence_after();
               const uint32_t sa = smem_u32(smem + mstage * C::STAGE_BYTES);
               const uint32_t sb = sa + C::A_BYTES;
 #pragma unroll
               for (int k = 0; k < BK / 16; ++k)
-                mma_bf16(d_tmem, sw128_desc(sa + 32u * k), sw128_desc(sb + 32u * k), idesc, (kb | k) != 0 ? 1u : 0u);
+                mma_bf16(d_tmem, sw128_desc(sa + 32u * k), sw128_desc(sb + 32u * k), idesc,
+                         (kb != kb0 || k != 0) ? 1u : 0u);
               mma_commit(empty_bar(mstage));
               if (++mstage == C::STAGES) { mstage = 0; mphase ^= 1u; }
             }
@@ -1276,45 +1345,113 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
         const int q = warp & 3;
         const bool resid = (ep.flags & CC2_EPI_RESID) != 0;
         const uint32_t box0 = smem_u32(epi_smem + (size_t)q * 2 * kEpiBox);
-        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++eit, ++use) {
+        bool aborted = false;
+        for (int u = blockIdx.x; u < num_units && !aborted; u += gridDim.x, ++eit) {
+          const int tile = u / S, sp = u % S;
           const int mt = tile / n_tiles, nt = tile % n_tiles;
           const int row0 = mt * BM + q * 32;
           const int col0 = nt * BN;
+          const bool mine = (q % S) == sp;  // this warp finishes rows 32q.. of the tile
           const int b = use & 1;
           const uint32_t box = box0 + b * kEpiBox;
-          if (lane == 0) {
-            bulk_wait_read0();  // the store that last used this box has read it
-            if (resid) {
-              mbar_arrive_expect_tx(rbar(q, b), kEpiBox);
-              tma_load_2d(box, tmR, rbar(q, b), col0, row0);
-            }
-          }
-          __syncwarp();
           const int row = row0 + lane;
           const bool row_ok = row < M;
-          const float rs = row_scale<true>(ep, ep.flags, row, row_ok);
-          const bool special = (ep.flags & CC2_EPI_SPECIAL) && row_ok && (row % ep.sp_period) == ep.sp_offset;
-          const bool rope_tile = (ep.flags & CC2_EPI_ROPE) && col0 < ep.rope_cols;
+          float rs = 1.0f;
+          bool special = false, rope_tile = false;
           uint32_t cs[32];
-          if (rope_tile) load_rope_row(ep, row, row_ok, cs);
           uint4 rl[8];
-          if ((ep.flags & CC2_EPI_LO) && resid) load_lo_group<true>(rl, ep, row, row_ok, col0, N);
+          if (mine) {
+            if (ktr && q == 2 && lane == 0 && u == (int)blockIdx.x) ktr[135] = globaltimer_ns();
+            if (lane == 0) {
+              bulk_wait_read0();  // the store that last used this box has read it
+              if (resid) {
+                mbar_arrive_expect_tx(rbar(q, b), kEpiBox);
+                tma_load_2d(box, tmR, rbar(q, b), col0, row0);
+              }
+            }
+            __syncwarp();
+            rs = row_scale<true>(ep, ep.flags, row, row_ok);
+            special = (ep.flags & CC2_EPI_SPECIAL) && row_ok && (row % ep.sp_period) == ep.sp_offset;
+            rope_tile = (ep.flags & CC2_EPI_ROPE) && col0 < ep.rope_cols;
+            if (rope_tile) load_rope_row(ep, row, row_ok, cs);
+            if ((ep.flags & CC2_EPI_LO) && resid) load_lo_group<true>(rl, ep, row, row_ok, col0, N);
+          }
           const int acc = eit & 1;
           const uint32_t acc_phase = (uint32_t)(eit >> 1) & 1u;
           if (!mbar_wait(tfull_bar(acc), acc_phase, abort_flag)) break;
+          if (ktr && q == 2 && lane == 0 && u == (int)blockIdx.x) ktr[128] = globaltimer_ns();
           tc_fence_after();
           const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN);
           uint32_t r[64];
           tmem_ld32(tbase, r);
           tmem_ld32(tbase + 32, r + 32);
           tmem_ld_wait();
+          if (ktr && q == 2 && lane == 0 && u == (int)blockIdx.x) ktr[132] = globaltimer_ns();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(tempty_bar(acc));  // accumulator is in registers
+          if (S > 1) {
+            // partial of rows 32q..32q+31: [unit][q][16 float4 columns][32 rows] (coalesced)
+            unsigned* cnt = p.cnt + s.cnt_off + tile * 4 + q;
+            if (!mine) {
+              float4* dst = reinterpret_cast<float4*>(p.part) + ((size_t)u * 4 + q) * 16 * 32 + lane;
+#pragma unroll
+              for (int c4 = 0; c4 < 16; ++c4)
+                __stcg(dst + c4 * 32, make_float4(__uint_as_float(r[4 * c4]), __uint_as_float(r[4 * c4 + 1]),
+                                                  __uint_as_float(r[4 * c4 + 2]), __uint_as_float(r[4 * c4 + 3])));
+              __syncwarp();
+              if (lane == 0) {
+                __threadfence();
+                atomicAdd(cnt, 1u);
+              }
+              __syncwarp();
+              continue;
+            }
+            // wait for the other S - 1 partials of these rows, then sum all S in split order
+            if (lane == 0) {
+              const unsigned long long t0 = globaltimer_ns();
+              for (uint32_t n = 1;; ++n) {
+                if (ld_acquire(cnt) >= (unsigned)(S - 1)) break;
+                if ((n & 15u) == 0) {
+                  if (*abort_flag || *(volatile unsigned*)(p.bar + 2)) { *abort_flag = 1; break; }
+                  if (globaltimer_ns() - t0 > kWaitLimitNs) {
+                    atomicOr(&g_dev_error, DEV_ERR_LAYER_TIMEOUT);
+                    atomicExch(p.bar + 2, 1u);
+                    *abort_flag = 1;
+                    break;
+                  }
+                }
+              }
+            }
+            __syncwarp();
+            if (*abort_flag) { aborted = true; break; }
+            float sum[64];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) sum[j] = 0.0f;
+            for (int o = 0; o < S; ++o) {
+              if (o == sp) {
+#pragma unroll
+                for (int j = 0; j < 64; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(r[j]));
+              } else {
+                const float4* src = reinterpret_cast<const float4*>(p.part) + ((size_t)(tile * S + o) * 4 + q) * 16 * 32 + lane;
+#pragma unroll
+                for (int c4 = 0; c4 < 16; ++c4) {
+                  const float4 v = __ldcg(src + c4 * 32);
+                  sum[4 * c4] = __fadd_rn(sum[4 * c4], v.x);
+                  sum[4 * c4 + 1] = __fadd_rn(sum[4 * c4 + 1], v.y);
+                  sum[4 * c4 + 2] = __fadd_rn(sum[4 * c4 + 2], v.z);
+                  sum[4 * c4 + 3] = __fadd_rn(sum[4 * c4 + 3], v.w);
+                }
+              }
+            }
+#pragma unroll
+            for (int j = 0; j < 64; ++j) r[j] = __float_as_uint(sum[j]);
+          }
           if (resid) {
             if (!mbar_wait(rbar(q, b), (rphase >> b) & 1u, abort_flag)) break;
             rphase ^= 1u << b;
           }
+          if (ktr && q == 2 && lane == 0 && u == (int)blockIdx.x) ktr[133] = globaltimer_ns();
           float rsg = rs;
           if (rope_tile) {
             rope_group(r, cs, rs);
@@ -1322,15 +1459,111 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
           }
           const float ssq = epilogue_group(ep, ep.flags, r, rsg, special, col0, N, box, lane, resid, row, row_ok, rl);
           if ((ep.flags & CC2_EPI_SSQ) && row_ok) ep.ssq_out[(size_t)(col0 >> 6) * ep.ssq_ld + row] = ssq;
+          if (ktr && q == 2 && lane == 0 && u == (int)blockIdx.x) ktr[134] = globaltimer_ns();
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
             tma_store_2d(tmC, box, col0, row0);
             bulk_commit();
           }
+          ++use;
+          if (ktr && q == 2 && lane == 0 && u == (int)blockIdx.x) ktr[129] = globaltimer_ns();
         }
         if (lane == 0) bulk_wait_all();  // this stage's outputs are in global memory
+        if (ktr && q == 2 && lane == 0) ktr[130] = globaltimer_ns();
         __syncwarp();
+      }
+    } else if (!p.exact) {
+      // time attention: items (set, head, 16-row query tile); the CTA's warps
+      // split the keys (chunks of kc, a multiple of 32) and their partial
+      // softmax states are merged in a fixed order
+      const int n = s.S;
+      const int npad = (n + 15) & ~15;
+      const int nqt = npad / 16;
+      const int kc = (((n + kWarps - 1) / kWarps) + 31) & ~31;
+      const int nkc = (n + kc - 1) / kc;
+      const int items = s.sets * s.heads * nqt;
+      const uint32_t qb = smem_u32(smem);
+      const uint32_t kb = qb + 16u * 128u;
+      const uint32_t vb = kb + (uint32_t)npad * 128u;
+      float* kbias = reinterpret_cast<float*>(smem + 2048 + (size_t)npad * 256);
+      float* mo = kbias + npad;                    // [kWarps][16][64] unnormalised outputs
+      float2* mm = reinterpret_cast<float2*>(mo + kWarps * 16 * 64);  // [kWarps][16] (max, sum)
+      for (int item = blockIdx.x; item < items; item += gridDim.x) {
+        const int set = item / (s.heads * nqt);
+        const int h = (item / nqt) % s.heads;
+        const int qt = item % nqt;
+        const size_t row0 = (size_t)set * n;
+        for (int idx = threadIdx.x; idx < npad * 8; idx += blockDim.x) {
+          const int rr = idx >> 3, c = idx & 7;
+          const int qr = rr - qt * 16;  // row of the Q tile, if any
+          if (rr < n) {
+            const bf16* src = s.qkv + (row0 + rr) * s.ld + c * 8;
+            if (qr >= 0 && qr < 16) aset::cp_async16(aset::swz(qb, qr, c), src + s.qcol + h * 64);
+            aset::cp_async16(aset::swz(kb, rr, c), src + s.kcol + h * 64);
+            aset::cp_async16(aset::swz(vb, rr, c), src + s.vcol + h * 64);
+          } else {
+            const uint4 z = make_uint4(0, 0, 0, 0);
+            if (qr >= 0 && qr < 16) *reinterpret_cast<uint4*>(smem + (aset::swz(qb, qr, c) - qb)) = z;
+            *reinterpret_cast<uint4*>(smem + (aset::swz(kb, rr, c) - qb)) = z;
+            *reinterpret_cast<uint4*>(smem + (aset::swz(vb, rr, c) - qb)) = z;
+          }
+        }
+        for (int rr = threadIdx.x; rr < npad; rr += blockDim.x)
+          kbias[rr] = rr < n ? (s.tok[row0 + rr] ? 0.0f : aset::kMaskedScore) : -INFINITY;
+        aset::cp_async_wait_all();
+        __syncthreads();
+        if (warp < nkc) {
+          float o[8][4];
+          float m0, m1, l0, l1;
+          const int k_lo = warp * kc;
+          aset::tile_range<32>(qb, kb, vb, kbias, k_lo, min(n, k_lo + kc), 0, lane, o, m0, m1, l0, l1);
+          l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
+          l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
+          l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
+          l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
+          const int r0 = lane >> 2;
+          float* mw = mo + warp * 16 * 64;
+#pragma unroll
+          for (int dt = 0; dt < 8; ++dt) {
+            const int c = dt * 8 + 2 * (lane & 3);
+            *reinterpret_cast<float2*>(mw + r0 * 64 + c) = make_float2(o[dt][0], o[dt][1]);
+            *reinterpret_cast<float2*>(mw + (r0 + 8) * 64 + c) = make_float2(o[dt][2], o[dt][3]);
+          }
+          if ((lane & 3) == 0) {
+            mm[warp * 16 + r0] = make_float2(m0, l0);
+            mm[warp * 16 + r0 + 8] = make_float2(m1, l1);
+          }
+        }
+        __syncthreads();
+        if (threadIdx.x < 128) {
+          const int row = threadIdx.x >> 3, c = threadIdx.x & 7;
+          float mx = -INFINITY;
+          for (int w = 0; w < nkc; ++w) mx = fmaxf(mx, mm[w * 16 + row].x);
+          float l = 0.0f, acc[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+          for (int w = 0; w < nkc; ++w) {
+            const float2 ml = mm[w * 16 + row];
+            const float f = exp2f(ml.x - mx);
+            l = __fmaf_rn(ml.y, f, l);
+            const float4 a = *reinterpret_cast<const float4*>(mo + (w * 16 + row) * 64 + c * 8);
+            const float4 b = *reinterpret_cast<const float4*>(mo + (w * 16 + row) * 64 + c * 8 + 4);
+            acc[0] = __fmaf_rn(a.x, f, acc[0]); acc[1] = __fmaf_rn(a.y, f, acc[1]);
+            acc[2] = __fmaf_rn(a.z, f, acc[2]); acc[3] = __fmaf_rn(a.w, f, acc[3]);
+            acc[4] = __fmaf_rn(b.x, f, acc[4]); acc[5] = __fmaf_rn(b.y, f, acc[5]);
+            acc[6] = __fmaf_rn(b.z, f, acc[6]); acc[7] = __fmaf_rn(b.w, f, acc[7]);
+          }
+          const float il = 1.0f / l;
+          const int qrow = qt * 16 + row;
+          if (qrow < n) {
+            uint4 v;
+            v.x = pack_bf16(acc[0] * il, acc[1] * il); v.y = pack_bf16(acc[2] * il, acc[3] * il);
+            v.z = pack_bf16(acc[4] * il, acc[5] * il); v.w = pack_bf16(acc[6] * il, acc[7] * il);
+            *reinterpret_cast<uint4*>(s.out + (row0 + qrow) * s.ldo + h * 64 + c * 8) = v;
+          }
+        }
+        __syncthreads();
       }
     } else {
       // time attention: items (set, head, chunk of up to kWarps query tiles);
@@ -1344,6 +1577,8 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
       const uint32_t kb = qb + (uint32_t)npad * 128u;
       const uint32_t vb = kb + (uint32_t)npad * 128u;
       float* kbias = reinterpret_cast<float*>(smem + (size_t)npad * 384);
+      if (g_chain_trace && blockIdx.x == 0 && si == 1 && threadIdx.x == 0)
+        g_chain_trace[(size_t)kTraceCtas * kMaxStages * 2 + 327] = globaltimer_ns();
       for (int item = blockIdx.x; item < items; item += gridDim.x) {
         const int set = item / (s.heads * chunks);
         const int h = (item / chunks) % s.heads;
@@ -1369,15 +1604,19 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
           kbias[rr] = rr < n ? (s.tok[row0 + rr] ? 0.0f : aset::kMaskedScore) : -INFINITY;
         aset::cp_async_wait_all();
         __syncthreads();
+        unsigned long long* atr = (g_chain_trace && blockIdx.x == 0 && si == 1 && item == (int)blockIdx.x)
+                                      ? g_chain_trace + (size_t)kTraceCtas * kMaxStages * 2 + 320 : nullptr;
+        if (atr && threadIdx.x == 0) atr[0] = globaltimer_ns();
         const int q0 = q_lo + warp * 16;
         if (q0 < n)
           aset::set_tile<64>(qb, kb, vb, kbias, n, q0, lane, [&](int rr, int c, const uint4& v) {
             *reinterpret_cast<uint4*>(s.out + (row0 + rr) * s.ldo + h * 64 + c * 8) = v;
           });
+        if (atr && lane == 0) atr[1 + warp] = globaltimer_ns();
         __syncthreads();
       }
     }
-    if (si + 1 < p.nstages && !grid_sync(p.bar, abort_flag, si)) break;
+    if (si + 1 < p.nstages && !grid_sync(p.bar, abort_flag, si, &p.st[si + 1], sst)) break;
   }
 
   tc_fence_before();
@@ -1528,7 +1767,12 @@ int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, in
 
 // ---- layer-persistent forward (see tc::chain) ----------------------------------
 int chain_max_stages() { return tc::chain::kMaxStages; }
-int chain_max_set() { return (tc::chain::C::STAGES * tc::chain::C::STAGE_BYTES) / (3 * 128 + 4) / 16 * 16; }
+int chain_max_set() {
+  const int ring = tc::chain::C::STAGES * tc::chain::C::STAGE_BYTES;
+  const int whole_set = ring / (3 * 128 + 4);  // exact mode: Q, K, V, bias of the whole set
+  const int split = (ring - 2048 - tc::chain::kWarps * 16 * (64 * 4 + 8)) / (2 * 128 + 4);  // split-key mode
+  return std::min(whole_set, split) / 16 * 16;
+}
 
 int chain_begin(int M) {
   tc::chain::Rec& r = tc::chain::t_rec;
@@ -1569,6 +1813,8 @@ int chain_add_gemm(const void* A, int lda, const void* W, int ldw, void* out, in
   s.kind = 0;
   s.N = N;
   s.K = K;
+  s.w = W;
+  s.wbytes = (ldw == K && (K * 2) % 16 == 0) ? (unsigned long long)N * K * 2 : 0;  // contiguous only
   ++r.p.nstages;
   return CC2_OK;
 }
@@ -1595,28 +1841,63 @@ int chain_add_attention(const void* qkv, int ld, int qcol, int kcol, int vcol, v
   return CC2_OK;
 }
 
-// Launches the recorded stages; bar: 16 bytes of device memory for the grid
-// barrier (zeroed here on the stream).
-int chain_launch(unsigned int* bar, cudaStream_t st) {
+// Device scratch of a layer-persistent launch over M token rows: barrier
+// word, split-K counters, split-K partials.
+size_t chain_scratch_bytes() {
+  const size_t counters = (size_t)tc::chain::kMaxStages * 3 * (3072 / tc::chain::BN) * 4 * sizeof(unsigned);
+  return 256 + align_up(counters, 256) + (size_t)num_sms() * 128 * tc::chain::BN * sizeof(float);
+}
+
+// Launches the recorded stages on scratch (chain_scratch_bytes(), 256-byte
+// aligned; its barrier word and counters are zeroed here on the stream).
+// exact: no split-K and the whole-set attention arithmetic.
+int chain_launch(void* scratch, size_t scratch_bytes, int exact, cudaStream_t st) {
   using namespace tc;
   chain::Rec& r = chain::t_rec;
   CC2_REQUIRE(r.active, "layer chain: nothing recorded");
   r.active = false;
   if (r.p.nstages == 0) return CC2_OK;
-  CC2_REQUIRE(bar && ((uintptr_t)bar & 15u) == 0, "layer chain: barrier word must be 16-byte aligned");
-  r.p.bar = bar;
+  CC2_REQUIRE(scratch && ((uintptr_t)scratch & 255u) == 0 && scratch_bytes >= chain_scratch_bytes(),
+              "layer chain: scratch must be 256-byte aligned and at least %zu bytes", chain_scratch_bytes());
+  const int grid = num_sms();
+  const size_t counters_max = (size_t)chain::kMaxStages * 3 * (3072 / chain::BN) * 4;
+  size_t cnt_used = 0;
+  const int m_tiles = (r.p.M + BM - 1) / BM;
+  for (int i = 0; i < r.p.nstages; ++i) {
+    chain::Stage& s = r.p.st[i];
+    if (s.kind != 0) continue;
+    const int tiles = m_tiles * ((s.N + chain::BN - 1) / chain::BN);
+    const int kblocks = (s.K + BK - 1) / BK;
+    // Split only long k-loops: the partial round trip (store, fence, count,
+    // reload) costs ~3 us, which a 12-k-block loop (~3.6 us) does not repay
+    // (K = 3072 at 24 tiles: 20.9 -> 16.3 us per stage; K = 768: 9.8 -> 13.2).
+    int S = 1;
+    if (!exact && kblocks >= 32) {
+      if (tiles * 4 <= grid) S = 4;
+      else if (tiles * 2 <= grid) S = 2;
+    }
+    if (S > 1 && cnt_used + (size_t)tiles * 4 > counters_max) S = 1;
+    s.split = S;
+    s.cnt_off = (int)cnt_used;
+    if (S > 1) cnt_used += (size_t)tiles * 4;
+  }
+  char* base = (char*)scratch;
+  r.p.bar = (unsigned int*)base;
+  r.p.cnt = (unsigned int*)(base + 256);
+  r.p.part = (float*)(base + 256 + align_up(counters_max * sizeof(unsigned), 256));
+  r.p.exact = exact ? 1 : 0;
   static unsigned long long attr_set = 0;  // one bit per device
   int dev = 0;
   CC2_CUDA(cudaGetDevice(&dev));
   if (dev >= 64 || !((attr_set >> dev) & 1ull)) {
-    CC2_CUDA(cudaFuncSetAttribute(chain::chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, chain::C::SMEM));
+    CC2_CUDA(cudaFuncSetAttribute(chain::chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, chain::SMEM));
     if (dev < 64) attr_set |= 1ull << dev;
   }
-  CC2_CUDA(cudaMemsetAsync(bar, 0, 16, st));
+  CC2_CUDA(cudaMemsetAsync(base, 0, 256 + cnt_used * sizeof(unsigned), st));
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(num_sms());
+  cfg.gridDim = dim3(grid);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = chain::C::SMEM;
+  cfg.dynamicSmemBytes = chain::SMEM;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeCooperative;

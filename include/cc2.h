@@ -279,15 +279,23 @@ CC2_API int cc2_set_attention_trace(void* device_buffer);
  * returns the previous value. */
 CC2_API int cc2_set_launch_overlap(int enabled);
 
-/* Layer-persistent forward (default 1): a bf16 forward with at most 384 token
+/* Layer-persistent forward (default 0, off): with 1, a bf16 forward with at most 384 token
  * rows (B x S; batch-1 serving), no series groups and no K/V quantiser runs
  * its encoder layers as ONE cooperative launch of one CTA per SM instead of
  * six launches per layer: the QKV GEMM, time attention, O-projection, group
  * block, FFN up and FFN down of every layer are stages separated by a
  * grid-wide barrier.  Its GEMMs compute exactly what the 128 x 64-tile GEMMs
- * compute and its attention exactly what the whole-set mma.sync kernel
- * (cc2_set_attention_variant(3)) computes.  0 launches the layers kernel by
- * kernel.  Process-wide; returns the previous value. */
+ * compute; its attention splits each 16-row query tile's keys over the CTA's
+ * warps and merges their softmax states (results within bf16 rounding of the
+ * per-kernel forward).  2 = the same launch with the attention of the
+ * whole-set mma.sync kernel (cc2_set_attention_variant(3)), bit-identical to
+ * the per-kernel forward with that variant (for tests).  0 launches the
+ * layers kernel by kernel.  Measured at batch 1 the persistent launch is no
+ * faster than the per-kernel forward (0.88 against 0.89 ms at context 2048,
+ * 0.83 against 0.79 ms at 512, CUDA graphs): each stage is bound by its own
+ * latency chain (first load, k-loop at one SM's TMA rate, epilogue, barrier),
+ * which the launches it replaces already overlapped.  Process-wide; returns
+ * the previous value. */
 CC2_API int cc2_set_layer_chain(int enabled);
 /* Test hook (no counterpart in the reference): on != 0 arms a one-shot
  * fault-free failure: the next single-SM bf16 GEMM CTA (cc2_gemm with
@@ -307,10 +315,16 @@ CC2_API int cc2_test_starve_gemm(int on);
 CC2_API int cc2_test_starve_layer_barrier(int on);
 
 /* Stage trace of the layer-persistent forward: with a device buffer of
- * 8 x 76 x 2 uint64 (zeroed by the caller), CTAs 0..7 of every later launch
- * write, for stage s, [cta][s][0] = %globaltimer (ns) when the CTA finished
- * the stage and [cta][s][1] when the grid barrier after it released the CTA.
- * NULL turns it off.  Process-wide. */
+ * 8 x 76 x 2 + 320 uint64 (zeroed by the caller), CTAs 0..7 of every later
+ * launch write, for stage s, [cta][s][0] = %globaltimer (ns) when the CTA
+ * finished the stage and [cta][s][1] when the grid barrier after it released
+ * the CTA; CTA 0 then records its first tile of stages 2 and 5 (160 entries
+ * each): [0..63] load of k-block issued, [64..127] k-block landed (MMA
+ * issue), [128] accumulator full, [129] tile stored, [130] stores complete,
+ * [131] stage start, [132] accumulator read, [133] residual box landed,
+ * [134] epilogue computed, [135] epilogue tile start; and of stage 1 (time
+ * attention, 8 entries from 320): [327] stage start, [320] Q/K/V staged,
+ * [321..326] warp w done.  NULL turns it off.  Process-wide. */
 CC2_API int cc2_set_layer_trace(void* device_buffer);
 
 /* Event trace of the 2-SM GEMM: with a device buffer of 32 x 8 uint64

@@ -72,17 +72,21 @@ def test_layer_barrier_timeout_sets_status_and_recovers():
     lib = nat.load()
     m = seeded_init_(CuteChronos2Model(small_config()), seed=0).to(DEV, torch.bfloat16).eval()
     ctx = torch.randn(1, 300).to(DEV)  # one series: 23 token rows, the layers in one launch
-    good = m(ctx, num_output_patches=3).clone()
-    torch.cuda.synchronize()
-    assert lib.cc2_device_status(1) == 0
-    nat.check(lib.cc2_test_starve_layer_barrier(1), "cc2_test_starve_layer_barrier")
+    old_c = lib.cc2_set_layer_chain(1)
     try:
-        m(ctx, num_output_patches=3)
-        status = lib.cc2_device_status(1)
+        good = m(ctx, num_output_patches=3).clone()
+        torch.cuda.synchronize()
+        assert lib.cc2_device_status(1) == 0
+        nat.check(lib.cc2_test_starve_layer_barrier(1), "cc2_test_starve_layer_barrier")
+        try:
+            m(ctx, num_output_patches=3)
+            status = lib.cc2_device_status(1)
+        finally:
+            nat.check(lib.cc2_test_starve_layer_barrier(0), "cc2_test_starve_layer_barrier")
+        assert status == 4  # CC2_DEV_LAYER_TIMEOUT
+        again = m(ctx, num_output_patches=3)
+        torch.cuda.synchronize()
+        assert lib.cc2_device_status(0) == 0
+        assert torch.equal(again, good)
     finally:
-        nat.check(lib.cc2_test_starve_layer_barrier(0), "cc2_test_starve_layer_barrier")
-    assert status == 4  # CC2_DEV_LAYER_TIMEOUT
-    again = m(ctx, num_output_patches=3)
-    torch.cuda.synchronize()
-    assert lib.cc2_device_status(0) == 0
-    assert torch.equal(again, good)
+        lib.cc2_set_layer_chain(old_c)

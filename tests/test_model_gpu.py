@@ -235,20 +235,25 @@ def test_batch1_equals_batched(base_bf16, base_weights):
 
 
 def _chain_pair(model, ctx, N):
-    """(layer-persistent forward, kernel-by-kernel forward with the same
-    attention arithmetic), both eager."""
+    """(layer-persistent forward with the whole-set attention arithmetic,
+    kernel-by-kernel forward with the same attention kernel,
+    layer-persistent forward in its default split-key mode), all eager."""
     from cutechronos_b200 import _native as nat
     lib = nat.load()
     old_v = lib.cc2_set_attention_variant(3)
+    old_c = lib.cc2_set_layer_chain(2)
     try:
-        lib.cc2_set_layer_chain(1)
         a = model(ctx.to(DEV), num_output_patches=N).cpu()
         lib.cc2_set_layer_chain(0)
         b = model(ctx.to(DEV), num_output_patches=N).cpu()
-    finally:
         lib.cc2_set_layer_chain(1)
+        c = model(ctx.to(DEV), num_output_patches=N).cpu()
+        c2 = model(ctx.to(DEV), num_output_patches=N).cpu()
+    finally:
+        lib.cc2_set_layer_chain(old_c)
         lib.cc2_set_attention_variant(old_v)
-    return a, b
+    assert torch.equal(c, c2)  # deterministic
+    return a, b, c
 
 
 # (B, L): 133 token rows (ctx 2048), 2 x 37 rows (ctx 512), 3 x 81 rows with
@@ -264,10 +269,12 @@ def test_layer_chain_equals_kernel_by_kernel(base_bf16, base_weights, B, L):
     if B == 3:
         ctx[1, : L // 3] = float("nan")  # left padding
         ctx[2, 100:140] = float("nan")   # a gap inside the context
-    a, b = _chain_pair(base_bf16, ctx, 4)
+    a, b, c = _chain_pair(base_bf16, ctx, 4)
     assert torch.equal(a, b)
     ref = orc.forward(orc.OracleConfig(), base_weights, ctx, None, 4)
-    assert _report(f"layer_chain_B{B}_L{L}_bf16_rel", _rel_err(a, ref)) <= 2e-2
+    assert _report(f"layer_chain_exact_B{B}_L{L}_bf16_rel", _rel_err(a, ref)) <= 2e-2
+    assert _report(f"layer_chain_B{B}_L{L}_bf16_rel", _rel_err(c, ref)) <= 2e-2
+    assert _rel_err(c, a) <= 2e-2
 
 
 def test_layer_chain_small_model_and_graph(small_bf16):
@@ -275,13 +282,19 @@ def test_layer_chain_small_model_and_graph(small_bf16):
     and replay of the cooperative launch from a CUDA graph."""
     g = torch.Generator().manual_seed(3)
     x = torch.randn(2, 300, generator=g)
-    a, b = _chain_pair(small_bf16, x, 3)
+    a, b, c = _chain_pair(small_bf16, x, 3)
     assert torch.equal(a, b)
+    assert _rel_err(c, a) <= 2e-2
+    from cutechronos_b200 import _native as nat
+    lib = nat.load()
+    old_c = lib.cc2_set_layer_chain(1)
     small_bf16.enable_cuda_graphs(True)
     try:
         outs = [small_bf16(x.to(DEV), num_output_patches=3).cpu() for _ in range(3)]
+        small_bf16.enable_cuda_graphs(False)
+        eager = small_bf16(x.to(DEV), num_output_patches=3).cpu()
     finally:
         small_bf16.enable_cuda_graphs(False)
-    eager = small_bf16(x.to(DEV), num_output_patches=3).cpu()
+        lib.cc2_set_layer_chain(old_c)
     for o in outs:
         assert torch.equal(o, eager)
