@@ -1033,11 +1033,18 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
     return launch_pair_t<0, 5, 2, true>(ma, mb, mc, mr, M, N, K, ep, st);
 #define CC2_PAIR(FL) \
   case (FL): return launch_pair_t<(FL), 5, 2>(ma, mb, mc, mr, M, N, K, ep, st);
+  // an epilogue without a residual needs one staging box per warp, which
+  // leaves room for a sixth ring stage (more loads in flight per SM): FFN up
+  // 141-142 -> 139-140 us at configs[1]; QKV measured no better (114 -> 116).
+  // Residual epilogues keep their boxes: reading the residual into registers
+  // instead, to free the room, doubled the O-projection's time (61 -> 123 us).
+#define CC2_PAIR6(FL) \
+  case (FL): return launch_pair_t<(FL), 6, 1>(ma, mb, mc, mr, M, N, K, ep, st);
   switch (ep.flags) {  // the epilogues the forward uses, specialised at compile time
     CC2_PAIR(RS | RP)            // time-attention QKV (RMSNorm + RoPE)
     CC2_PAIR(RP)                 // RoPE alone (component use)
     CC2_PAIR(RS)                 // group QKV
-    CC2_PAIR(RS | RL)            // FFN up
+    CC2_PAIR6(RS | RL)           // FFN up
     CC2_PAIR(RE | SQ)            // O-projections, FFN down (component use)
     CC2_PAIR(RE | SQ | LO)       // O-projections, FFN down (hi + lo residual stream)
     CC2_PAIR(RS | RE | SQ)       // one-series group block (component use)
@@ -1051,6 +1058,7 @@ static int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUten
       break;
   }
 #undef CC2_PAIR
+#undef CC2_PAIR6
   if (ep.flags & RP) {
     set_error("gemm: CC2_EPI_ROPE combines with CC2_EPI_ROWSCALE only");
     return CC2_E_UNSUPPORTED;
