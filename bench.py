@@ -698,6 +698,17 @@ def run_micro(args):
             lib.cc2_set_attention_variant(old)
         return run
 
+    def gemm_variant(v, fn):
+        def run():
+            old = lib.cc2_set_gemm_variant(v)
+            fn()
+            lib.cc2_set_gemm_variant(old)
+        return run
+
+    # batch-1 serving shapes (one series, context 2048: 133 token rows)
+    x1, h1 = x[:133].contiguous(), h[:133].contiguous()
+    res1 = x1.clone()
+
     B4 = 4096
     qkv4 = rnd(B4 * 37, 3 * d, scale=0.5)
     tok4 = torch.ones(B4 * 37, dtype=torch.uint8, device=dev)
@@ -764,6 +775,12 @@ def run_micro(args):
             lambda: kk.linear(h, wf, residual=res, residual_lo=res_lo, lo_out=res_lo, ssq_out=so, out=res),
             2 * M * d * dff),
         "gemm 8192^3 plain": (lambda: kk.linear(big, big), 2 * 8192 ** 3),
+        # batch-1 FFN down (133 token rows): the micro time of one call is host-bound
+        # (tensor maps built per call); the device time comes from ncu
+        "b1 ffn2 M=133 N=768 K=3072 (128x64 tiles)": (
+            lambda: kk.linear(h1, wf, residual=res1, out=res1), 2 * 133 * d * dff, d * dff * 2),
+        "b1 ffn2 M=133 N=768 K=3072 (2-SM tiles)": (
+            gemm_variant(2, lambda: kk.linear(h1, wf, residual=res1, out=res1)), 2 * 133 * d * dff, d * dff * 2),
         "attn time S=133 (rope)": (lambda: kk.attention_rows(qkvr, tok, args.batch, 133, 12, True, att),
                                    4 * args.batch * 12 * 133 * 133 * 64),
         "attn time S=133 (no rope)": (lambda: kk.attention_rows(qkvr, tok, args.batch, 133, 12, False, att),
