@@ -76,6 +76,22 @@ struct Cfg {
   static constexpr int SMEM = STAGES * STAGE_BYTES + 8 * 32 * 64 * 2 + 1024 + 256;
 };
 
+// The single-SM kernel moves KPS = 2 k-blocks per ring stage (one mbarrier
+// round trip per 2 k-blocks): a TMA probe on this pool streamed ~58 GB/s per
+// SM with one 16 KB box per barrier and ~116 GB/s with two, whatever the
+// number of barriers in flight - the per-barrier round trip, not the bytes,
+// bounded the k-loop of few-row GEMMs (0.29 us per k-block).
+template <int BN>
+struct Cfg2 {
+  static constexpr int KPS = 2;
+  static constexpr int STAGES = BN == 256 ? 2 : BN == 128 ? 3 : 4;
+  static constexpr int A_BYTES = BM * BK * 2;  // per k-block
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = KPS * (A_BYTES + B_BYTES);  // [A kb0][A kb1][B kb0][B kb1]
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 8 * 32 * 64 * 2 + 1024 + 256;
+};
+
 struct Epi {
   int flags;
   const float* ssq_in;
@@ -422,10 +438,10 @@ __device__ __forceinline__ float row_scale(const Epi& ep, const int flags, int r
 template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-               const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR, int M, int N,
-               int K, Epi ep) {
+               const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR,
+               const __grid_constant__ CUtensorMap tmAt, int tail_rows, int M, int N, int K, Epi ep) {
   pdl_launch_dependents();
-  using C = Cfg<BN>;
+  using C = Cfg2<BN>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* epi_smem = smem + C::STAGES * C::STAGE_BYTES;  // 4 warps x 2 boxes
@@ -460,6 +476,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
     tma_prefetch_desc(&tmB);
     tma_prefetch_desc(&tmC);
     tma_prefetch_desc(&tmR);
+    tma_prefetch_desc(&tmAt);
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
@@ -483,7 +500,7 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int mt = tile / n_tiles, nt = tile % n_tiles;
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = 0; kb < kblocks; kb += C::KPS) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) { ok = false; break; }
           if (kb == 0 && tile == (int)blockIdx.x && *(volatile int*)&g_gemm_starve &&
               atomicExch(&g_gemm_starve, 0)) {
@@ -491,9 +508,17 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
             continue;  // test hook: this stage never fills
           }
           const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
-          mbar_arrive_expect_tx(full_bar(stage), C::STAGE_BYTES);
-          tma_load_2d(sa, &tmA, full_bar(stage), kb * BK, mt * BM);
-          tma_load_2d(sa + C::A_BYTES, &tmB, full_bar(stage), kb * BK, nt * BN);
+          const uint32_t sb = sa + C::KPS * C::A_BYTES;
+          const int nk = min(C::KPS, kblocks - kb);
+          // the last row tile loads only its tail_rows rows (a smaller box); the MMA
+          // rows past them only produce accumulator rows that are never stored
+          const bool tail = mt == m_tiles - 1 && tail_rows < BM;
+          const uint32_t a_bytes = tail ? (uint32_t)tail_rows * BK * 2 : (uint32_t)C::A_BYTES;
+          mbar_arrive_expect_tx(full_bar(stage), (uint32_t)nk * (a_bytes + (uint32_t)C::B_BYTES));
+          for (int j = 0; j < nk; ++j) {
+            tma_load_2d(sa + j * C::A_BYTES, tail ? &tmAt : &tmA, full_bar(stage), (kb + j) * BK, mt * BM);
+            tma_load_2d(sb + j * C::B_BYTES, &tmB, full_bar(stage), (kb + j) * BK, nt * BN);
+          }
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         }
       }
@@ -512,14 +537,18 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
         if (!mbar_wait(tempty_bar(acc), acc_phase ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int kb = 0; kb < kblocks; ++kb) {
+        for (int kb = 0; kb < kblocks; kb += C::KPS) {
           if (!mbar_wait(full_bar(stage), phase, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint32_t sa = smem_u32(smem + stage * C::STAGE_BYTES);
-          const uint32_t sb = sa + C::A_BYTES;
+          const uint32_t sb = sa + C::KPS * C::A_BYTES;
+          const int nk = min(C::KPS, kblocks - kb);
+          for (int j = 0; j < nk; ++j) {
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_bf16(d_tmem, sw128_desc(sa + 32u * k), sw128_desc(sb + 32u * k), idesc, (kb | k) != 0 ? 1u : 0u);
+            for (int k = 0; k < BK / 16; ++k)
+              mma_bf16(d_tmem, sw128_desc(sa + j * C::A_BYTES + 32u * k), sw128_desc(sb + j * C::B_BYTES + 32u * k),
+                       idesc, ((kb + j) | k) != 0 ? 1u : 0u);
+          }
           mma_commit(empty_bar(stage));
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -976,8 +1005,13 @@ static int make_map(CUtensorMap* map, const void* ptr, int cols, int rows, int l
 
 template <int BN>
 static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mr, int M,
-                  int N, int K, const Epi& ep, cudaStream_t st) {
-  using C = Cfg<BN>;
+                  int N, int K, const Epi& ep, cudaStream_t st, const void* A, int lda) {
+  using C = Cfg2<BN>;
+  // rows of the last row tile, rounded up to whole 8-row swizzle atoms
+  const int rem = M % BM;
+  const int tail_rows = rem == 0 ? BM : (rem + 7) / 8 * 8;
+  CUtensorMap mat = ma;
+  if (tail_rows < BM) CC2_TRY(make_map(&mat, A, K, M, lda, tail_rows));
   static unsigned long long attr_set = 0;  // one bit per device
   int dev = 0;
   CC2_CUDA(cudaGetDevice(&dev));
@@ -987,7 +1021,7 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMa
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  CC2_CUDA(launch_k(gemm_tc_kernel<BN>, grid, kThreads, C::SMEM, st, ma, mb, mc, mr, M, N, K, ep));
+  CC2_CUDA(launch_k(gemm_tc_kernel<BN>, grid, kThreads, C::SMEM, st, ma, mb, mc, mr, mat, tail_rows, M, N, K, ep));
   CC2_CHECK_LAUNCH();
   return CC2_OK;
 }
@@ -1758,7 +1792,7 @@ int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, in
   const int pair_ctas = 2 * ((M + 255) / 256) * ((N + 255) / 256);
   if (g_gemm_variant == 0 && N >= 64 && 2 * pair_ctas <= num_sms()) {
     CC2_TRY(make_map(&mb, W, K, N, ldw, 64));
-    return launch<64>(ma, mb, mc, mr, M, N, K, ep, st);
+    return launch<64>(ma, mb, mc, mr, M, N, K, ep, st, A, lda);
   }
   if (g_gemm_variant != 1 && M > BM) {  // 2-SM tiles (256 x 256 per CTA pair)
     CC2_TRY(make_map(&mb, W, K, N, ldw, 128));
@@ -1767,10 +1801,10 @@ int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, in
   const int tiles256 = ((M + BM - 1) / BM) * ((N + 255) / 256);
   if (N >= 256 && tiles256 >= num_sms()) {
     CC2_TRY(make_map(&mb, W, K, N, ldw, 256));
-    return launch<256>(ma, mb, mc, mr, M, N, K, ep, st);
+    return launch<256>(ma, mb, mc, mr, M, N, K, ep, st, A, lda);
   }
   CC2_TRY(make_map(&mb, W, K, N, ldw, 128));
-  return launch<128>(ma, mb, mc, mr, M, N, K, ep, st);
+  return launch<128>(ma, mb, mc, mr, M, N, K, ep, st, A, lda);
 }
 
 // ---- layer-persistent forward (see tc::chain) ----------------------------------
