@@ -5,7 +5,6 @@ test_predict_df.py, test_pipeline_api.py and test_lora_loading.py."""
 
 import json
 import os
-import socket
 
 import pytest
 import torch
@@ -175,16 +174,10 @@ def test_partition_groups_keeps_groups_whole_and_balances():
     assert [len(s) for s in partition_groups(None, 10, 3)] in ([4, 3, 3], [3, 4, 3], [3, 3, 4])
 
 
-def _free_port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
-
-
-def _rank_main(rank, world, port, ctx, gid, result_q):
+def _rank_main(rank, world, init_file, ctx, gid, result_q):
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    # file rendezvous: no TCP port to race for while the ranks start up
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=world)
     try:
         shards = partition_groups(gid, ctx.shape[0], world)
         mine = shards[rank]
@@ -195,14 +188,14 @@ def _rank_main(rank, world, port, ctx, gid, result_q):
         dist.destroy_process_group()
 
 
-def test_two_rank_gloo_sharding_and_gather():
+def test_two_rank_gloo_sharding_and_gather(tmp_path):
     ctx = torch.randn(11, 40)
     gid = torch.tensor([0, 0, 1, 2, 2, 2, 3, 4, 4, 5, 6])
     expect = FakeModel()(ctx, num_output_patches=2, group_ids=gid)
     mpc = mp.get_context("spawn")
     q = mpc.Queue()
-    port = _free_port()
-    procs = [mpc.Process(target=_rank_main, args=(r, 2, port, ctx, gid, q)) for r in range(2)]
+    init_file = str(tmp_path / "rendezvous")
+    procs = [mpc.Process(target=_rank_main, args=(r, 2, init_file, ctx, gid, q)) for r in range(2)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=120) for _ in procs)
