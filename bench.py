@@ -715,7 +715,7 @@ def run_micro(args):
     att4 = torch.empty(B4 * 37, d, dtype=torch.bfloat16, device=dev)
     # memory-bound kernels at a streaming size (HBM-bound; the forward's own
     # launches are a few MB and launch/latency-bound)
-    Bp, Lp = 16384, 2048
+    Bp, Lp = 65536, 2048  # the survey's streaming size: inputs and outputs well above the 126 MB L2
     Pp = Lp // 16
     ctxp = torch.randn(Bp, Lp, generator=g, device=dev)
     predp = rnd(Bp, 4, 336)
@@ -753,10 +753,10 @@ def run_micro(args):
         "group attn 64x8 S=133 bf16 (tcgen05)": (
             lambda: kk.group_attention_contig(qkvg.view(Bg, Sg, 3 * d), tokg.view(Bg, Sg), 8, 12), 0,
             Bg * Sg * d * 2 * 4),
-        "preprocess B=16384 L=2048 bf16": (
+        "preprocess B=65536 L=2048 bf16": (
             lambda: kk.fused_preprocess(ctxp, 16, 8192, True, dtype=torch.bfloat16), 0,
             Bp * (4 * Lp + 2 * 48 * Pp + Pp + 4 * Pp + 8)),
-        "output transform B=16384 N=4 bf16": (
+        "output transform B=65536 N=4 bf16": (
             lambda: kk.fused_output_transform(predp, locp, scp, 21, 16, True), 0, 2 * 2 * Bp * 4 * 336 + 8 * Bp),
         "rmsnorm M=34048 d=768 bf16": (lambda: kk.rms_layernorm(x, wln), 0, 2 * 2 * M * d),
         "rmsnorm M=136192 d=768 bf16": (lambda: kk.rms_layernorm(x4, wln), 0, 2 * 2 * 4 * M * d),

@@ -23,19 +23,23 @@ __device__ __forceinline__ uint32_t pack2bf(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// Two sums in one pass over the block (one pair of barriers); red holds
-// 2 * warps doubles.
-// s + e += x with an error-free transformation (Knuth's two-sum): s + e keeps
-// the exact sum of the values added so far, up to the rounding of e itself
-// (below 2^-48 of the sum for the <= 32 values a thread adds).
-__device__ __forceinline__ void two_sum_acc(float& s, float& e, float x) {
-  const float t = __fadd_rn(s, x);
-  const float bp = __fsub_rn(t, s);
-  const float err = __fadd_rn(__fsub_rn(s, __fsub_rn(t, bp)), __fsub_rn(x, bp));
+// s + e += x with an error-free transformation (Knuth's two-sum), on two
+// independent accumulators at once (packed fp32, each lane rounded as a
+// scalar instruction would be; t - s is formed as fma(s, -1, t), the same
+// single rounding as a subtraction): s + e keeps the exact sum of the values
+// added so far, up to the rounding of e itself (below 2^-48 of the sum for
+// the <= 32 values a thread adds).
+__device__ __forceinline__ void two_sum_acc2(float2& s, float2& e, float2 x) {
+  const float2 m1 = make_float2(-1.0f, -1.0f);
+  const float2 t = __fadd2_rn(s, x);
+  const float2 bp = __ffma2_rn(s, m1, t);
+  const float2 err = __fadd2_rn(__ffma2_rn(__ffma2_rn(bp, m1, t), m1, s), __ffma2_rn(bp, m1, x));
   s = t;
-  e = __fadd_rn(e, err);
+  e = __fadd2_rn(e, err);
 }
 
+// Two sums in one pass over the block (one pair of barriers); red holds
+// 2 * warps doubles.
 __device__ __forceinline__ void block_sum2(double& a, double& b, double* red) {
   for (int o = 16; o > 0; o >>= 1) {
     a += __shfl_xor_sync(0xffffffffu, a, o);
@@ -84,6 +88,24 @@ __device__ __forceinline__ float asinh_fast(float x) {
   float l;
   asm("lg2.approx.f32 %0, %1;" : "=f"(l) : "f"(large ? a : a + r));
   return copysignf((l + (large ? 1.0f : 0.0f)) * 0.6931471805599453f, x);
+}
+
+// asinh_fast for two values at once (packed fp32), without the overflow
+// branch: the vectorised preprocessing applies it to (x - loc) / scale of a
+// series, whose magnitude is at most sqrt(n - 1) <= 91 for n <= 8192 values
+// (Samuelson's inequality; a sanitised 0 for missing values), far below the
+// 1e18 where x^2 + 1 would overflow.
+__device__ __forceinline__ float2 asinh_bounded2(float2 x) {
+  const float2 a = make_float2(fabsf(x.x), fabsf(x.y));
+  const float2 q = __ffma2_rn(a, a, make_float2(1.0f, 1.0f));
+  float2 r, l;
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(r.x) : "f"(q.x));
+  asm("sqrt.approx.f32 %0, %1;" : "=f"(r.y) : "f"(q.y));
+  const float2 u = __fadd2_rn(a, r);
+  asm("lg2.approx.f32 %0, %1;" : "=f"(l.x) : "f"(u.x));
+  asm("lg2.approx.f32 %0, %1;" : "=f"(l.y) : "f"(u.y));
+  l = __fmul2_rn(l, make_float2(0.6931471805599453f, 0.6931471805599453f));
+  return make_float2(copysignf(l.x, x.x), copysignf(l.y, x.y));
 }
 
 // One CTA per series.  Sums are accumulated in double so that the loc/scale
@@ -244,36 +266,46 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
   // same exact partial sums as accumulating in double, without a conversion
   // to double per value; the block then reduces them in double
   // (one pair per chunk: independent dependency chains)
-  float s_hi[CH], s_lo[CH];
+  // (two chains per chunk, even and odd positions, as the lanes of packed
+  // fp32 instructions)
+  float2 s_hi[CH], s_lo[CH];
   int n_ok = 0;
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
-    s_hi[c] = s_lo[c] = 0.0f;
+    s_hi[c] = s_lo[c] = make_float2(0.0f, 0.0f);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const bool ok = !isnan(v[c][i]);
-      n_ok += ok ? 1 : 0;
-      two_sum_acc(s_hi[c], s_lo[c], ok ? v[c][i] : 0.0f);
+    for (int i = 0; i < 8; i += 2) {
+      const bool ok0 = !isnan(v[c][i]), ok1 = !isnan(v[c][i + 1]);
+      n_ok += (ok0 ? 1 : 0) + (ok1 ? 1 : 0);
+      two_sum_acc2(s_hi[c], s_lo[c], make_float2(ok0 ? v[c][i] : 0.0f, ok1 ? v[c][i + 1] : 0.0f));
     }
   }
   double sum = 0.0, cnt = (double)n_ok;
 #pragma unroll
-  for (int c = 0; c < CH; ++c) sum += (double)s_hi[c] + (double)s_lo[c];
+  for (int c = 0; c < CH; ++c)
+    sum += ((double)s_hi[c].x + (double)s_lo[c].x) + ((double)s_hi[c].y + (double)s_lo[c].y);
   block_sum2(sum, cnt, red);
   const float lo = cnt > 0.0 ? (float)(sum / cnt) : 0.0f;
-  float q_hi[CH], q_lo[CH];
+  // squared deviations: non-negative terms, so the sum needs no
+  // compensation: two plain fp32 sums (fused multiply-adds) of 4 terms per
+  // chunk (at most 4 roundings each, 2.4e-7 relative, about 1e-7 on the
+  // scale), then double across chunks and threads
+  float2 q[CH];
+  const float2 nlo = make_float2(-lo, -lo);
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
-    q_hi[c] = q_lo[c] = 0.0f;
+    q[c] = make_float2(0.0f, 0.0f);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float d = v[c][i] - lo;
-      two_sum_acc(q_hi[c], q_lo[c], isnan(v[c][i]) ? 0.0f : d * d);
+    for (int i = 0; i < 8; i += 2) {
+      float2 d = __fadd2_rn(make_float2(v[c][i], v[c][i + 1]), nlo);
+      d.x = isnan(d.x) ? 0.0f : d.x;
+      d.y = isnan(d.y) ? 0.0f : d.y;
+      q[c] = __ffma2_rn(d, d, q[c]);
     }
   }
   double ssp = 0.0;
 #pragma unroll
-  for (int c = 0; c < CH; ++c) ssp += (double)q_hi[c] + (double)q_lo[c];
+  for (int c = 0; c < CH; ++c) ssp += (double)q[c].x + (double)q[c].y;
   double ss = block_sum(ssp, red);
   // the scale is computed once (thread 0) and shared
   __shared__ float sc_sh;
@@ -291,6 +323,7 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
   const float rsc = 1.0f / sc;
   const size_t row0 = (size_t)b * S;
   const int cpp = ps / 8;  // chunks per patch: 1, 2 or 4 adjacent lanes
+  const int ps_log = __ffs(ps) - 1;  // the patch width is 8, 16 or 32 here: shifts, not divisions
 #pragma unroll
   for (int c = 0; c < CH; ++c) {
     const int k = tid + c * G;
@@ -305,19 +338,33 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
       // uniform conditions are tested once per chunk, outside the per-value
       // loops, so no value pays for the path it does not take
       if (te_inv != 0.0f) {
+        // te_inv is a power of two here, so tbase * te_inv and i * te_inv are
+        // exact and so is their sum (the value (tbase + i) * te_inv): one FMA
+        const float2 tb = make_float2(tbase * te_inv, tbase * te_inv), ti = make_float2(te_inv, te_inv);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) te[i] = (tbase + (float)i) * te_inv;
+        for (int i = 0; i < 8; i += 2) {
+          const float2 t2 = __ffma2_rn(make_float2((float)i, (float)(i + 1)), ti, tb);
+          te[i] = t2.x; te[i + 1] = t2.y;
+        }
       } else {
 #pragma unroll
         for (int i = 0; i < 8; ++i) te[i] = (float)(j0 + i - total) / te_scale;
       }
       if (sizeof(T) == 2 && m == nullptr && j0 - pad >= 0) {  // bf16, NaN mask, all 8 positions in the series
         if (use_arcsinh) {
+          // branch-free, two positions per packed instruction: asinh of a
+          // sanitised argument (0 for a NaN value, asinh(0) = 0), then times
+          // the 0/1 mask
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            const bool ok = !isnan(v[c][i]);
-            mt[i] = ok ? 1.0f : 0.0f;
-            val[i] = ok ? asinh_fast((v[c][i] - lo) * rsc) : 0.0f;
+          for (int i = 0; i < 8; i += 2) {
+            const bool ok0 = !isnan(v[c][i]), ok1 = !isnan(v[c][i + 1]);
+            const float2 mk = make_float2(ok0 ? 1.0f : 0.0f, ok1 ? 1.0f : 0.0f);
+            float2 z = __fmul2_rn(__fadd2_rn(make_float2(v[c][i], v[c][i + 1]), nlo), make_float2(rsc, rsc));
+            z.x = ok0 ? z.x : 0.0f;
+            z.y = ok1 ? z.y : 0.0f;
+            z = __fmul2_rn(asinh_bounded2(z), mk);
+            mt[i] = mk.x; mt[i + 1] = mk.y;
+            val[i] = z.x; val[i + 1] = z.y;
           }
         } else {
 #pragma unroll
@@ -351,7 +398,7 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
         acc += mt[i];
       }
       }
-      const int p = j0 / ps, c0 = j0 % ps;
+      const int p = j0 >> ps_log, c0 = j0 & (ps - 1);
       T* r = out + (row0 + p) * ld + c0;
       if constexpr (sizeof(T) == 2) {
         uint4 w;
@@ -377,8 +424,8 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
     // attention mask per patch: sum of the (rounded) patch mask > 0, over the
     // patch's cpp adjacent lanes
     for (int o = 1; o < cpp; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-    if (j0 < total && (k % cpp) == 0) {
-      const int p = j0 / ps;
+    if (j0 < total && (k & (cpp - 1)) == 0) {
+      const int p = j0 >> ps_log;
       const bool on = acc > 0.0f;
       tok_mask[row0 + p] = on ? 1 : 0;
       if (attn_out) attn_out[(size_t)b * P + p] = on ? 1.0f : 0.0f;
@@ -390,7 +437,8 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
   for (int c = tid; c < 3 * ps; c += G)
     for (int e = 0; e < extra; ++e) {
       const int n = e - use_reg;
-      const float fv = n >= 0 && c < ps ? (float)(n * ps + c) / te_scale : 0.0f;
+      const float pos = (float)(n * ps + c);  // an integer below 2^24: exact
+      const float fv = n >= 0 && c < ps ? (te_inv != 0.0f ? pos * te_inv : pos / te_scale) : 0.0f;
       out[(row0 + P + e) * ld + c] = fromf<T>(fv);
     }
   for (int e = tid; e < extra; e += G) tok_mask[row0 + P + e] = 1;
@@ -409,76 +457,120 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
   }
 }
 
-// sinh for the output transform, from its definition: |x| < 1/2 by the odd
+// sinh for the bf16 output transform, from its definition: |x| < 1/2 by the odd
 // Taylor series x + x^3/3! + x^5/5! + x^7/7! (truncation below 5e-9
 // relative), otherwise (e - 1/e) / 2 with e = 2^(|x| log2 e) from the hardware
 // exp2 (relative error about 6e-8 |x|, below 1e-6 for the |x| <= 15 a
-// forecast in arcsinh space reaches), sign restored.
-__device__ __forceinline__ float sinh_fast(float x) {
-  const float a = fabsf(x);
-  const float a2 = a * a;
-  const float poly = fmaf(fmaf(fmaf(a2, 1.0f / 5040.0f, 1.0f / 120.0f), a2, 1.0f / 6.0f), a2 * a, a);
-  float e;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(a * 1.4426950408889634f));
-  float inv;
-  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv) : "f"(e));
-  const float big = 0.5f * (e - inv);
-  return copysignf(a < 0.5f ? poly : big, x);
+// forecast in arcsinh space reaches), sign restored.  (An FMA-only version -
+// Cody-Waite reduction and a shared even/odd polynomial, no MUFU op - was
+// slower: the kernel is bound by instruction issue, where a MUFU op is one
+// slot, and it needed ~30 instructions per output against ~18.)
+// Computed for a pair of values with the Blackwell packed-fp32 instructions
+// (one issue slot for both lanes, each lane rounded as a scalar instruction
+// would be).
+__device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
+__device__ __forceinline__ float2 sinh_fast2(float2 x) {
+  const float2 a = make_float2(fabsf(x.x), fabsf(x.y));
+  const float2 a2 = __fmul2_rn(a, a);
+  float2 poly = __ffma2_rn(a2, f2(1.0f / 5040.0f), f2(1.0f / 120.0f));
+  poly = __ffma2_rn(poly, a2, f2(1.0f / 6.0f));
+  poly = __ffma2_rn(poly, __fmul2_rn(a2, a), a);
+  const float2 t = __fmul2_rn(a, f2(1.4426950408889634f));
+  float2 e, inv;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(t.x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(t.y));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv.x) : "f"(e.x));
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv.y) : "f"(e.y));
+  const float2 big = __fmul2_rn(__ffma2_rn(inv, f2(-1.0f), e), f2(0.5f));
+  return make_float2(copysignf(a.x < 0.5f ? poly.x : big.x, x.x), copysignf(a.y < 0.5f ? poly.y : big.y, x.y));
 }
 
-// Vectorised output transform: one thread per 8 consecutive outputs of a
-// (series, quantile, patch) row; 16-byte (bf16) / 32-byte (fp32) loads and stores.
-template <typename T>
+// Output transform: (B, N, ld) forecasts in the model's row layout ->
+// (B, Q, N * ps) rows, sinh and unscale.  A thread owns one 8-output segment
+// of the per-series layout (its source and destination offsets computed once)
+// and walks the series of its block, UNR of them per step so that UNR
+// 16-byte loads are in flight per thread.
+template <typename T, int UNR>
 __global__ void __launch_bounds__(256)
-output_transform_vec_kernel(const T* __restrict__ preds, int ld, const float* __restrict__ loc,
+output_transform_seg_kernel(const T* __restrict__ preds, int ld, const float* __restrict__ loc,
                             const float* __restrict__ scale, T* __restrict__ out, int B, int N, int Q, int ps,
                             int use_arcsinh) {
   pdl_launch_dependents();
   pdl_wait();
-  // flat segment index r = ((b * Q + q) * N + n) * spp + s8 (the output order)
-  // in 32-bit arithmetic (the launcher keeps the total below 2^31)
-  const unsigned spp = (unsigned)ps / 8u;  // segments per patch row
-  const unsigned per_series = (unsigned)(Q * N) * spp;
-  const unsigned total = (unsigned)B * per_series;
-  for (unsigned r = blockIdx.x * blockDim.x + threadIdx.x; r < total; r += gridDim.x * blockDim.x) {
-    const unsigned b = r / per_series, rem = r - b * per_series;
-    const unsigned t = rem / spp, s8 = rem - t * spp;
-    const unsigned qq = t / (unsigned)N;
-    const int n = (int)(t - qq * (unsigned)N), q = (int)qq;
-    const T* src = preds + ((size_t)b * N + n) * ld + q * ps + 8 * s8;
-    T* dst = out + (((size_t)b * Q + q) * N + n) * ps + 8 * s8;
-    const float sc = scale[b], lo = loc[b];
-    float f[8];
-    if constexpr (sizeof(T) == 2) {
-      const uint4 w = *reinterpret_cast<const uint4*>(src);
-      const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+  const int spp = ps / 8;  // segments per patch row
+  const int per_series = Q * N * spp;
+  constexpr int V = 8 * (int)sizeof(T) / 16;  // 16-byte vectors per segment
+  using Vec = uint4;
+  for (int seg = (int)threadIdx.x; seg < per_series; seg += (int)blockDim.x) {
+    // output order: seg = (q * N + n) * spp + s8
+    const int t = seg / spp, s8 = seg - t * spp;
+    const int q = t / N, n = t - q * N;
+    const size_t src0 = (size_t)n * ld + (size_t)q * ps + 8 * s8;
+    const size_t dst0 = (size_t)seg * 8;
+    const size_t src_step = (size_t)N * ld, dst_step = (size_t)per_series * 8;
+    for (int b0 = (int)blockIdx.x * UNR; b0 < B; b0 += (int)gridDim.x * UNR) {
+      Vec w[UNR][V];
+      float sc[UNR], lo[UNR];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        f[2 * i] = __uint_as_float(u[i] << 16);
-        f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
-      }
-    } else {
-      const float4 a = reinterpret_cast<const float4*>(src)[0], e = reinterpret_cast<const float4*>(src)[1];
-      f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = e.x; f[5] = e.y; f[6] = e.z; f[7] = e.w;
-    }
+      for (int u = 0; u < UNR; ++u) {
+        const int b = b0 + u;
+        if (b < B) {
+          const Vec* src = reinterpret_cast<const Vec*>(preds + (size_t)b * src_step + src0);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      float vv = f[i];
-      if (use_arcsinh) {
-        if constexpr (sizeof(T) == 4)
-          vv = sinhf(vv);  // fp32 model: the error is not hidden by a bf16 rounding
-        else
-          vv = sinh_fast(vv);
+          for (int v = 0; v < V; ++v) w[u][v] = __ldcs(src + v);
+          sc[u] = __ldg(scale + b);
+          lo[u] = __ldg(loc + b);
+        }
       }
-      f[i] = __fadd_rn(__fmul_rn(vv, sc), lo);
-    }
-    if constexpr (sizeof(T) == 2) {
-      uint4 w;
-      w.x = pack2bf(f[0], f[1]); w.y = pack2bf(f[2], f[3]); w.z = pack2bf(f[4], f[5]); w.w = pack2bf(f[6], f[7]);
-      *reinterpret_cast<uint4*>(dst) = w;
-    } else {
-      reinterpret_cast<float4*>(dst)[0] = make_float4(f[0], f[1], f[2], f[3]);
-      reinterpret_cast<float4*>(dst)[1] = make_float4(f[4], f[5], f[6], f[7]);
+#pragma unroll
+      for (int u = 0; u < UNR; ++u) {
+        const int b = b0 + u;
+        if (b >= B) break;
+        float f[8];
+        if constexpr (sizeof(T) == 2) {
+          const uint32_t uu[4] = {w[u][0].x, w[u][0].y, w[u][0].z, w[u][0].w};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            f[2 * i] = __uint_as_float(uu[i] << 16);
+            f[2 * i + 1] = __uint_as_float(uu[i] & 0xffff0000u);
+          }
+        } else {
+#pragma unroll
+          for (int v = 0; v < V; ++v) {
+            f[4 * v] = __uint_as_float(w[u][v].x); f[4 * v + 1] = __uint_as_float(w[u][v].y);
+            f[4 * v + 2] = __uint_as_float(w[u][v].z); f[4 * v + 3] = __uint_as_float(w[u][v].w);
+          }
+        }
+        if constexpr (sizeof(T) == 2) {
+          // bf16 model: pairs of outputs on the packed-fp32 path
+#pragma unroll
+          for (int i = 0; i < 8; i += 2) {
+            float2 vv = make_float2(f[i], f[i + 1]);
+            if (use_arcsinh) vv = sinh_fast2(vv);
+            vv = __fadd2_rn(__fmul2_rn(vv, f2(sc[u])), f2(lo[u]));
+            f[i] = vv.x;
+            f[i + 1] = vv.y;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float vv = f[i];
+            if (use_arcsinh) vv = sinhf(vv);  // fp32 model: the error is not hidden by a bf16 rounding
+            f[i] = __fadd_rn(__fmul_rn(vv, sc[u]), lo[u]);
+          }
+        }
+        Vec* dst = reinterpret_cast<Vec*>(out + (size_t)b * dst_step + dst0);
+        if constexpr (sizeof(T) == 2) {
+          Vec o;
+          o.x = pack2bf(f[0], f[1]); o.y = pack2bf(f[2], f[3]); o.z = pack2bf(f[4], f[5]); o.w = pack2bf(f[6], f[7]);
+          __stcs(dst, o);
+        } else {
+          __stcs(dst, make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]),
+                                 __float_as_uint(f[3])));
+          __stcs(dst + 1, make_uint4(__float_as_uint(f[4]), __float_as_uint(f[5]), __float_as_uint(f[6]),
+                                     __float_as_uint(f[7])));
+        }
+      }
     }
   }
 }
@@ -639,16 +731,30 @@ int launch_output_transform(int dtype, const void* preds, int ld, const float* l
   const size_t esz = dtype == CC2_BF16 ? 2 : 4;
   if (ps % 8 == 0 && ((uintptr_t)preds & 15u) == 0 && ((uintptr_t)out & 15u) == 0 && (ld * esz) % 16 == 0 &&
       (ps * esz) % 16 == 0 && total / 8 < ((size_t)1 << 31)) {
-    const size_t segs = total / 8;
-    const int vt = 256;
-    const int vb = (int)std::min<size_t>((segs + vt - 1) / vt, (size_t)num_sms() * 16);
+    // one 8-output segment per thread of the per-series layout, whole series per block step
+    const int per_series = Q * N * (ps / 8);
+    const int vt = per_series >= 256 ? 256 : (per_series + 31) / 32 * 32;
+    // a small batch (the forward's) takes one series per block and step, so
+    // that every series has its own block; a streaming batch eight, so that
+    // eight loads per thread are in flight
+    int per_sm = 0;  // resident blocks per SM of the streaming kernel (registers bound it)
     if (dtype == CC2_BF16)
-      CC2_CUDA(launch_k(output_transform_vec_kernel<__nv_bfloat16>, vb, vt, 0, st, 
-          (const __nv_bfloat16*)preds, ld, loc, scale, (__nv_bfloat16*)out, B, N, Q, ps, use_arcsinh));
-    else if (dtype == CC2_F32)
-      CC2_CUDA(launch_k(output_transform_vec_kernel<float>, vb, vt, 0, st, (const float*)preds, ld, loc, scale, (float*)out, B,
-                                                                 N, Q, ps, use_arcsinh));
+      CC2_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, output_transform_seg_kernel<__nv_bfloat16, 8>,
+                                                             vt, 0));
     else
+      CC2_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, output_transform_seg_kernel<float, 8>, vt, 0));
+    const long resident = (long)num_sms() * std::max(per_sm, 1);
+    const bool stream = B > resident;
+    const int vb = (int)std::min<long>(stream ? (B + 7) / 8 : B, resident);
+#define CC2_OT_SEG(TT, U)                                                                                    \
+  CC2_CUDA(launch_k(output_transform_seg_kernel<TT, U>, vb, vt, 0, st, (const TT*)preds, ld, loc, scale, (TT*)out, \
+                    B, N, Q, ps, use_arcsinh))
+    if (dtype == CC2_BF16) {
+      if (stream) CC2_OT_SEG(__nv_bfloat16, 8); else CC2_OT_SEG(__nv_bfloat16, 1);
+    } else if (dtype == CC2_F32) {
+      if (stream) CC2_OT_SEG(float, 8); else CC2_OT_SEG(float, 1);
+    } else
+#undef CC2_OT_SEG
       CC2_REQUIRE(false, "output_transform: unsupported dtype %d", dtype);
     CC2_CHECK_LAUNCH();
     return CC2_OK;

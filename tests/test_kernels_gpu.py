@@ -121,7 +121,7 @@ def test_preprocess_patch_size_1():
 # output transform / RMSNorm
 # ---------------------------------------------------------------------------
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("B,N", [(1, 1), (3, 4), (64, 8)])
+@pytest.mark.parametrize("B,N", [(1, 1), (3, 4), (64, 8), (3001, 4), (2499, 8)])
 def test_output_transform(dtype, B, N):
     g = torch.Generator().manual_seed(B * 10 + N)
     x = (torch.randn(B, N, 21 * 16, generator=g) * 2).to(dtype)
@@ -131,6 +131,30 @@ def test_output_transform(dtype, B, N):
     assert out.shape == (B, 21, N * 16) and out.dtype == dtype
     tol = 1e-5 if dtype == torch.float32 else 2 ** -7
     assert ((out.float() - ref.float()).abs() <= tol * ref.float().abs() + 1e-5 * scale.max()).all()
+
+
+@pytest.mark.parametrize("B", [5, 4000])
+def test_output_transform_bf16_sinh_within_one_ulp(B):
+    # the bf16 path computes sinh on the FMA pipe (range reduction + shared
+    # even/odd polynomial); checked against a float64 sinh over |x| <= 60,
+    # values near 0 included, one bf16 ulp of the exact result (the fp32
+    # arithmetic adds ~3e-7 relative to the final rounding's 2^-9); where
+    # sinh leaves the fp32 range the result is inf with the sign of x, and
+    # NaN stays NaN
+    g = torch.Generator().manual_seed(B)
+    x = torch.randn(B, 4, 21 * 16, generator=g, dtype=torch.float64) * 12
+    x[:, 0, :16] = torch.linspace(-1e-3, 1e-3, 16, dtype=torch.float64)
+    x[0, 1, :8] = torch.tensor([0.0, -0.0, 1e-30, -60.0, 60.0, 88.5, -100.0, float("nan")], dtype=torch.float64)
+    xb = x.to(torch.bfloat16)
+    loc, scale = torch.zeros(B, 1), torch.ones(B, 1)
+    out = K().fused_output_transform(xb.to(DEV), loc.to(DEV), scale.to(DEV), 21, 16).cpu().double()
+    ref = torch.sinh(xb.double()).view(B, 4, 21, 16).permute(0, 2, 1, 3).reshape(B, 21, 64)
+    fin = torch.isfinite(ref) & (ref.abs() < 3.0e38)
+    assert ((out[fin] - ref[fin]).abs() <= 2.0 ** -8 * ref[fin].abs() + 1e-38).all()
+    big = ref.abs() > 3.5e38
+    assert big.sum() >= 1 and fin[0, 0, 16 + 5]  # -100 overflows; 88.5 (1.4e38) does not
+    assert torch.isinf(out[big]).all() and (torch.sign(out[big]) == torch.sign(ref[big])).all()
+    assert torch.isnan(out[0, 0, 16 + 7]) and torch.isnan(ref[0, 0, 16 + 7])
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
