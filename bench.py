@@ -720,6 +720,7 @@ def run_micro(args):
     ctxp = torch.randn(Bp, Lp, generator=g, device=dev)
     predp = rnd(Bp, 4, 336)
     locp, scp = torch.zeros(Bp, device=dev), torch.ones(Bp, device=dev)
+    predc = torch.empty_like(predp)
     wln = rnd(d)
     x4 = rnd(4 * M, d)
     # group attention as configs[2] runs it: 64 groups x 8 series, S = 133, layout prepared once
@@ -758,6 +759,12 @@ def run_micro(args):
             Bp * (4 * Lp + 2 * 48 * Pp + Pp + 4 * Pp + 8)),
         "output transform B=65536 N=4 bf16": (
             lambda: kk.fused_output_transform(predp, locp, scp, 21, 16, True), 0, 2 * 2 * Bp * 4 * 336 + 8 * Bp),
+        # yardsticks for the output transform: the same bytes copied by torch, and the
+        # transform without the sinh (rearrange and unscale only)
+        "output transform B=65536 N=4 bf16 (no sinh)": (
+            lambda: kk.fused_output_transform(predp, locp, scp, 21, 16, False), 0, 2 * 2 * Bp * 4 * 336 + 8 * Bp),
+        "output transform B=65536 N=4 bf16 (torch copy of the bytes)": (
+            lambda: predc.copy_(predp), 0, 2 * 2 * Bp * 4 * 336),
         "rmsnorm M=34048 d=768 bf16": (lambda: kk.rms_layernorm(x, wln), 0, 2 * 2 * M * d),
         "rmsnorm M=136192 d=768 bf16": (lambda: kk.rms_layernorm(x4, wln), 0, 2 * 2 * 4 * M * d),
         "qkv  N=2304 K=768 rowscale": (lambda: kk.linear(x, wqkv, row_ssq=ssq, norm_dim=d), 2 * M * 3 * d * d),

@@ -457,32 +457,31 @@ preprocess_vec_kernel(const float* __restrict__ ctx, const float* __restrict__ c
   }
 }
 
-// sinh for the bf16 output transform, from its definition: |x| < 1/2 by the odd
-// Taylor series x + x^3/3! + x^5/5! + x^7/7! (truncation below 5e-9
-// relative), otherwise (e - 1/e) / 2 with e = 2^(|x| log2 e) from the hardware
-// exp2 (relative error about 6e-8 |x|, below 1e-6 for the |x| <= 15 a
-// forecast in arcsinh space reaches), sign restored.  (An FMA-only version -
-// Cody-Waite reduction and a shared even/odd polynomial, no MUFU op - was
-// slower: the kernel is bound by instruction issue, where a MUFU op is one
-// slot, and it needed ~30 instructions per output against ~18.)
-// Computed for a pair of values with the Blackwell packed-fp32 instructions
-// (one issue slot for both lanes, each lane rounded as a scalar instruction
-// would be).
+// sinh for the bf16 output transform, from its definition, for a pair of
+// values with the Blackwell packed-fp32 instructions (one issue slot for both
+// lanes, each lane rounded as a scalar instruction would be): |x| < 1/2 by
+// the odd Taylor polynomial x + x^3/3! + x^5/5! (truncation below 1.6e-6
+// relative, three orders below the final bf16 rounding's 2^-9), otherwise
+// (e - 1/e) / 2 with e = 2^(|x| log2 e) from the hardware exp2 and
+// reciprocal (relative error about 6e-8 |x|, below 1e-6 for the |x| <= 15 a
+// forecast in arcsinh space reaches), sign restored.  Overflow gives inf,
+// NaN stays NaN.  The kernel is bound by instruction issue (an FMA-only
+// version, Cody-Waite reduction and a shared even/odd polynomial with no MUFU
+// op, needed ~30 instructions per output and was slower).
 __device__ __forceinline__ float2 f2(float v) { return make_float2(v, v); }
 __device__ __forceinline__ float2 sinh_fast2(float2 x) {
   const float2 a = make_float2(fabsf(x.x), fabsf(x.y));
   const float2 a2 = __fmul2_rn(a, a);
-  float2 poly = __ffma2_rn(a2, f2(1.0f / 5040.0f), f2(1.0f / 120.0f));
-  poly = __ffma2_rn(poly, a2, f2(1.0f / 6.0f));
-  poly = __ffma2_rn(poly, __fmul2_rn(a2, a), a);
-  const float2 t = __fmul2_rn(a, f2(1.4426950408889634f));
+  const float2 u = __fmul2_rn(__ffma2_rn(a2, f2(1.0f / 120.0f), f2(1.0f / 6.0f)), a2);
+  const float2 poly = __ffma2_rn(u, a, a);
   float2 e, inv;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(t.x));
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(t.y));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.x) : "f"(fabsf(x.x) * 1.4426950408889634f));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e.y) : "f"(fabsf(x.y) * 1.4426950408889634f));
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv.x) : "f"(e.x));
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(inv.y) : "f"(e.y));
   const float2 big = __fmul2_rn(__ffma2_rn(inv, f2(-1.0f), e), f2(0.5f));
-  return make_float2(copysignf(a.x < 0.5f ? poly.x : big.x, x.x), copysignf(a.y < 0.5f ? poly.y : big.y, x.y));
+  return make_float2(copysignf(fabsf(x.x) < 0.5f ? poly.x : big.x, x.x),
+                     copysignf(fabsf(x.y) < 0.5f ? poly.y : big.y, x.y));
 }
 
 // Output transform: (B, N, ld) forecasts in the model's row layout ->

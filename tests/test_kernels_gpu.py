@@ -133,6 +133,30 @@ def test_output_transform(dtype, B, N):
     assert ((out.float() - ref.float()).abs() <= tol * ref.float().abs() + 1e-5 * scale.max()).all()
 
 
+# forecasts with a row pitch larger than Q * ps (the streaming path then
+# copies each (series, patch) row on its own; the padding is never read)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("B", [5, 3001])
+def test_output_transform_row_pitch(dtype, B):
+    from cutechronos_b200 import _native as nat
+    g = torch.Generator().manual_seed(B + 7)
+    N, ld = 4, 344
+    xp = torch.full((B, N, ld), float("nan")).to(dtype)
+    xp[..., :336] = (torch.randn(B, N, 336, generator=g) * 2).to(dtype)
+    loc, scale = torch.randn(B, 1, generator=g) * 100, torch.rand(B, 1, generator=g) * 10 + 0.1
+    ref = orc.output_transform(xp[..., :336].contiguous(), loc, scale, 21, 16)
+    xd, lf, sf = xp.to(DEV), loc.view(B).to(DEV), scale.view(B).to(DEV)
+    out = torch.empty(B, 21, N * 16, dtype=dtype, device=DEV)
+    code = nat.CC2_BF16 if dtype == torch.bfloat16 else nat.CC2_F32
+    nat.check(nat.load().cc2_output_transform(code, xd.data_ptr(), ld, lf.data_ptr(), sf.data_ptr(), out.data_ptr(),
+                                              B, N, 21, 16, 1, torch.cuda.current_stream().cuda_stream),
+              "cc2_output_transform")
+    out = out.cpu()
+    tol = 1e-5 if dtype == torch.float32 else 2 ** -7
+    assert torch.isfinite(out.float()).all()
+    assert ((out.float() - ref.float()).abs() <= tol * ref.float().abs() + 1e-5 * scale.max()).all()
+
+
 @pytest.mark.parametrize("B", [5, 4000])
 def test_output_transform_bf16_sinh_within_one_ulp(B):
     # the bf16 path computes sinh on the FMA pipe (range reduction + shared
