@@ -404,6 +404,45 @@ def pipeline_rates(model_bf16, dev, steps=3, warmup=1):
     }
 
 
+def memory_bound_streaming(dev, reps=10):
+    """The memory-bound kernels on streaming cases (inputs and outputs well
+    above the 126 MB L2), CUDA events, median of `reps` launches: algorithmic
+    bytes per launch / duration, against the measured HBM copy bandwidth."""
+    from cutechronos_b200 import kernels as kk
+    hbm = measured_peaks()[0]
+    g = torch.Generator(device=dev).manual_seed(5)
+    Bp, Lp, P = 65536, 2048, 128
+    ctx = torch.randn(Bp, Lp, generator=g, device=dev)
+    pred = torch.randn(Bp, 4, 336, generator=g, device=dev).to(torch.bfloat16)
+    loc, sc = torch.zeros(Bp, device=dev), torch.ones(Bp, device=dev)
+    rows = torch.randn(136192, 768, generator=g, device=dev).to(torch.bfloat16)
+    wln = torch.ones(768, device=dev, dtype=torch.bfloat16)
+    cases = {
+        "preprocess_65536x2048": (lambda: kk.fused_preprocess(ctx, 16, 8192, True, dtype=torch.bfloat16),
+                                  Bp * (4 * Lp + 2 * 48 * P + P + 4 * P + 8)),
+        "output_transform_65536x4": (lambda: kk.fused_output_transform(pred, loc, sc, 21, 16, True),
+                                     2 * 2 * Bp * 4 * 336 + 8 * Bp),
+        "rmsnorm_136192x768": (lambda: kk.rms_layernorm(rows, wln), 2 * 2 * 136192 * 768),
+    }
+    out = {}
+    for name, (fn, nbytes) in cases.items():
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for a, b in evs:
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        ms = statistics.median(a.elapsed_time(b) for a, b in evs)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out[name] = {"us": round(ms * 1e3, 1), "gbs": round(gbs, 1), "frac_of_measured_hbm": round(gbs / hbm, 3)}
+    del ctx, pred, rows
+    torch.cuda.empty_cache()
+    return out
+
+
 def e2e_pipelined(step, ctx_host, out_host, flush, steps, dev):
     """End-to-end milliseconds of `steps` forwards with host buffers, the way a
     serving loop runs them: the context of step i+1 goes host -> device and the
@@ -564,10 +603,11 @@ def run_b200(args):
             sharded = {"univariate": cfg4_sharded(model, dev, flush, max(3, args.steps // 2), 2),
                        "grouped": cfg4_sharded(model, dev, flush, max(3, args.steps // 2), 2, grouped=True),
                        "scaling": "strong (4096 series in total, split over the ranks)"}
-        other = pipe_rates = None
+        other = pipe_rates = mem_bound = None
         if rank == 0 and not args.no_configs:
             other = other_configs(model, dev, flush)
             pipe_rates = pipeline_rates(model, dev)
+            mem_bound = memory_bound_streaming(dev)
 
     # ---- roofline of the dominant kernel (tcgen05 GEMM), live from the timed region
     n = cnt.value
@@ -647,6 +687,7 @@ def run_b200(args):
             "other_configs": other,
             "pipeline": pipe_rates,
             "kernels": kernels,
+            "memory_bound_streaming": mem_bound,
             "clocks": clk,
             "cpu_baseline": {"value": cpu_v, "unit": UNIT, "cores": cpu_threads,
                              "kind": ref.kind if cpu_v is not None else None,
