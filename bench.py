@@ -788,6 +788,31 @@ def run_micro(args):
     vq_p = tqm.TurboQuantParams.build(64, 4, mode="mse", seed=12, device=dev)
     qkv_tq = rnd(M, 3 * d, scale=0.5)
 
+    # batch-1 forward (bf16, N = 4) replayed from a CUDA graph, built on first use
+    b1 = {}
+
+    def b1_forward(L):
+        def run():
+            if L not in b1:
+                from cutechronos_b200.model import CuteChronos2Config, CuteChronos2Model
+                from cutechronos_b200.workloads import seeded_init_, series_cfg1
+                if "model" not in b1:
+                    b1["model"] = seeded_init_(CuteChronos2Model(CuteChronos2Config()), seed=0).to(
+                        dev, torch.bfloat16).eval()
+                m, xb = b1["model"], series_cfg1(1, L, 7).to(dev)
+                m(xb, num_output_patches=4)
+                torch.cuda.synchronize()
+                gr, st = torch.cuda.CUDAGraph(), torch.cuda.Stream()
+                st.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(st):
+                    m(xb, num_output_patches=4)
+                    with torch.cuda.graph(gr, stream=st):
+                        m(xb, num_output_patches=4)
+                torch.cuda.synchronize()
+                b1[L] = gr
+            b1[L].replay()
+        return run
+
     cases = {
         "kv_quant prod4/mse4 M=34048": (
             lambda: tqm.kv_quant(qkv_tq, M, 12, kq_p, vq_p, q_col=0, k_col=d, v_col=2 * d), 0, M * 2 * d * 2 * 2),
@@ -823,6 +848,9 @@ def run_micro(args):
             lambda: kk.linear(h, wf, residual=res, residual_lo=res_lo, lo_out=res_lo, ssq_out=so, out=res),
             2 * M * d * dff),
         "gemm 8192^3 plain": (lambda: kk.linear(big, big), 2 * 8192 ** 3),
+        # batch-1 serving latency (graph replay; the "TFLOP/s" column is the forward's FLOPs / latency)
+        "b1 forward ctx512 (graph)": (b1_forward(512), 8.644e9),
+        "b1 forward ctx2048 (graph)": (b1_forward(2048), 31.481e9),
         # batch-1 FFN down (133 token rows): the micro time of one call is host-bound
         # (tensor maps built per call); the device time comes from ncu
         "b1 ffn2 M=133 N=768 K=3072 (128x64 tiles)": (

@@ -78,6 +78,7 @@ int launch_output_transform(int, const void*, int, const float*, const float*, v
                             cudaStream_t);
 int launch_rmsnorm_rows(int, const void*, int, const void*, void*, int, int, int, int, int, int, float,
                         cudaStream_t);
+void set_gemm_weights_const(bool on);
 int launch_gemm_tc(const void*, int, const void*, int, void*, int, int, int, int, const cc2_epilogue*,
                    cudaStream_t);
 extern int g_gemm_variant;
@@ -424,6 +425,12 @@ struct SplitKScope {
   ~SplitKScope() { t_splitk = nullptr; t_splitk_floats = 0; }
 };
 
+// The forward's GEMMs read only the packed model weights as W.
+struct WeightsConstScope {
+  WeightsConstScope() { set_gemm_weights_const(true); }
+  ~WeightsConstScope() { set_gemm_weights_const(false); }
+};
+
 cc2_epilogue epi(int flags) {
   cc2_epilogue e;
   std::memset(&e, 0, sizeof(e));
@@ -612,6 +619,7 @@ int cc2_forward(const cc2_model* m, const float* context, const float* context_m
   Workspace w;
   plan_ws(*m, B, L, N, &w, (char*)workspace);
   SplitKScope splitk_scope(w.splitk, w.splitk_floats);
+  const WeightsConstScope weights_const;
   const int dt = m->dtype;
   const size_t e = m->esz;
   const int d = c.d_model, dff = c.d_ff, ps = c.input_patch_size;

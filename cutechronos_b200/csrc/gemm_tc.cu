@@ -81,15 +81,24 @@ struct Cfg {
 // SM with one 16 KB box per barrier and ~116 GB/s with two, whatever the
 // number of barriers in flight - the per-barrier round trip, not the bytes,
 // bounded the k-loop of few-row GEMMs (0.29 us per k-block).
-template <int BN>
+// AR: rows of an A slot.  With at most 64 token rows (batch-1 serving at
+// context <= 1024) the A box never holds more than 64 rows, so the ring uses
+// 64-row A slots and 4 k-blocks per stage: twice the bytes per barrier round
+// trip in the same shared memory.  The M = 128 MMA still reads 128 rows from
+// the slot; rows past the box read the next slot's bytes and only produce
+// accumulator rows that are never stored.
+template <int BN, int AR = BM, int KPS_ = 2>
 struct Cfg2 {
-  static constexpr int KPS = 2;
-  static constexpr int STAGES = BN == 256 ? 2 : BN == 128 ? 3 : 4;
-  static constexpr int A_BYTES = BM * BK * 2;  // per k-block
+  static constexpr int KPS = KPS_;
+  static constexpr int A_BYTES = AR * BK * 2;  // per k-block
   static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int STAGE_BYTES = KPS * (A_BYTES + B_BYTES);  // [A kb0][A kb1][B kb0][B kb1]
+  static constexpr int STAGE_BYTES = KPS * (A_BYTES + B_BYTES);  // [A kb0][A kb1]..[B kb0][B kb1]..
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;      // 256: 2, 128: 3, 64: 4 (64-row slots: 3)
   static constexpr int TMEM_COLS = 2 * BN;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 8 * 32 * 64 * 2 + 1024 + 256;
+  static_assert(STAGES >= 2 && SMEM <= 232448, "single-SM GEMM ring");
+  // the last A slot of a stage, read as 128 rows, stays inside the stage
+  static_assert((KPS - 1) * A_BYTES + BM * BK * 2 <= STAGE_BYTES, "A slot read past its stage");
 };
 
 struct Epi {
@@ -112,6 +121,8 @@ struct Epi {
   bf16* lo_out;          // LO: low halves of the result
   const bf16* resid_lo;  // LO + RESID: low halves of the residual
   int ld_lo;
+  int wpre;  // W is constant (packed model weights): the single-SM kernel may load
+             // it before the grid dependency wait, under the previous kernel's tail
 };
 
 // ---- PTX wrappers -------------------------------------------------------------
@@ -435,13 +446,13 @@ __device__ __forceinline__ float row_scale(const Epi& ep, const int flags, int r
   return rsqrtf(__fmaf_rn(t, ep.inv_dim, ep.eps));
 }
 
-template <int BN>
+template <int BN, int AR = BM, int KPS = 2>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmR,
                const __grid_constant__ CUtensorMap tmAt, int tail_rows, int M, int N, int K, Epi ep) {
   pdl_launch_dependents();
-  using C = Cfg2<BN>;
+  using C = Cfg2<BN, AR, KPS>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* epi_smem = smem + C::STAGES * C::STAGE_BYTES;  // 4 warps x 2 boxes
@@ -485,7 +496,8 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  pdl_wait();  // the kernel before may still run until here; activations are read from now on
+  // the producer warp waits below, after it has issued the weight loads it may issue early
+  if (warp != 0 || !ep.wpre) pdl_wait();  // activations are read from now on
   const uint32_t tmem_base = *tmem_slot;
 
   const int m_tiles = (M + BM - 1) / BM;
@@ -495,6 +507,24 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
 
   if (warp == 0) {
     if (lane == 0) {
+      // Weights do not depend on the previous kernel: with ep.wpre the first
+      // tile's W boxes for the first `pre` (fresh) stages are issued before the
+      // grid dependency wait, so their HBM latency overlaps the previous
+      // kernel's tail; the stage's full barrier expects the A bytes too, which
+      // are issued after the wait.
+      int pre = 0;
+      if (ep.wpre && (int)blockIdx.x < num_tiles) {
+        const int mt = (int)blockIdx.x / n_tiles, nt = (int)blockIdx.x % n_tiles;
+        const bool tail = mt == m_tiles - 1 && tail_rows < BM;
+        const uint32_t a_bytes = tail ? (uint32_t)tail_rows * BK * 2 : (uint32_t)C::A_BYTES;
+        for (int kb = 0; kb < kblocks && pre < C::STAGES; kb += C::KPS, ++pre) {
+          const uint32_t sb = smem_u32(smem + pre * C::STAGE_BYTES) + C::KPS * C::A_BYTES;
+          const int nk = min(C::KPS, kblocks - kb);
+          mbar_arrive_expect_tx(full_bar(pre), (uint32_t)nk * (a_bytes + (uint32_t)C::B_BYTES));
+          for (int j = 0; j < nk; ++j) tma_load_2d(sb + j * C::B_BYTES, &tmB, full_bar(pre), (kb + j) * BK, nt * BN);
+        }
+        pdl_wait();
+      }
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -514,10 +544,12 @@ gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ 
           // rows past them only produce accumulator rows that are never stored
           const bool tail = mt == m_tiles - 1 && tail_rows < BM;
           const uint32_t a_bytes = tail ? (uint32_t)tail_rows * BK * 2 : (uint32_t)C::A_BYTES;
-          mbar_arrive_expect_tx(full_bar(stage), (uint32_t)nk * (a_bytes + (uint32_t)C::B_BYTES));
+          // the first tile's first `pre` stages: W already in flight, A only
+          const bool early = tile == (int)blockIdx.x && kb / C::KPS < pre;
+          if (!early) mbar_arrive_expect_tx(full_bar(stage), (uint32_t)nk * (a_bytes + (uint32_t)C::B_BYTES));
           for (int j = 0; j < nk; ++j) {
             tma_load_2d(sa + j * C::A_BYTES, tail ? &tmAt : &tmA, full_bar(stage), (kb + j) * BK, mt * BM);
-            tma_load_2d(sb + j * C::B_BYTES, &tmB, full_bar(stage), (kb + j) * BK, nt * BN);
+            if (!early) tma_load_2d(sb + j * C::B_BYTES, &tmB, full_bar(stage), (kb + j) * BK, nt * BN);
           }
           if (++stage == C::STAGES) { stage = 0; phase ^= 1u; }
         }
@@ -1003,10 +1035,13 @@ static int make_map(CUtensorMap* map, const void* ptr, int cols, int rows, int l
   return make_map_box(map, ptr, cols, rows, ld, BK, box_rows);
 }
 
-template <int BN>
+template <int BN, int AR = BM, int KPS = 2>
 static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mr, int M,
                   int N, int K, const Epi& ep, cudaStream_t st, const void* A, int lda) {
-  using C = Cfg2<BN>;
+  using C = Cfg2<BN, AR, KPS>;
+  static_assert(AR == BM || AR == 64, "A slot rows");
+  // 64-row A slots hold only the tail box: one row tile of at most 64 rows
+  CC2_REQUIRE(AR == BM || M <= AR, "gemm: %d rows do not fit the %d-row A slots", M, AR);
   // rows of the last row tile, rounded up to whole 8-row swizzle atoms
   const int rem = M % BM;
   const int tail_rows = rem == 0 ? BM : (rem + 7) / 8 * 8;
@@ -1016,12 +1051,14 @@ static int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMa
   int dev = 0;
   CC2_CUDA(cudaGetDevice(&dev));
   if (dev >= 64 || !((attr_set >> dev) & 1ull)) {
-    CC2_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM));
+    CC2_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, AR, KPS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  C::SMEM));
     if (dev < 64) attr_set |= 1ull << dev;
   }
   const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
-  CC2_CUDA(launch_k(gemm_tc_kernel<BN>, grid, kThreads, C::SMEM, st, ma, mb, mc, mr, mat, tail_rows, M, N, K, ep));
+  CC2_CUDA(launch_k(gemm_tc_kernel<BN, AR, KPS>, grid, kThreads, C::SMEM, st, ma, mb, mc, mr, mat, tail_rows, M, N,
+                    K, ep));
   CC2_CHECK_LAUNCH();
   return CC2_OK;
 }
@@ -1768,6 +1805,11 @@ static int build_epi(const cc2_epilogue* e, int M, int N, tc::Epi* ep) {
   return CC2_OK;
 }
 
+// Set by the forward for its lifetime: every GEMM it issues reads the packed
+// (constant) model weights as W.
+static thread_local bool t_weights_const = false;
+void set_gemm_weights_const(bool on) { t_weights_const = on; }
+
 int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, int ldo, int M, int N, int K,
                    const cc2_epilogue* e, cudaStream_t st) {
   using namespace tc;
@@ -1776,6 +1818,7 @@ int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, in
   CC2_REQUIRE(((uintptr_t)out & 15u) == 0 && ldo % 8 == 0, "gemm(bf16): out alignment");
   Epi ep{};
   CC2_TRY(build_epi(e, M, N, &ep));
+  ep.wpre = t_weights_const && launch_overlap() ? 1 : 0;
   CUtensorMap ma, mb, mc, mr;
   CC2_TRY(make_map(&ma, A, K, M, lda, BM));
   CC2_TRY(make_map_box(&mc, out, N, M, ldo, 64, 32));
@@ -1792,6 +1835,7 @@ int launch_gemm_tc(const void* A, int lda, const void* W, int ldw, void* out, in
   const int pair_ctas = 2 * ((M + 255) / 256) * ((N + 255) / 256);
   if (g_gemm_variant == 0 && N >= 64 && 2 * pair_ctas <= num_sms()) {
     CC2_TRY(make_map(&mb, W, K, N, ldw, 64));
+    if (M <= 64) return launch<64, 64, 4>(ma, mb, mc, mr, M, N, K, ep, st, A, lda);
     return launch<64>(ma, mb, mc, mr, M, N, K, ep, st, A, lda);
   }
   if (g_gemm_variant != 1 && M > BM) {  // 2-SM tiles (256 x 256 per CTA pair)

@@ -279,9 +279,11 @@ def test_gemm_pair_vs_single_sm_tiles(M, N, Kd):
 
 
 # few token rows (batch-1 serving): 128 x 64 single-SM tiles instead of the
-# 256 x 256 pair tiles; the per-element accumulation is the same, so the
-# results must be too, bit for bit
-@pytest.mark.parametrize("M,N,Kd", [(4, 3072, 768), (133, 768, 768), (133, 2304, 768), (133, 768, 3072),
+# 256 x 256 pair tiles (at most 64 rows: 64-row A slots, 4 k-blocks per ring
+# stage); the per-element accumulation is the same, so the results must be
+# too, bit for bit
+@pytest.mark.parametrize("M,N,Kd", [(4, 3072, 768), (37, 768, 3072), (64, 2304, 768), (65, 768, 768),
+                                    (133, 768, 768), (133, 2304, 768), (133, 768, 3072),
                                     (266, 3072, 768), (532, 768, 768), (100, 336, 256)])
 def test_gemm_small_m_tiles_bit_identical(M, N, Kd):
     from cutechronos_b200 import _native as nat
