@@ -814,7 +814,8 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   tc_fence_before();
   cluster_sync();  // barriers of both CTAs initialised, TMEM allocated
   tc_fence_after();
-  pdl_wait();  // the kernel before may still run until here; activations are read from now on
+  // the producer warp waits below, after it has issued the weight loads it may issue early
+  if (warp != 0 || !ep.wpre) pdl_wait();  // activations are read from now on
   const uint32_t tmem_base = *tmem_slot;
 
   const int m_tiles = (M + 255) / 256;
@@ -827,6 +828,19 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
   if (warp == 0) {
     if (lane == 0) {
       const uint32_t lead_full0 = map_to_rank(full_bar(0), 0);
+      // constant weights (ep.wpre): this CTA's W half of the first tile's first
+      // `pre` (fresh) stages is issued before the grid dependency wait; the
+      // leader's full barrier expects both CTAs' A and W bytes as usual
+      int pre = 0;
+      if (ep.wpre && pair_id < num_tiles) {
+        const int nt = pair_id % n_tiles;
+        for (int kb = 0; kb < kblocks && pre < STAGES; ++kb, ++pre) {
+          const uint32_t fb = lead_full0 + 8u * pre;
+          if (leader) arrive_expect_tx_cluster(fb, 2 * STAGE_BYTES);
+          tma_load_2d_pair(smem_u32(smem + pre * STAGE_BYTES) + A_BYTES, &tmB, fb, kb * BK, nt * BN + (int)rank * 128);
+        }
+        pdl_wait();
+      }
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -838,9 +852,10 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant_
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) { ok = false; break; }
           const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
           const uint32_t fb = lead_full0 + 8u * stage;
-          if (leader) arrive_expect_tx_cluster(fb, 2 * STAGE_BYTES);
+          const bool early = tile == pair_id && kb < pre;  // W already in flight: A only
+          if (leader && !early) arrive_expect_tx_cluster(fb, 2 * STAGE_BYTES);
           tma_load_2d_pair(sa, &tmA, fb, kb * BK, mt * 256 + (int)rank * 128);
-          tma_load_2d_pair(sa + A_BYTES, &tmB, fb, kb * BK, nt * BN + (int)rank * 128);
+          if (!early) tma_load_2d_pair(sa + A_BYTES, &tmB, fb, kb * BK, nt * BN + (int)rank * 128);
           if (++stage == STAGES) { stage = 0; phase ^= 1u; }
         }
       }
