@@ -62,6 +62,7 @@ __device__ __forceinline__ void trace(unsigned long long* tr, uint32_t unit, int
 
 struct Args {
   int S, heads, items, NK, T, q1rows;
+  int split;  // 1: an item is one query tile of a (series, head) set (few sets: twice the CTAs)
   int qcol, kcol, vcol, ldo;
   int stages;
   uint32_t stage_bytes, q1_off, k_off, v_off, p_off, qk_bytes, v_bytes;
@@ -133,15 +134,20 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__
     for (int li = 0; li < my_items && !abort_flag; ++li) {
       const int st = li % a.stages, n = li / a.stages;
       const int item = (int)blockIdx.x + li * (int)gridDim.x;
-      const int b = item / a.heads, h = item % a.heads;
+      const int set_item = a.split ? item / a.T : item, tile = a.split ? item % a.T : -1;
+      const int b = set_item / a.heads, h = set_item % a.heads;
       const uint32_t dst = sbase + (uint32_t)st * a.stage_bytes;
       const int row0 = b * a.S;
       if (n > 0 && !mbar_wait(smem_u32(&empty_qk[st]), (uint32_t)(n - 1) & 1u, &abort_flag, err)) break;
       const uint32_t bqk = smem_u32(&full_qk[st]);
       if (lane == 0) {
-        mbar_expect_tx(bqk, a.qk_bytes);
-        tma_load(dst, &tmQ0, bqk, a.qcol + h * 64, row0);
-        if (a.T == 2) tma_load(dst + a.q1_off, &tmQ1, bqk, a.qcol + h * 64, row0 + 128);
+        // a split item loads only its own query box (tile 1 reads the Q0 slot's
+        // last 64 rows as the A operand's first rows: stale, and their score
+        // and output rows are never used)
+        mbar_expect_tx(bqk, tile < 0 ? a.qk_bytes
+                                     : a.v_bytes + (tile == 0 ? 128u * 128u : (uint32_t)a.q1rows * 128u));
+        if (tile <= 0) tma_load(dst, &tmQ0, bqk, a.qcol + h * 64, row0);
+        if (a.T == 2 && tile != 0) tma_load(dst + a.q1_off, &tmQ1, bqk, a.qcol + h * 64, row0 + 128);
         tma_load(dst + a.k_off, &tmKV, bqk, a.kcol + h * 64, row0);
         trace(tr, (uint32_t)(li * a.T), 0);
       }
@@ -187,8 +193,10 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__
         trace(tr, u, 1);
         const uint32_t stage = sbase + (uint32_t)st * a.stage_bytes;
         const uint64_t dk = sw128_desc(stage + a.k_off), dv = sw128_desc(stage + a.v_off);
+        const int item = (int)blockIdx.x + li * (int)gridDim.x;
+        const int t_begin = a.split ? item % a.T : 0, t_end = a.split ? t_begin + 1 : a.T;
         bool ok = true;
-        for (int t = 0; t < a.T; ++t, ++u) {
+        for (int t = t_begin; t < t_end; ++t, ++u) {
           // tile 1: the A operand starts 64 rows before the Q1 box, so the
           // set's last rows land on TMEM lanes 64.. (warps 2 and 6, whose
           // SM sub-partition runs neither the producer nor the MMA warp)
@@ -196,11 +204,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) mma_bf16(tmem, dq + 2u * ks, dk + 2u * ks, id_s, ks > 0);
           mma_commit(smem_u32(&s_full));
-          if (t == a.T - 1) mma_commit(smem_u32(&empty_qk[st]));
+          if (t == t_end - 1) mma_commit(smem_u32(&empty_qk[st]));
           trace(tr, u, 2);
           any = true;
           if (!mbar_wait(smem_u32(&p_full), u & 1u, &abort_flag, err) ||
-              (t == 0 && !mbar_wait(smem_u32(&full_v[st]), (uint32_t)n & 1u, &abort_flag, err))) {
+              (t == t_begin && !mbar_wait(smem_u32(&full_v[st]), (uint32_t)n & 1u, &abort_flag, err))) {
             ok = false;
             break;
           }
@@ -213,7 +221,7 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__
                      ks > 0);
           mma_commit(smem_u32(&o_full));
           trace(tr, u, 4);
-          if (t == a.T - 1) mma_commit(smem_u32(&empty_v[st]));
+          if (t == t_end - 1) mma_commit(smem_u32(&empty_v[st]));
         }
         if (!ok) break;
       }
@@ -248,9 +256,11 @@ attn_tc_kernel(const __grid_constant__ CUtensorMap tmQ0, const __grid_constant__
     for (int li = 0; li < my_items && ok; ++li) {
       ok = mbar_wait(smem_u32(&kb_full[li % 3]), (uint32_t)(li / 3) & 1u, &abort_flag, err);  // key bias
       const int item = (int)blockIdx.x + li * (int)gridDim.x;
-      const int b = item / a.heads, h = item % a.heads;
+      const int set_item = a.split ? item / a.T : item;
+      const int t_begin = a.split ? item % a.T : 0, t_end = a.split ? t_begin + 1 : a.T;
+      const int b = set_item / a.heads, h = set_item % a.heads;
       const float* kb = kbias[li % 3] + c0;
-      for (int t = 0; t < a.T; ++t, ++u) {
+      for (int t = t_begin; t < t_end; ++t, ++u) {
         // lane r holds query row t * 128 + r - lane0 (tile 1 starts at lane 64)
         const int lane0 = t == 0 ? 0 : 64;
         const int rows_t = t == 0 ? min(a.S, 128) : a.S - 128;
@@ -447,6 +457,10 @@ int launch_attn_tc(const void* qkv, int ld, int qcol, int kcol, int vcol, void* 
     CC2_CUDA(cudaFuncSetAttribute(attn_tc_kernel<144>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)half));
     if (dev < 64) attr_done |= 1ull << dev;
   }
+  // few sets (batch-1 serving): each query tile of a two-tile set is an item
+  // of its own, so the two tile chains run on two CTAs at once
+  a.split = a.T == 2 && 2 * a.items <= 2 * num_sms() ? 1 : 0;
+  if (a.split) a.items *= a.T;
   const int grid = std::min(a.items, 2 * num_sms());
   if (a.NK <= 64)
     CC2_CUDA(launch_k(attn_tc_kernel<64>, grid, kThreads, smem, st, mq0, mq1, mkv, (bf16*)out, tok, a, err));

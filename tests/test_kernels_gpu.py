@@ -317,6 +317,25 @@ def test_gemm_small_m_tiles_bit_identical(M, N, Kd):
         assert torch.equal(a, b), i
 
 
+# few two-tile sets (batch-1 serving): each query tile of a set runs as an
+# item of its own on its own CTA; the per-tile arithmetic is the same as in a
+# large batch (one CTA running both tiles), so the rows must match bit for bit
+@pytest.mark.parametrize("S", [129, 133, 144])
+@pytest.mark.parametrize("n_few", [1, 5])
+def test_time_attention_split_tiles_bit_identical(S, n_few):
+    g = torch.Generator().manual_seed(S + n_few)
+    B, H = 300, 12
+    qkv = (torch.randn(B * S, 3 * H * 64, generator=g) * 0.5).to(torch.bfloat16).to(DEV)
+    tok = torch.ones(B * S, dtype=torch.uint8)
+    tok[: S // 3] = 0  # a left-padded first series
+    tok = tok.to(DEV)
+    full = K().attention_rows(qkv, tok, B, S, H, False)
+    few = K().attention_rows(qkv[: n_few * S].contiguous(), tok[: n_few * S].contiguous(), n_few, S, H, False)
+    torch.cuda.synchronize()
+    assert torch.isfinite(few[S // 3:].float()).all()
+    assert torch.equal(few.cpu(), full[: n_few * S].cpu())
+
+
 @pytest.mark.parametrize("M,S", [(133 * 3, 133), (37, 37), (521 * 2, 521)])
 def test_qkv_epilogue_rope(M, S):
     # RoPE applied in the QKV GEMM epilogue (Q and K columns, position = row % S)
