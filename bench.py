@@ -882,11 +882,40 @@ def run_micro(args):
     }
     out = {}
     hbm, *_ = measured_peaks()
+    trace_buf = torch.zeros(32 * 8, dtype=torch.int64, device=dev) if args.gemm_trace else None
     for name, spec in cases.items():
         fn, flops = spec[0], spec[1]
         nbytes = spec[2] if len(spec) > 2 else 0
         if args.only and args.only not in name:
             continue
+        if trace_buf is not None:
+            # per-tile event stamps of the 2-SM GEMM's CTA pair 0 (cc2_set_gemm_trace), one
+            # traced launch after a warm-up: tile period (MMA warp's accumulator-free stamps),
+            # epilogue span (accumulator full -> epilogue done, warp 2), MMA waits on loads
+            fn()
+            torch.cuda.synchronize()
+            trace_buf.zero_()
+            nat.check(lib.cc2_set_gemm_trace(trace_buf.data_ptr()), "cc2_set_gemm_trace")
+            fn()
+            torch.cuda.synchronize()
+            nat.check(lib.cc2_set_gemm_trace(None), "cc2_set_gemm_trace")
+            t = trace_buf.view(32, 8).cpu().double()
+            n = int((t[:, 0] > 0).sum().item())
+            if n >= 3:
+                period = (t[2:n, 0] - t[1:n - 1, 0]) / 1e3
+                epi = (t[1:n, 4] - t[1:n, 3]) / 1e3
+                issue_full = (t[1:n, 3] - t[1:n, 2]) / 1e3  # last k-block issued -> accumulator full
+                loadw = t[1:n, 6] / 1e3
+                tr = {"tiles": n, "period_us": round(period.median().item(), 2),
+                      "epilogue_us": round(epi.median().item(), 2),
+                      "issue_to_full_us": round(issue_full.median().item(), 2),
+                      "mma_load_wait_us": round(loadw.median().item(), 2),
+                      # pair 0: first accumulator-free stamp -> last epilogue done, and the
+                      # first tile's wait for its first loaded stage
+                      "span_us": round((t[n - 1, 4] - t[0, 0]).item() / 1e3, 2),
+                      "first_load_us": round((t[0, 1] - t[0, 0]).item() / 1e3, 2)}
+                out[name + " [trace]"] = tr
+                log(f"{name:36s} trace: {tr}")
         # warm up for at least 30 ms of GPU time so that the SM clock has ramped up
         t_end = time.perf_counter() + 0.03
         n_warm = 0
@@ -925,6 +954,8 @@ def main():
     ap.add_argument("--no-configs", action="store_true", help="skip the configs[0,2,3,4] measurements")
     ap.add_argument("--micro", action="store_true", help="per-kernel micro-benchmark instead of the step")
     ap.add_argument("--only", default="", help="with --micro: run only cases whose name contains this")
+    ap.add_argument("--gemm-trace", action="store_true",
+                    help="with --micro: per-tile event trace of the 2-SM GEMM's CTA pair 0 for each case")
     ap.add_argument("--gemm-variant", type=int, default=0, help="0: 2-SM GEMM tiles, 1: 1-SM tiles only, 3: mainloop only (no output)")
     args = ap.parse_args()
     if args.warmup < 3:
